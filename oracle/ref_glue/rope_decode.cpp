@@ -1,0 +1,15 @@
+// Glue for test/kernel/test_fused_reshape_rope_kvcache_decode.cu (reference).
+#include "test/kernel/test_fused_reshape_rope_kvcache_decode.cu"
+#include "common.h"
+
+extern "C" void ref_rope_kvcache_decode(const float *input, const unsigned char *is_done, const unsigned int *kv_lens,
+                                        unsigned int B, unsigned int Hq, unsigned int Hkv, unsigned int hd,
+                                        unsigned int S, float *q, float *k, float *v)
+{
+    std::vector<float> eq, ek, ev;
+    compute_expected_decode(ref_glue_vec(is_done, B), ref_glue_vec(kv_lens, B), S, Hq, Hkv, hd,
+                            ref_glue_vec(input, size_t(B) * (Hq + 2 * Hkv) * hd), eq, ek, ev);
+    ref_glue_out(eq, q);
+    ref_glue_out(ek, k);
+    ref_glue_out(ev, v);
+}
