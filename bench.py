@@ -1,0 +1,375 @@
+"""Benchmark of the fused Llama-2 layer-kernel chain on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+A step is one pass of the chain (update lens -> embedding -> RMSNorm -> RoPE +
+KV append -> fused scores -> SwiGLU) over one batch of synthetic input
+(llama2_b200.workloads). The default workload is 7b-b1: Llama-2-7B dims,
+batch 1 decode, fp32, KV cache 4096 — the first 7B-dims configuration of the
+reference path's benchmark set. Under torchrun each rank runs its own batch
+on its own GPU (sharding by sequence batch; no collective on the data path),
+so scaling is weak; time is the max over ranks of the summed per-step device
+time (CUDA events), and value = tokens of all ranks / that time.
+
+Between timed steps the L2 cache is flushed (a 2 x L2-sized buffer is
+written) and the sequence lengths are restored, outside the timed windows.
+
+--impl reference times the reference's own CPU implementation of the path
+(its CPU test helpers compiled from its sources, oracle/_ref; the C
+restatement oracle/liboracle.so where those are absent) on this box's host
+cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from llama2_b200.workloads import WORKLOADS, algorithmic_bytes, host_cache_ok, host_inputs  # noqa: E402
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", default="7b-b1", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling (NVML) during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index, period=0.002):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.period = period
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def _sample(self):
+        n = self.nvml
+        try:
+            self.samples.append(n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM))
+            r = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for bit, name in self.REASONS.items():
+                if r & bit and name != "gpu_idle":
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def start(self):
+        if self.nvml:
+            self._sample()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread:
+            self._stop.set()
+            self._thread.join()
+            self._sample()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baselines (oracle / reference helpers) — only the CPU legs touch oracle/
+# ---------------------------------------------------------------------------
+def cpu_chain_rate(w, inputs, seconds, impl):
+    """tokens/s of the CPU chain on a bounded sample: whole steps until `seconds`."""
+    from oracle import cpu_chain
+    runner = cpu_chain.CpuChain(w, inputs, impl=impl)
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        runner.step()
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": steps * w.tokens / el, "unit": "tokens/s", "cores": runner.threads, "kind": runner.kind,
+            "sample": f"{steps} full chain step(s) of {w.name} (batch {w.batch}) in {el:.1f} s on "
+                      f"{runner.threads} thread(s)"}
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from llama2_b200.chain import Chain
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    w = WORKLOADS[args.workload]
+    inputs = host_inputs(w, seed=0, rank=rank, kv_cache=host_cache_ok(w))
+    chain = Chain(w, inputs, device=dev)
+
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    flush = torch.empty(max(2 * l2, 256 << 20) // 4, dtype=torch.float32, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # The dominant kernel (fused scores) is bracketed inside the graph by
+    # external event-record nodes so its duration is measured in every step.
+    kev = (torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+    capture_with_kernel_events(chain, kev)
+
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+
+    def one_step(i=None, timed=False):
+        chain.reset_lengths()
+        flush.zero_()
+        if timed:
+            ev[i][0].record(stream)
+        chain.graph.replay()
+        if timed:
+            ev[i][1].record(stream)
+
+    for _ in range(max(args.warmup, 3)):
+        one_step()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local_rank)
+    kernel_ms = []
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    for i in range(args.steps):
+        one_step(i, timed=True)
+        kev[1].synchronize()
+        kernel_ms.append(kev[0].elapsed_time(kev[1]))
+    torch.cuda.synchronize()
+    clocks.stop()
+    barrier()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = sum(step_ms)
+
+    # End to end through the public API: H2D of the step's inputs from pinned
+    # memory, the chain, D2H of its results, every step.
+    chain.host_buffers(inputs)
+    h2d, d2h = chain.e2e_bytes()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        chain.step_e2e()
+    torch.cuda.synchronize()
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        ev2[i][0].record(stream)
+        chain.step_e2e()
+        ev2[i][1].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in ev2)
+
+    kv_after = inputs["kv_lens"].astype(np.int64) + inputs["q_lens"].astype(np.int64)
+    chain_bytes = algorithmic_bytes(w, kv_after)
+    score_bytes = scores_bytes(w, kv_after)
+
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = t.tolist()
+
+    result = None
+    if rank == 0:
+        tokens = w.tokens * world * args.steps
+        peak, peak_kind = peaks()
+        kmean = float(np.mean(kernel_ms)) if kernel_ms else None
+        achieved = score_bytes / (kmean * 1e-3) / 1e9 if kmean else None
+        result = {
+            "metric": "layer-kernel tokens/s at Llama-2-7B dims",
+            "value": tokens / (total_ms * 1e-3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": {"f32": "fp32", "bf16": "bf16", "f16": "fp16"}[w.dtype],
+            "data": "synthetic (seeded; N(0,1) activations and KV cache, N(0,0.02) embeddings)",
+            "config": {"workload": w.name, "dim": w.dim, "heads": w.heads, "head_dim": w.head_dim,
+                       "hidden": w.hidden, "kv_cache_len": w.kv_cache_len, "batch_per_gpu": w.batch,
+                       "prefill_len": w.prefill_len, "parallelism": f"sequence-batch shards x{world}",
+                       "l2": "flushed between timed steps"},
+            "chain_hbm": {"algorithmic_bytes_per_step": chain_bytes,
+                          "achieved_gbs": chain_bytes / (total_ms / args.steps * 1e-3) / 1e9,
+                          "frac_of_peak": chain_bytes / (total_ms / args.steps * 1e-3) / 1e9 / peak},
+            "roofline": {"kernel": "fused decode scores" if w.decode else "fused prefill scores",
+                         "bound": "hbm", "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": achieved / peak if achieved else None,
+                         "algorithmic_bytes_per_launch": score_bytes, "mean_launch_ms": kmean,
+                         "traffic": profiled_traffic(w.name)},
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": chain.kernels_per_step() * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if not args.no_cpu_baseline and world == 1:
+            result["cpu_baseline"] = cpu_chain_rate(w, inputs, args.cpu_sample_seconds, impl="port")
+    return result
+
+
+def capture_with_kernel_events(chain, kev):
+    """Capture chain.step() as a graph with event-record nodes around the scores kernel."""
+    import torch
+    from llama2_b200 import ops
+
+    orig_dec, orig_pre = ops.decode_attention_scores, ops.prefill_attention_scores
+
+    def wrap(fn):
+        def inner(*a, **k):
+            kev[0].record()
+            fn(*a, **k)
+            kev[1].record()
+        return inner
+
+    ops.decode_attention_scores, ops.prefill_attention_scores = wrap(orig_dec), wrap(orig_pre)
+    try:
+        chain.capture()
+    finally:
+        ops.decode_attention_scores, ops.prefill_attention_scores = orig_dec, orig_pre
+
+
+def scores_bytes(w, kv_after):
+    """Algorithmic bytes of one fused-scores launch: q, K rows 0..pos, score rows."""
+    s = 2 if w.dtype in ("bf16", "f16") else 4
+    kv = np.asarray(kv_after, np.int64)
+    max_kv = int(kv.max())
+    if w.decode:
+        return int(w.batch * w.dim * s + kv.sum() * w.dim * s + w.batch * w.heads * max_kv * s)
+    q = w.prefill_len
+    return int(w.tokens * w.dim * s + kv.sum() * w.dim * s + w.batch * w.heads * q * max_kv * s)
+
+
+def profiled_traffic(workload):
+    """DRAM bytes per launch of the scores kernel from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# Reference arm: the reference's CPU implementation on the host cores
+# ---------------------------------------------------------------------------
+def run_reference(args):
+    from oracle import cpu_chain
+
+    w = WORKLOADS[args.workload]
+    inputs = host_inputs(w, seed=0, kv_cache=host_cache_ok(w))
+    impl = "ref" if cpu_chain.ref_available() else "port"
+    runner = cpu_chain.CpuChain(w, inputs, impl=impl, threads=os.cpu_count())
+    sample = runner.sample_batch()
+    for _ in range(max(args.warmup, 1)):
+        runner.step(sample)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        runner.step(sample)
+    el = time.perf_counter() - t0
+    tokens = len(sample) * (w.prefill_len or 1) * args.steps
+    value = tokens / el
+    return {
+        "impl": "reference",
+        "metric": "layer-kernel tokens/s at Llama-2-7B dims",
+        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": {"f32": "fp32", "bf16": "bf16", "f16": "fp16"}[w.dtype],
+        "data": "synthetic (seeded)",
+        "config": {"workload": w.name, "batch_per_step_sample": len(sample)},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": runner.threads, "kind": runner.kind,
+                         "sample": f"{len(sample)} of {w.batch} sequence(s) per step, {args.steps} steps"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)))
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        res = run_ours(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(res))
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,272 @@
+/*
+ * llama2_b200.h — C ABI of the B200 (sm_100a) Llama-2 layer kernels.
+ *
+ * One entry point per operator of the reference's operator API
+ * (pentatracy5/llama2, include/kernel/*.h), plus the fused score kernels and
+ * the fused decode step. Every entry point:
+ *   - takes plain device pointers and 64-bit sizes (no C++ or torch types);
+ *   - enqueues its work on `stream` and returns without synchronizing;
+ *   - never allocates device memory (the caller owns every buffer);
+ *   - returns L2K_OK (0) or a nonzero l2k_status; on error nothing was
+ *     launched and l2k_last_error_message() describes the problem (the
+ *     message is per host thread).
+ * Shapes follow the reference: row-major, caches laid out as
+ * (batch, kv_head, kv_cache_len, head_dim).
+ *
+ * Element types (`dtype`): L2K_F32, L2K_F16, L2K_BF16. Arithmetic is fp32 in
+ * every kernel; 16-bit types are rounded to nearest-even on store.
+ */
+#ifndef LLAMA2_B200_H
+#define LLAMA2_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *l2k_stream_t; /* same handle as cudaStream_t; NULL = legacy default stream */
+
+enum l2k_dtype
+{
+    L2K_F32 = 0,
+    L2K_F16 = 1,
+    L2K_BF16 = 2
+};
+
+enum l2k_status
+{
+    L2K_OK = 0,
+    L2K_ERR_INVALID_ARGUMENT = 1,  /* null pointer, negative size, inconsistent shapes */
+    L2K_ERR_UNSUPPORTED_DTYPE = 2, /* dtype not handled by this operator */
+    L2K_ERR_UNSUPPORTED_SHAPE = 3, /* valid but outside what this operator implements */
+    L2K_ERR_CUDA = 4               /* a CUDA runtime call or launch failed */
+};
+
+/* RoPE pairings: (2i, 2i+1) as in the reference's generic kernels, or
+ * (i, i + head_dim/2) as in its "_llama2" kernels. */
+enum l2k_rope_pairing
+{
+    L2K_ROPE_INTERLEAVED = 0,
+    L2K_ROPE_HALF = 1
+};
+
+const char *l2k_status_string(int status);
+const char *l2k_last_error_message(void);
+int l2k_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * Token-embedding gather: output[t, :] = embed_table[input_ids[t], :].
+ * Replaces launch_embedding (include/kernel/embedding.h:6-9,
+ * src/kernel/embedding.cu:35-49). Ids >= vocab_size produce a zero row
+ * (the reference reads out of bounds there).
+ * ------------------------------------------------------------------------ */
+int l2k_embedding(const uint32_t *input_ids, int64_t num_tokens, const void *embed_table, int64_t vocab_size,
+                  int64_t embed_dim, void *output, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused add-residual + RMSNorm, in place:
+ *   if add_residual: x = x + residual (written back to x)
+ *   residual = x * weights * 1/sqrt(mean(x^2) + 1e-5)
+ * Replaces launch_fused_add_residual_rmsnorm<T, add_residual>
+ * (include/kernel/fused_add_residual_rmsnorm.h:16-19,
+ * src/kernel/fused_add_residual_rmsnorm.cu:104-126).
+ * ------------------------------------------------------------------------ */
+int l2k_fused_add_residual_rmsnorm(const void *weights, void *x, void *residual, int64_t num_tokens,
+                                   int64_t embed_dim, int add_residual, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * RoPE cos/sin table. The RoPE entry points take an optional device table of
+ * num_positions x (head_dim/2) float pairs {cos, sin} for the angle
+ * pos / 10000^(2i/head_dim), which is the reference's angle whenever the
+ * sequence length is <= 4096 (its length-scaling factor is then exactly 1).
+ * l2k_rope_table_fill computes the table on the host with the C library's
+ * powf/cosf/sinf, the functions the reference's CPU oracle uses, so the
+ * kernels' rotations agree with that oracle bit for bit. Positions beyond
+ * the table, and sequences longer than 4096, fall back to on-device
+ * evaluation of the reference formula (include/kernel/rope.cuh:14-17).
+ * ------------------------------------------------------------------------ */
+int64_t l2k_rope_table_floats(int64_t head_dim, int64_t num_positions);
+int l2k_rope_table_fill(float *host_table, int64_t head_dim, int64_t num_positions);
+
+/* ------------------------------------------------------------------------
+ * Decode RoPE + KV-cache append. input: (batch, (Hq + 2 Hkv) * head_dim);
+ * q: (batch, Hq, 1, head_dim); k, v: (batch, Hkv, kv_cache_len, head_dim).
+ * For each sequence with is_done == 0 and pos = kv_lens[b] - 1: rotate the
+ * q and k heads at pos, write q and k row pos, copy v row pos.
+ * l2k_fused_reshape_rope_kvcache_decode replaces
+ * launch_fused_reshape_rope_kvcache_decode (interleaved pairs;
+ * include/kernel/fused_reshape_rope_kvcache_decode.h:6-12,
+ * src/kernel/fused_reshape_rope_kvcache_decode.cu:86-125);
+ * l2k_fused_reshape_rope_kvcache_llama2_decode replaces
+ * launch_fused_reshape_rope_kvcache_llama2_decode (half pairs;
+ * include/kernel/fused_reshape_rope_kvcache_llama2_decode.h:6-12,
+ * src/kernel/fused_reshape_rope_kvcache_llama2_decode.cu:76-114), which
+ * the reference restricts to head_dim 128; here any even head_dim works.
+ * rope_table may be NULL (on-device evaluation).
+ * ------------------------------------------------------------------------ */
+int l2k_fused_reshape_rope_kvcache_decode(const void *input, const uint8_t *is_done, const uint32_t *kv_lens,
+                                          void *q, void *k, void *v, int64_t batch, int64_t q_head_num,
+                                          int64_t kv_head_num, int64_t head_dim, int64_t kv_cache_len,
+                                          const float *rope_table, int64_t rope_table_positions, int dtype,
+                                          l2k_stream_t stream);
+int l2k_fused_reshape_rope_kvcache_llama2_decode(const void *input, const uint8_t *is_done,
+                                                 const uint32_t *kv_lens, void *q, void *k, void *v, int64_t batch,
+                                                 int64_t q_head_num, int64_t kv_head_num, int64_t head_dim,
+                                                 int64_t kv_cache_len, const float *rope_table,
+                                                 int64_t rope_table_positions, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Prefill RoPE + pad/transpose + KV-cache append. input: (num_tokens,
+ * (Hq + 2 Hkv) * head_dim), unpadded; unpad_to_pad_idx from
+ * l2k_build_padding_index_maps; q: (batch, Hq, q_cache_len, head_dim).
+ * Token t of sequence b is at pos = kv_lens[b] - q_lens[b] + t.
+ * Replaces launch_fused_pad_reshape_transpose_rope_kvcache
+ * (include/kernel/fused_pad_reshape_transpose_rope_kvcache.h:6-13,
+ * src/kernel/fused_pad_reshape_transpose_rope_kvcache.cu:85-126) and the
+ * "_llama2" variant (…_llama2.h:6-13, …_llama2.cu:77-117).
+ * ------------------------------------------------------------------------ */
+int l2k_fused_pad_reshape_transpose_rope_kvcache(const void *input, const uint32_t *q_lens,
+                                                 const uint32_t *kv_lens, const uint32_t *unpad_to_pad_idx,
+                                                 void *q, void *k, void *v, int64_t num_tokens, int64_t batch,
+                                                 int64_t q_head_num, int64_t kv_head_num, int64_t head_dim,
+                                                 int64_t q_cache_len, int64_t kv_cache_len,
+                                                 const float *rope_table, int64_t rope_table_positions, int dtype,
+                                                 l2k_stream_t stream);
+int l2k_fused_pad_reshape_transpose_rope_kvcache_llama2(const void *input, const uint32_t *q_lens,
+                                                        const uint32_t *kv_lens, const uint32_t *unpad_to_pad_idx,
+                                                        void *q, void *k, void *v, int64_t num_tokens,
+                                                        int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                                        int64_t head_dim, int64_t q_cache_len,
+                                                        int64_t kv_cache_len, const float *rope_table,
+                                                        int64_t rope_table_positions, int dtype,
+                                                        l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Length update: kv_lens[b] += q_lens[b]; *max_q_len = max(q_lens);
+ * *max_kv_len = max(kv_lens) (device pointers; no host synchronization).
+ * Replaces launch_update_q_kv_lens (include/kernel/update_q_kv_lens.h:6-9,
+ * src/kernel/update_q_kv_lens.cu:43-61), without its batch <= 512 limit.
+ * ------------------------------------------------------------------------ */
+int l2k_update_q_kv_lens(const uint32_t *q_lens, uint32_t *kv_lens, int64_t batch, uint32_t *max_q_len,
+                         uint32_t *max_kv_len, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Causal mask, u8 (batch, q_cache_len, kv_cache_len), written over
+ * [0, max_q_len) x [0, max_kv_len) with the reference's expression
+ *   q < q_len && k < kv_len && q >= k - (kv_len - q_len)
+ * evaluated in 32-bit unsigned arithmetic, bit-identical to the reference
+ * (src/kernel/build_causal_mask.cu:35), including its wrap-around for
+ * k < kv_len - q_len. Replaces launch_build_causal_mask
+ * (include/kernel/build_causal_mask.h:6-11, src/kernel/build_causal_mask.cu:45-67).
+ * ------------------------------------------------------------------------ */
+int l2k_build_causal_mask(uint32_t max_q_len, uint32_t max_kv_len, const uint32_t *q_lens,
+                          const uint32_t *kv_lens, uint8_t *mask, int64_t batch, int64_t q_cache_len,
+                          int64_t kv_cache_len, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Unpad -> pad index map: unpad_to_pad_idx[off_b + i] = b * q_cache_len + i,
+ * seq_offsets[b] = sum(seq_lens[:b]). Replaces launch_build_padding_index_maps
+ * (include/kernel/build_padding_index_maps.h:6-10,
+ * src/kernel/build_padding_index_maps.cu:30-43). batch <= 16384.
+ * ------------------------------------------------------------------------ */
+int l2k_build_padding_index_maps(int64_t num_tokens, const uint32_t *seq_lens, int64_t batch, int64_t q_cache_len,
+                                 uint32_t *unpad_to_pad_idx, uint32_t *seq_offsets, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Batched-GEMM pointer arrays. For slot idx = b * Hq + qh (kv slot
+ * b * Hkv + qh / (Hq / Hkv) for entries 2 and 3):
+ *   arrays[a][idx] = bases[a] + slot * slice_elems[a] * elem_size
+ * with a = 0..7 the reference's q, q_decode, k, v, qk, qk_decode, qkv,
+ * qkv_decode. bases, slice_elems and arrays are host arrays of 8; each
+ * arrays[a] is a device array of batch * Hq pointers.
+ * Replaces launch_build_q_k_v_qk_qkv_array
+ * (include/kernel/build_q_k_v_qk_qkv_array.h:6-22,
+ * src/kernel/build_q_k_v_qk_qkv_array.cu:66-137).
+ * ------------------------------------------------------------------------ */
+int l2k_build_q_k_v_qk_qkv_array(void *const bases[8], const int64_t slice_elems[8], int64_t elem_size,
+                                 int64_t batch, int64_t q_head_num, int64_t kv_head_num, void **const arrays[8],
+                                 l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Row-major GEMM C = op(A) op(B) (C is m x n), fp32 accumulation.
+ * batch_count == 0: plain GEMM on a, b, c. batch_count > 0: one GEMM per
+ * entry of the device pointer arrays a_array, b_array, c_array (a, b, c
+ * ignored). lda/ldb/ldc are the row strides of the stored matrices.
+ * Replaces launch_linear (include/kernel/linear.h:9-24,
+ * src/kernel/linear.cu:42-155), which calls cuBLAS; here it is a CUDA
+ * kernel of this library. (The reference accumulates fp16 in fp16.)
+ * ------------------------------------------------------------------------ */
+int l2k_linear(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda,
+               const void *b, int64_t ldb, void *c, int64_t ldc, int64_t batch_count, const void *const *a_array,
+               const void *const *b_array, void *const *c_array, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * QK^T at the reference's launch_linear call site (trans_B = true), per
+ * (b, q head) with grouped KV heads, without pointer arrays:
+ *   qk[b, h, i, j] = sum_d q[b, h, i, d] * k[b, h / (Hq/Hkv), j, d],
+ * i < m, j < n. q: (B, Hq, q_cache_len, hd); k: (B, Hkv, kv_cache_len, hd);
+ * qk: (B, Hq, q_cache_len, kv_cache_len). Other entries are left as is.
+ * ------------------------------------------------------------------------ */
+int l2k_qk_scores(const void *q, const void *k, void *qk, int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                  int64_t q_cache_len, int64_t kv_cache_len, int64_t head_dim, int64_t m, int64_t n, int dtype,
+                  l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Masked attention score, in place on qk (B, H, q_cache_len, kv_cache_len):
+ * for rows q < q_lens[b] and keys k < max_kv_len,
+ *   qk = mask[b, q, k] ? exp(qk / sqrt(head_dim) - m) / (sum + 1e-6) : 0
+ * (m, sum over the masked-in keys); every other entry is left untouched.
+ * Replaces launch_compute_masked_attention_score<T, unsigned char>
+ * (include/kernel/compute_masked_attention_score.h:6-12,
+ * src/kernel/compute_masked_attention_score.cu:105-140).
+ * ------------------------------------------------------------------------ */
+int l2k_compute_masked_attention_score(int64_t head_dim, uint32_t max_q_len, uint32_t max_kv_len,
+                                       const uint32_t *q_lens, const uint8_t *mask, void *qk, int64_t batch,
+                                       int64_t q_head_num, int64_t q_cache_len, int64_t kv_cache_len, int dtype,
+                                       l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * SwiGLU: output[t, i] = silu(input[t, i]) * input[t, F + i].
+ * Replaces launch_swiglu (include/kernel/swiglu.h:6-8, src/kernel/swiglu.cu:55-72).
+ * ------------------------------------------------------------------------ */
+int l2k_swiglu(const void *input, void *output, int64_t num_tokens, int64_t intermediate_size, int dtype,
+               l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused decode attention scores: QK^T + 1/sqrt(head_dim) scale + causal
+ * length mask + softmax in one pass over the K cache, for one query token
+ * per sequence. qk: (B, Hq, 1, kv_cache_len). With kv_len = kv_lens[b] and
+ * M = *max_kv_len (device pointer, e.g. from l2k_update_q_kv_lens):
+ *   qk[b,h,0,j] = exp(s_j - max) / (sum + 1e-6)  for j < kv_len,
+ *   s_j = (q[b,h] . k[b,h/(Hq/Hkv),j]) / sqrt(head_dim);
+ *   qk[b,h,0,j] = 0 for kv_len <= j < M; untouched for j >= M.
+ * This is the composition of the reference's QK^T call site
+ * (src/kernel/linear.cu:96-128), its masked softmax
+ * (src/kernel/compute_masked_attention_score.cu:12-103) and the mask
+ * "positions 0..pos" (k <= kv_len - 1), without materializing the mask.
+ * ------------------------------------------------------------------------ */
+int l2k_decode_attention_scores(const void *q, const void *k, const uint32_t *kv_lens, const uint32_t *max_kv_len,
+                                void *qk, int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                int64_t kv_cache_len, int64_t head_dim, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused prefill attention scores: the same composition for q_len query rows
+ * per sequence, with the causal mask k <= (kv_len - q_len) + q:
+ *   qk[b,h,i,j] = softmax over j < kv_len, j <= kv_len - q_len + i   (i < q_len)
+ *   qk[b,h,i,j] = 0 for masked j < max_kv_len; untouched for j >= max_kv_len
+ *   or i >= q_len.
+ * q: (B, Hq, q_cache_len, hd) from the prefill RoPE; k as for decode.
+ * BF16/F16 run QK^T on the tcgen05 tensor cores (fp32 accumulation in
+ * tensor memory); F32 runs it on the CUDA cores.
+ * ------------------------------------------------------------------------ */
+int l2k_prefill_attention_scores(const void *q, const void *k, const uint32_t *q_lens, const uint32_t *kv_lens,
+                                 uint32_t max_q_len, uint32_t max_kv_len, void *qk, int64_t batch,
+                                 int64_t q_head_num, int64_t kv_head_num, int64_t q_cache_len,
+                                 int64_t kv_cache_len, int64_t head_dim, int dtype, l2k_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLAMA2_B200_H */

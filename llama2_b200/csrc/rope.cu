@@ -1,0 +1,386 @@
+// RoPE fused with the KV-cache append, for decode and prefill, in both pair
+// layouts (interleaved (2i, 2i+1) and half (i, i + hd/2)).
+//
+// Work item = VP rotation pairs of one q or k head, or 2*VP elements of one
+// v head. gridDim.x covers the items of a token, gridDim.y strides over
+// tokens, so a single decode token already spreads over several SMs. With
+// VP = 16 / (2 sizeof(T)) every item is one 16-byte load + store (interleaved)
+// or two 8-byte ones (half pairs) — no warp shuffles, any even head_dim.
+//
+// Angles come from the host-built cos/sin table (rope_table.cpp) when the
+// reference's length-scaling factor is exactly 1 (sequence length <= 4096),
+// which makes the rotation bit-identical to the reference's CPU oracle: the
+// products are evaluated as c*x0 - s*x1 and s*x0 + c*x1 with round-to-nearest
+// intrinsics (no FMA contraction), exactly as the oracle's C++ does. Other
+// positions evaluate the reference formula on the device
+// (include/kernel/rope.cuh:14-17).
+//
+// Tokens whose cache position falls outside [0, kv_cache_len) are skipped
+// (the reference writes out of bounds there).
+//
+// Reference: src/kernel/fused_reshape_rope_kvcache_decode.cu:11-84,
+// src/kernel/fused_reshape_rope_kvcache_llama2_decode.cu:11-74,
+// src/kernel/fused_pad_reshape_transpose_rope_kvcache.cu:11-83,
+// src/kernel/fused_pad_reshape_transpose_rope_kvcache_llama2.cu:11-75.
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace l2k
+{
+namespace
+{
+
+struct RopeArgs
+{
+    const void *input;
+    const uint8_t *is_done;       // decode only
+    const uint32_t *q_lens;       // prefill only
+    const uint32_t *kv_lens;
+    const uint32_t *unpad_to_pad; // prefill only
+    void *q;
+    void *k;
+    void *v;
+    int64_t n_tokens;
+    int64_t batch;
+    int64_t hq;
+    int64_t hkv;
+    int64_t hd;
+    int64_t qc; // q rows per sequence in q (1 for decode)
+    int64_t S;
+    const float2 *table;
+    int64_t table_pos;
+};
+
+template <int BYTES>
+struct RawT;
+template <>
+struct RawT<16>
+{
+    using type = uint4;
+};
+template <>
+struct RawT<8>
+{
+    using type = uint2;
+};
+template <>
+struct RawT<4>
+{
+    using type = uint32_t;
+};
+template <>
+struct RawT<2>
+{
+    using type = uint16_t;
+};
+
+// CNT elements at p: one vector access when WIDE (alignment checked by the
+// launcher), element by element otherwise.
+template <typename T, int CNT, bool WIDE>
+__device__ __forceinline__ void load_elems(const T *p, float (&out)[CNT])
+{
+    if constexpr (WIDE)
+    {
+        using R = typename RawT<CNT * sizeof(T)>::type;
+        const R raw = *reinterpret_cast<const R *>(p);
+        T tmp[CNT];
+        __builtin_memcpy(tmp, &raw, sizeof(R));
+#pragma unroll
+        for (int e = 0; e < CNT; ++e)
+            out[e] = to_f(tmp[e]);
+    }
+    else
+    {
+#pragma unroll
+        for (int e = 0; e < CNT; ++e)
+            out[e] = to_f(p[e]);
+    }
+}
+
+template <typename T, int CNT, bool WIDE>
+__device__ __forceinline__ void store_elems(T *p, const float (&in)[CNT])
+{
+    T tmp[CNT];
+#pragma unroll
+    for (int e = 0; e < CNT; ++e)
+        tmp[e] = from_f<T>(in[e]);
+    if constexpr (WIDE)
+    {
+        using R = typename RawT<CNT * sizeof(T)>::type;
+        R raw;
+        __builtin_memcpy(&raw, tmp, sizeof(R));
+        *reinterpret_cast<R *>(p) = raw;
+    }
+    else
+    {
+#pragma unroll
+        for (int e = 0; e < CNT; ++e)
+            p[e] = tmp[e];
+    }
+}
+
+// Reference angle formula on the device (include/kernel/rope.cuh:14-17).
+__device__ __forceinline__ void rope_cos_sin_device(int64_t i, int64_t hd, uint32_t pos, uint32_t seq_len, float &c,
+                                                    float &s)
+{
+    const float theta = __fdiv_rn(1.f, powf(10000.f, __fdiv_rn(2.f * (float)i, (float)hd)));
+    const float ratio = __fdiv_rn((float)seq_len, 4096.f);
+    const float alpha = __fdiv_rn(1.f, powf(fmaxf(1.f, ratio), __fdiv_rn(2.f * (float)i, (float)(uint32_t)(hd - 2))));
+    const float angle = __fmul_rn(__fmul_rn((float)pos, alpha), theta);
+    c = cosf(angle);
+    s = sinf(angle);
+}
+
+template <typename T, int PAIRING, int VP, bool PREFILL>
+__global__ void __launch_bounds__(256) rope_kvcache_kernel(const RopeArgs a)
+{
+    const int64_t half = a.hd / 2;
+    const int pc = (int)(half / VP); // items per rotated head (and per v head)
+    const int items = (int)((a.hq + 2 * a.hkv) * pc);
+    const int it = blockIdx.x * blockDim.x + threadIdx.x;
+    if (it >= items)
+        return;
+    const int head = it / pc;
+    const int64_t i0 = (int64_t)(it - head * pc) * VP;
+    const int64_t total_heads = a.hq + 2 * a.hkv;
+
+    for (int64_t tok = blockIdx.y; tok < a.n_tokens; tok += gridDim.y)
+    {
+        int64_t seq, t;
+        uint32_t kv_len, pos;
+        if constexpr (PREFILL)
+        {
+            const int64_t padded = a.unpad_to_pad[tok];
+            seq = padded / a.qc;
+            t = padded - seq * a.qc;
+            if (seq >= a.batch)
+                continue;
+            kv_len = a.kv_lens[seq];
+            pos = kv_len - a.q_lens[seq] + (uint32_t)t;
+        }
+        else
+        {
+            seq = tok;
+            t = 0;
+            if (a.is_done[seq])
+                continue;
+            kv_len = a.kv_lens[seq];
+            pos = kv_len - 1u;
+        }
+        if ((int64_t)pos >= a.S)
+            continue;
+        const T *src = static_cast<const T *>(a.input) + (tok * total_heads + head) * a.hd;
+        if (head >= a.hq + a.hkv)
+        {
+            // v: copy 2*VP elements into cache row pos.
+            const int64_t h = head - a.hq - a.hkv;
+            T *dst = static_cast<T *>(a.v) + ((seq * a.hkv + h) * a.S + pos) * a.hd;
+            if constexpr (VP > 1)
+            {
+                using R = typename RawT<2 * VP * sizeof(T)>::type;
+                *reinterpret_cast<R *>(dst + 2 * i0) = *reinterpret_cast<const R *>(src + 2 * i0);
+            }
+            else
+            {
+                dst[2 * i0] = src[2 * i0];
+                dst[2 * i0 + 1] = src[2 * i0 + 1];
+            }
+            continue;
+        }
+        float x0[VP], x1[VP];
+        if constexpr (PAIRING == L2K_ROPE_INTERLEAVED)
+        {
+            float xx[2 * VP];
+            load_elems<T, 2 * VP, (VP > 1)>(src + 2 * i0, xx);
+#pragma unroll
+            for (int e = 0; e < VP; ++e)
+            {
+                x0[e] = xx[2 * e];
+                x1[e] = xx[2 * e + 1];
+            }
+        }
+        else
+        {
+            load_elems<T, VP, (VP > 1)>(src + i0, x0);
+            load_elems<T, VP, (VP > 1)>(src + half + i0, x1);
+        }
+        float c[VP], s[VP];
+        if (a.table && kv_len <= 4096u && (int64_t)pos < a.table_pos)
+        {
+            const float2 *row = a.table + (int64_t)pos * half + i0;
+#pragma unroll
+            for (int e = 0; e < VP; ++e)
+            {
+                const float2 cs = __ldg(row + e);
+                c[e] = cs.x;
+                s[e] = cs.y;
+            }
+        }
+        else
+        {
+#pragma unroll
+            for (int e = 0; e < VP; ++e)
+                rope_cos_sin_device(i0 + e, a.hd, pos, kv_len, c[e], s[e]);
+        }
+        float o0[VP], o1[VP];
+#pragma unroll
+        for (int e = 0; e < VP; ++e)
+        {
+            o0[e] = __fsub_rn(__fmul_rn(c[e], x0[e]), __fmul_rn(s[e], x1[e]));
+            o1[e] = __fadd_rn(__fmul_rn(s[e], x0[e]), __fmul_rn(c[e], x1[e]));
+        }
+        T *dst;
+        if (head < a.hq)
+            dst = static_cast<T *>(a.q) + ((seq * a.hq + head) * a.qc + t) * a.hd;
+        else
+            dst = static_cast<T *>(a.k) + ((seq * a.hkv + (head - a.hq)) * a.S + pos) * a.hd;
+        if constexpr (PAIRING == L2K_ROPE_INTERLEAVED)
+        {
+            float oo[2 * VP];
+#pragma unroll
+            for (int e = 0; e < VP; ++e)
+            {
+                oo[2 * e] = o0[e];
+                oo[2 * e + 1] = o1[e];
+            }
+            store_elems<T, 2 * VP, (VP > 1)>(dst + 2 * i0, oo);
+        }
+        else
+        {
+            store_elems<T, VP, (VP > 1)>(dst + i0, o0);
+            store_elems<T, VP, (VP > 1)>(dst + half + i0, o1);
+        }
+    }
+}
+
+template <typename T, int PAIRING, int VP, bool PREFILL>
+int launch_rope_vp(const RopeArgs &a, cudaStream_t stream)
+{
+    const int64_t pc = a.hd / 2 / VP;
+    const int64_t items = (a.hq + 2 * a.hkv) * pc;
+    const int block = (int)std::min<int64_t>(256, std::max<int64_t>(32, ceil_div(items, 32) * 32));
+    const int64_t gx = ceil_div(items, block);
+    const int64_t gy = std::min<int64_t>(a.n_tokens, 65535);
+    rope_kvcache_kernel<T, PAIRING, VP, PREFILL><<<dim3((unsigned)gx, (unsigned)gy), block, 0, stream>>>(a);
+    return check_launch(PREFILL ? "l2k prefill rope" : "l2k decode rope");
+}
+
+template <typename T, int PAIRING, bool PREFILL>
+int launch_rope(const RopeArgs &a, cudaStream_t stream)
+{
+    constexpr int VPMAX = 16 / (2 * sizeof(T));
+    const int64_t half = a.hd / 2;
+    const bool vec = half % VPMAX == 0 && (a.hd * (int64_t)sizeof(T)) % 16 == 0 && is_aligned(a.input, 16) &&
+                     is_aligned(a.q, 16) && is_aligned(a.k, 16) && is_aligned(a.v, 16) &&
+                     (a.table == nullptr || is_aligned(a.table, 16));
+    if (vec)
+        return launch_rope_vp<T, PAIRING, VPMAX, PREFILL>(a, stream);
+    return launch_rope_vp<T, PAIRING, 1, PREFILL>(a, stream);
+}
+
+int check_common(const RopeArgs &a, const char *name, int dtype)
+{
+    L2K_REQUIRE(dtype_ok(dtype), "%s: unsupported dtype %d", name, dtype);
+    L2K_REQUIRE(a.n_tokens >= 0 && a.batch >= 0 && a.hq >= 0 && a.hkv >= 0 && a.hd >= 0 && a.S >= 0 && a.qc >= 0,
+                "%s: negative size", name);
+    L2K_REQUIRE(a.hd % 2 == 0, "%s: head_dim must be even (got %lld)", name, (long long)a.hd);
+    L2K_REQUIRE(a.table_pos >= 0, "%s: negative rope_table_positions", name);
+    L2K_REQUIRE(a.table == nullptr || is_aligned(a.table, 8), "%s: rope_table must be 8-byte aligned", name);
+    L2K_REQUIRE_SHAPE((a.hq + 2 * a.hkv) * a.hd < (int64_t(1) << 30), "%s: too many heads", name);
+    return L2K_OK;
+}
+
+int rope_entry(const RopeArgs &a, int pairing, bool prefill, int dtype, cudaStream_t stream, const char *name)
+{
+    if (int st = check_common(a, name, dtype))
+        return st;
+    if (a.n_tokens == 0 || a.hd == 0 || a.hq + a.hkv == 0)
+        return L2K_OK;
+    L2K_REQUIRE(a.input && a.kv_lens && a.q && (a.hkv == 0 || (a.k && a.v)), "%s: null pointer", name);
+    if (prefill)
+        L2K_REQUIRE(a.q_lens && a.unpad_to_pad && a.qc > 0, "%s: null q_lens/unpad_to_pad or q_cache_len 0", name);
+    else
+        L2K_REQUIRE(a.is_done, "%s: null is_done", name);
+    L2K_DISPATCH(dtype, {
+        if (pairing == L2K_ROPE_INTERLEAVED)
+            return prefill ? launch_rope<T, L2K_ROPE_INTERLEAVED, true>(a, stream)
+                           : launch_rope<T, L2K_ROPE_INTERLEAVED, false>(a, stream);
+        return prefill ? launch_rope<T, L2K_ROPE_HALF, true>(a, stream)
+                       : launch_rope<T, L2K_ROPE_HALF, false>(a, stream);
+    });
+    return L2K_OK;
+}
+
+RopeArgs decode_args(const void *input, const uint8_t *is_done, const uint32_t *kv_lens, void *q, void *k, void *v,
+                     int64_t batch, int64_t hq, int64_t hkv, int64_t hd, int64_t S, const float *table,
+                     int64_t table_pos)
+{
+    return RopeArgs{input, is_done, nullptr, kv_lens, nullptr, q, k, v, batch, batch, hq, hkv, hd, 1, S,
+                    reinterpret_cast<const float2 *>(table), table ? table_pos : 0};
+}
+
+RopeArgs prefill_args(const void *input, const uint32_t *q_lens, const uint32_t *kv_lens, const uint32_t *unpad,
+                      void *q, void *k, void *v, int64_t n_tokens, int64_t batch, int64_t hq, int64_t hkv, int64_t hd,
+                      int64_t qc, int64_t S, const float *table, int64_t table_pos)
+{
+    return RopeArgs{input, nullptr, q_lens, kv_lens, unpad, q, k, v, n_tokens, batch, hq, hkv, hd, qc, S,
+                    reinterpret_cast<const float2 *>(table), table ? table_pos : 0};
+}
+
+} // namespace
+} // namespace l2k
+
+extern "C" int l2k_fused_reshape_rope_kvcache_decode(const void *input, const uint8_t *is_done,
+                                                     const uint32_t *kv_lens, void *q, void *k, void *v,
+                                                     int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                                     int64_t head_dim, int64_t kv_cache_len, const float *rope_table,
+                                                     int64_t rope_table_positions, int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    return rope_entry(decode_args(input, is_done, kv_lens, q, k, v, batch, q_head_num, kv_head_num, head_dim,
+                                  kv_cache_len, rope_table, rope_table_positions),
+                      L2K_ROPE_INTERLEAVED, false, dtype, stream, "l2k_fused_reshape_rope_kvcache_decode");
+}
+
+extern "C" int l2k_fused_reshape_rope_kvcache_llama2_decode(const void *input, const uint8_t *is_done,
+                                                            const uint32_t *kv_lens, void *q, void *k, void *v,
+                                                            int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                                            int64_t head_dim, int64_t kv_cache_len,
+                                                            const float *rope_table, int64_t rope_table_positions,
+                                                            int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    return rope_entry(decode_args(input, is_done, kv_lens, q, k, v, batch, q_head_num, kv_head_num, head_dim,
+                                  kv_cache_len, rope_table, rope_table_positions),
+                      L2K_ROPE_HALF, false, dtype, stream, "l2k_fused_reshape_rope_kvcache_llama2_decode");
+}
+
+extern "C" int l2k_fused_pad_reshape_transpose_rope_kvcache(const void *input, const uint32_t *q_lens,
+                                                            const uint32_t *kv_lens, const uint32_t *unpad_to_pad_idx,
+                                                            void *q, void *k, void *v, int64_t num_tokens,
+                                                            int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                                            int64_t head_dim, int64_t q_cache_len,
+                                                            int64_t kv_cache_len, const float *rope_table,
+                                                            int64_t rope_table_positions, int dtype,
+                                                            l2k_stream_t stream)
+{
+    using namespace l2k;
+    return rope_entry(prefill_args(input, q_lens, kv_lens, unpad_to_pad_idx, q, k, v, num_tokens, batch, q_head_num,
+                                   kv_head_num, head_dim, q_cache_len, kv_cache_len, rope_table,
+                                   rope_table_positions),
+                      L2K_ROPE_INTERLEAVED, true, dtype, stream, "l2k_fused_pad_reshape_transpose_rope_kvcache");
+}
+
+extern "C" int l2k_fused_pad_reshape_transpose_rope_kvcache_llama2(
+    const void *input, const uint32_t *q_lens, const uint32_t *kv_lens, const uint32_t *unpad_to_pad_idx, void *q,
+    void *k, void *v, int64_t num_tokens, int64_t batch, int64_t q_head_num, int64_t kv_head_num, int64_t head_dim,
+    int64_t q_cache_len, int64_t kv_cache_len, const float *rope_table, int64_t rope_table_positions, int dtype,
+    l2k_stream_t stream)
+{
+    using namespace l2k;
+    return rope_entry(prefill_args(input, q_lens, kv_lens, unpad_to_pad_idx, q, k, v, num_tokens, batch, q_head_num,
+                                   kv_head_num, head_dim, q_cache_len, kv_cache_len, rope_table,
+                                   rope_table_positions),
+                      L2K_ROPE_HALF, true, dtype, stream, "l2k_fused_pad_reshape_transpose_rope_kvcache_llama2");
+}

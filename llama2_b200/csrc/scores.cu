@@ -1,0 +1,53 @@
+// Fused prefill attention scores entry point.
+//
+// Dispatch: BF16/F16 run the cluster score-row kernel (decode_scores.cu) with
+// one cluster per query row, fp32 logits until the final store. F32 runs
+// QK^T on the CUDA cores (gemm.cu) followed by the causal masked softmax
+// (masked_softmax.cu): two kernels, the fp32 scores round-trip through HBM.
+#include "common.cuh"
+
+namespace l2k
+{
+int qk_scores_cuda_cores(const void *q, const void *k, void *qk, int64_t batch, int64_t Hq, int64_t Hkv, int64_t qc,
+                         int64_t S, int64_t hd, int64_t m, int64_t n, const uint32_t *row_lens, int dtype,
+                         cudaStream_t stream);
+int masked_softmax_causal(void *qk, const uint32_t *q_lens, const uint32_t *kv_lens, int64_t batch, int64_t H,
+                          int64_t qc, int64_t S, int64_t max_q, int64_t max_kv, int64_t head_dim, int dtype,
+                          cudaStream_t stream);
+int prefill_score_rows(const void *q, const void *k, const uint32_t *q_lens, const uint32_t *kv_lens,
+                       uint32_t max_kv, void *qk, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc, int64_t S,
+                       int64_t hd, int dtype, cudaStream_t stream);
+} // namespace l2k
+
+extern "C" int l2k_prefill_attention_scores(const void *q, const void *k, const uint32_t *q_lens,
+                                            const uint32_t *kv_lens, uint32_t max_q_len, uint32_t max_kv_len,
+                                            void *qk, int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                            int64_t q_cache_len, int64_t kv_cache_len, int64_t head_dim, int dtype,
+                                            l2k_stream_t stream)
+{
+    using namespace l2k;
+    L2K_REQUIRE(dtype_ok(dtype), "l2k_prefill_attention_scores: unsupported dtype %d", dtype);
+    L2K_REQUIRE(batch >= 0 && q_head_num >= 0 && kv_head_num >= 0 && head_dim > 0 && q_cache_len >= 0 &&
+                    kv_cache_len >= 0,
+                "l2k_prefill_attention_scores: bad size");
+    L2K_REQUIRE(max_q_len <= q_cache_len && max_kv_len <= kv_cache_len,
+                "l2k_prefill_attention_scores: max_q_len/max_kv_len exceed the cache dims");
+    if (batch == 0 || q_head_num == 0 || max_q_len == 0 || max_kv_len == 0)
+        return L2K_OK;
+    L2K_REQUIRE(kv_head_num > 0 && q_head_num % kv_head_num == 0,
+                "l2k_prefill_attention_scores: q_head_num must be a multiple of kv_head_num");
+    L2K_REQUIRE(q && k && q_lens && kv_lens && qk, "l2k_prefill_attention_scores: null pointer");
+    L2K_REQUIRE_SHAPE(batch <= 65535 && q_head_num <= 65535, "l2k_prefill_attention_scores: grid too large");
+    if (dtype != L2K_F32)
+    {
+        // 16-bit storage: keep the logits in fp32 until the final store (a QK^T
+        // round trip through a bf16/f16 qk buffer would cost ~1% accuracy).
+        return prefill_score_rows(q, k, q_lens, kv_lens, max_kv_len, qk, batch, q_head_num, kv_head_num,
+                                  q_cache_len, kv_cache_len, head_dim, dtype, stream);
+    }
+    if (int st = qk_scores_cuda_cores(q, k, qk, batch, q_head_num, kv_head_num, q_cache_len, kv_cache_len, head_dim,
+                                      max_q_len, max_kv_len, q_lens, dtype, stream))
+        return st;
+    return masked_softmax_causal(qk, q_lens, kv_lens, batch, q_head_num, q_cache_len, kv_cache_len, max_q_len,
+                                 max_kv_len, head_dim, dtype, stream);
+}

@@ -1,0 +1,316 @@
+"""Python mirror of the reference operator API (include/kernel/*.h of
+pentatracy5/llama2) over torch CUDA tensors.
+
+Each ``launch_*`` function keeps the reference function's name, argument
+order and meaning; tensors replace ``Tensor<T>``. Shapes are read from the
+tensors exactly as the reference's host wrappers read ``Tensor::shape()``,
+and the reference's ``assert``s become ``ValueError``s raised before anything
+is launched. Work is enqueued on torch's current CUDA stream through the C
+ABI (llama2_b200.capi); nothing here computes on the CPU.
+
+Integer tensors (ids, lengths, index maps) are 4-byte (torch.uint32 or
+torch.int32, read as unsigned); masks and done flags are torch.uint8.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import capi
+
+_DT = {torch.float32: capi.L2K_F32, torch.float16: capi.L2K_F16, torch.bfloat16: capi.L2K_BF16}
+_U32 = (torch.uint32, torch.int32)
+
+ROPE_TABLE_POSITIONS = 4096  # positions covered by the host-built cos/sin table
+
+
+def _code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}") from None
+
+
+def _dev(*ts):
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("tensors must be on a CUDA device")
+        if not t.is_contiguous():
+            raise ValueError("tensors must be contiguous")
+
+
+def _u32(t, name):
+    if t.dtype not in _U32:
+        raise ValueError(f"{name} must be a 4-byte integer tensor, got {t.dtype}")
+
+
+def _same(a, b, name):
+    if a.dtype != b.dtype:
+        raise ValueError(f"{name}: dtype mismatch {a.dtype} vs {b.dtype}")
+
+
+def _require(cond, msg):
+    if not cond:
+        raise ValueError(msg)
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+# --------------------------------------------------------------------------
+# RoPE cos/sin tables, one per (device, head_dim), built once on the host.
+# --------------------------------------------------------------------------
+_tables = {}
+_tables_lock = threading.Lock()
+
+
+def rope_table(head_dim: int, device: torch.device) -> torch.Tensor:
+    key = (torch.device(device), head_dim)
+    with _tables_lock:
+        t = _tables.get(key)
+        if t is None:
+            n = capi.lib().l2k_rope_table_floats(head_dim, ROPE_TABLE_POSITIONS)
+            host = torch.empty(n, dtype=torch.float32)
+            capi.call("l2k_rope_table_fill", host.data_ptr(), head_dim, ROPE_TABLE_POSITIONS)
+            t = host.to(device)
+            _tables[key] = t
+    return t
+
+
+# --------------------------------------------------------------------------
+# Operators
+# --------------------------------------------------------------------------
+def launch_embedding(input_ids, embed_table, output):
+    """include/kernel/embedding.h:6-9"""
+    _dev(input_ids, embed_table, output)
+    _u32(input_ids, "input_ids")
+    _same(embed_table, output, "launch_embedding")
+    n, (vocab, dim) = input_ids.shape[0], embed_table.shape
+    _require(tuple(output.shape) == (n, dim), "Incorrect output size")
+    capi.call("l2k_embedding", input_ids.data_ptr(), n, embed_table.data_ptr(), vocab, dim, output.data_ptr(),
+              _code(output), _stream())
+
+
+def launch_fused_add_residual_rmsnorm(weights, x, residual, add_residual: bool):
+    """include/kernel/fused_add_residual_rmsnorm.h:16-19 (add_residual is the template flag)."""
+    _dev(weights, x, residual)
+    _same(x, residual, "launch_fused_add_residual_rmsnorm")
+    _same(x, weights, "launch_fused_add_residual_rmsnorm")
+    n, dim = x.shape
+    _require(tuple(residual.shape) == (n, dim), "Incorrect residual size")
+    _require(tuple(weights.shape) == (dim,), "Incorrect rmsnorm weight size")
+    capi.call("l2k_fused_add_residual_rmsnorm", weights.data_ptr(), x.data_ptr(), residual.data_ptr(), n, dim,
+              int(bool(add_residual)), _code(x), _stream())
+
+
+def _rope_decode(name, input, is_done, kv_lens, q, k, v, table):
+    _dev(input, is_done, kv_lens, q, k, v)
+    _u32(kv_lens, "kv_lens")
+    for t in (q, k, v):
+        _same(input, t, name)
+    b, hq, one, hd = q.shape
+    hkv, s = k.shape[1], k.shape[2]
+    _require(hd % 2 == 0, "Head dim should be even")
+    _require(k.shape[3] == hd and v.shape[3] == hd, "Head dim of q k v do not match")
+    _require(v.shape[1] == hkv, "Head num of k v do not match")
+    _require(input.shape[1] == (hq + 2 * hkv) * hd, "Incorrect embedding dim")
+    _require(input.shape[0] == b and is_done.shape[0] == b and kv_lens.shape[0] == b, "Incorrect batch size")
+    _require(k.shape[0] == b and v.shape[0] == b, "Batch size of k v do not match")
+    _require(one == 1, "Incorrect q cache length")
+    _require(v.shape[2] == s, "k v cache length do not match")
+    tab = rope_table(hd, q.device) if table else None
+    capi.call(name, input.data_ptr(), is_done.data_ptr(), kv_lens.data_ptr(), q.data_ptr(), k.data_ptr(),
+              v.data_ptr(), b, hq, hkv, hd, s, tab.data_ptr() if tab is not None else None,
+              ROPE_TABLE_POSITIONS if tab is not None else 0, _code(q), _stream())
+
+
+def launch_fused_reshape_rope_kvcache_decode(input, is_done, kv_lens, q, k, v, *, use_table=True):
+    """include/kernel/fused_reshape_rope_kvcache_decode.h:6-12 (pairs (2i, 2i+1))."""
+    _rope_decode("l2k_fused_reshape_rope_kvcache_decode", input, is_done, kv_lens, q, k, v, use_table)
+
+
+def launch_fused_reshape_rope_kvcache_llama2_decode(input, is_done, kv_lens, q, k, v, *, use_table=True):
+    """include/kernel/fused_reshape_rope_kvcache_llama2_decode.h:6-12 (pairs (i, i + hd/2))."""
+    _rope_decode("l2k_fused_reshape_rope_kvcache_llama2_decode", input, is_done, kv_lens, q, k, v, use_table)
+
+
+def _rope_prefill(name, input, q_lens, kv_lens, unpad_to_pad_idx, q, k, v, table):
+    _dev(input, q_lens, kv_lens, unpad_to_pad_idx, q, k, v)
+    for t, nm in ((q_lens, "q_lens"), (kv_lens, "kv_lens"), (unpad_to_pad_idx, "unpad_to_pad_idx")):
+        _u32(t, nm)
+    for t in (q, k, v):
+        _same(input, t, name)
+    n = input.shape[0]
+    b, hq, qc, hd = q.shape
+    hkv, s = k.shape[1], k.shape[2]
+    _require(hd % 2 == 0, "Head dim should be even")
+    _require(k.shape[3] == hd and v.shape[3] == hd, "Head dim of q k v do not match")
+    _require(v.shape[1] == hkv, "Head num of k v do not match")
+    _require(input.shape[1] == (hq + 2 * hkv) * hd, "Incorrect embedding dim")
+    _require(q_lens.shape[0] == b and kv_lens.shape[0] == b, "Incorrect batch size of sequence length")
+    _require(k.shape[0] == b and v.shape[0] == b, "Batch size of k v do not match")
+    _require(v.shape[2] == s, "k v cache length do not match")
+    _require(unpad_to_pad_idx.numel() >= n, "unpad_to_pad_idx too small")
+    tab = rope_table(hd, q.device) if table else None
+    capi.call(name, input.data_ptr(), q_lens.data_ptr(), kv_lens.data_ptr(), unpad_to_pad_idx.data_ptr(),
+              q.data_ptr(), k.data_ptr(), v.data_ptr(), n, b, hq, hkv, hd, qc, s,
+              tab.data_ptr() if tab is not None else None, ROPE_TABLE_POSITIONS if tab is not None else 0, _code(q),
+              _stream())
+
+
+def launch_fused_pad_reshape_transpose_rope_kvcache(input, q_lens, kv_lens, unpad_to_pad_idx, q, k, v, *,
+                                                    use_table=True):
+    """include/kernel/fused_pad_reshape_transpose_rope_kvcache.h:6-13"""
+    _rope_prefill("l2k_fused_pad_reshape_transpose_rope_kvcache", input, q_lens, kv_lens, unpad_to_pad_idx, q, k, v,
+                  use_table)
+
+
+def launch_fused_pad_reshape_transpose_rope_kvcache_llama2(input, q_lens, kv_lens, unpad_to_pad_idx, q, k, v, *,
+                                                           use_table=True):
+    """include/kernel/fused_pad_reshape_transpose_rope_kvcache_llama2.h:6-13"""
+    _rope_prefill("l2k_fused_pad_reshape_transpose_rope_kvcache_llama2", input, q_lens, kv_lens, unpad_to_pad_idx,
+                  q, k, v, use_table)
+
+
+def launch_update_q_kv_lens(q_lens, kv_lens, max_q_len, max_kv_len):
+    """include/kernel/update_q_kv_lens.h:6-9.
+
+    max_q_len / max_kv_len are 1-element tensors. On the device the results
+    stay there (no synchronization). On the host, as in the reference
+    (src/kernel/update_q_kv_lens.cu:52-61), the call synchronizes and the
+    results land in them.
+    """
+    _dev(q_lens, kv_lens)
+    _u32(q_lens, "q_lens")
+    _u32(kv_lens, "kv_lens")
+    b = q_lens.shape[0]
+    _require(kv_lens.shape[0] == b, "Incorrect kv_lens size")
+    if max_q_len.is_cuda and max_kv_len.is_cuda:
+        capi.call("l2k_update_q_kv_lens", q_lens.data_ptr(), kv_lens.data_ptr(), b, max_q_len.data_ptr(),
+                  max_kv_len.data_ptr(), _stream())
+        return
+    dev = torch.empty(2, dtype=torch.uint32, device=q_lens.device)
+    capi.call("l2k_update_q_kv_lens", q_lens.data_ptr(), kv_lens.data_ptr(), b, dev.data_ptr(), dev.data_ptr() + 4,
+              _stream())
+    host = dev.cpu()
+    max_q_len.view(-1)[0] = host[0].to(max_q_len.dtype)
+    max_kv_len.view(-1)[0] = host[1].to(max_kv_len.dtype)
+
+
+def launch_build_causal_mask(max_q_len, max_kv_len, q_lens, kv_lens, mask):
+    """include/kernel/build_causal_mask.h:6-11 (the reference's unsigned-wrap expression)."""
+    _dev(q_lens, kv_lens, mask)
+    _require(mask.dtype == torch.uint8, "mask must be uint8")
+    b, qc, s = mask.shape
+    capi.call("l2k_build_causal_mask", int(max_q_len), int(max_kv_len), q_lens.data_ptr(), kv_lens.data_ptr(),
+              mask.data_ptr(), b, qc, s, _stream())
+
+
+def launch_build_padding_index_maps(num_input_tokens, seq_lens, unpad_to_pad_idx, seq_offsets):
+    """include/kernel/build_padding_index_maps.h:6-10 (unpad_to_pad_idx is (batch, q_cache_len))."""
+    _dev(seq_lens, unpad_to_pad_idx, seq_offsets)
+    b = seq_lens.shape[0]
+    qc = unpad_to_pad_idx.shape[1] if unpad_to_pad_idx.dim() == 2 else unpad_to_pad_idx.shape[0]
+    _require(unpad_to_pad_idx.numel() >= num_input_tokens, "unpad_to_pad_idx too small")
+    _require(seq_offsets.shape[0] == b, "Incorrect seq_offsets size")
+    capi.call("l2k_build_padding_index_maps", int(num_input_tokens), seq_lens.data_ptr(), b, qc,
+              unpad_to_pad_idx.data_ptr(), seq_offsets.data_ptr(), _stream())
+
+
+def launch_build_q_k_v_qk_qkv_array(q, q_decode, k, v, qk, qk_decode, qkv, qkv_decode, q_array, q_decode_array,
+                                    k_array, v_array, qk_array, qk_decode_array, qkv_array, qkv_decode_array):
+    """include/kernel/build_q_k_v_qk_qkv_array.h:6-22 (arrays: int64 tensors of batch * q_head_num)."""
+    tensors = (q, q_decode, k, v, qk, qk_decode, qkv, qkv_decode)
+    arrays = (q_array, q_decode_array, k_array, v_array, qk_array, qk_decode_array, qkv_array, qkv_decode_array)
+    _dev(*tensors, *arrays)
+    b, hq = q.shape[0], q.shape[1]
+    hkv = k.shape[1]
+    _require(hq % hkv == 0, "q_head_num is not divisible by kv_head_num")
+    for a in arrays:
+        _require(a.numel() == b * hq and a.element_size() == 8, "Incorrect pointer array size")
+    bases = (capi.vp * 8)(*[t.data_ptr() for t in tensors])
+    slices = (capi.i64 * 8)(*[t.shape[2] * t.shape[3] for t in tensors])
+    outs = (capi.vp * 8)(*[a.data_ptr() for a in arrays])
+    capi.call("l2k_build_q_k_v_qk_qkv_array", bases, slices, q.element_size(), b, hq, hkv, outs, _stream())
+
+
+def launch_linear(trans_A, trans_B, M, N, K, A, B, C, A_array=None, B_array=None, C_array=None):
+    """include/kernel/linear.h:9-24 (no cuBLAS handle: the library's own kernel runs)."""
+    _dev(A, B, C)
+    _same(A, C, "launch_linear")
+    _same(B, C, "launch_linear")
+    dim = C.dim()
+    _require(dim >= 2 and A.dim() == dim and B.dim() == dim, "Matrix dim do not match")
+    lda, ldb, ldc = A.shape[-1], B.shape[-1], C.shape[-1]
+    if dim > 2:
+        batch = 1
+        for s in C.shape[:-2]:
+            batch *= s
+        for arr in (A_array, B_array, C_array):
+            _require(arr is not None and arr.numel() == batch, "Illegal pointer array size")
+        capi.call("l2k_linear", int(trans_A), int(trans_B), M, N, K, None, lda, None, ldb, None, ldc, batch,
+                  A_array.data_ptr(), B_array.data_ptr(), C_array.data_ptr(), _code(C), _stream())
+    else:
+        capi.call("l2k_linear", int(trans_A), int(trans_B), M, N, K, A.data_ptr(), lda, B.data_ptr(), ldb,
+                  C.data_ptr(), ldc, 0, None, None, None, _code(C), _stream())
+
+
+def launch_qk_scores(q, k, qk, M, N):
+    """QK^T at the launch_linear call site, per (seq, head) with grouped KV heads."""
+    _dev(q, k, qk)
+    _same(q, k, "launch_qk_scores")
+    _same(q, qk, "launch_qk_scores")
+    b, hq, qc, hd = q.shape
+    hkv, s = k.shape[1], k.shape[2]
+    _require(tuple(qk.shape) == (b, hq, qc, s), "Incorrect qk size")
+    capi.call("l2k_qk_scores", q.data_ptr(), k.data_ptr(), qk.data_ptr(), b, hq, hkv, qc, s, hd, M, N, _code(q),
+              _stream())
+
+
+def launch_compute_masked_attention_score(head_dim, max_q_len, max_kv_len, q_lens, mask, qk):
+    """include/kernel/compute_masked_attention_score.h:6-12"""
+    _dev(q_lens, mask, qk)
+    b, hq, qc, s = qk.shape
+    _require(q_lens.shape[0] == b, "Incorrect q_lens size")
+    _require(tuple(mask.shape) == (b, qc, s), "Incorrect mask size")
+    _require(max_q_len <= qc and max_kv_len <= s, "Incorrect max_q_len / max_kv_len")
+    capi.call("l2k_compute_masked_attention_score", head_dim, int(max_q_len), int(max_kv_len), q_lens.data_ptr(),
+              mask.data_ptr(), qk.data_ptr(), b, hq, qc, s, _code(qk), _stream())
+
+
+def launch_swiglu(input, output):
+    """include/kernel/swiglu.h:6-8"""
+    _dev(input, output)
+    _same(input, output, "launch_swiglu")
+    n, f = output.shape
+    _require(tuple(input.shape) == (n, 2 * f), "Incorrect input size")
+    capi.call("l2k_swiglu", input.data_ptr(), output.data_ptr(), n, f, _code(output), _stream())
+
+
+def decode_attention_scores(q, k, kv_lens, max_kv_len, qk):
+    """Fused QK^T + scale + length mask + softmax for one query token per sequence.
+
+    q (B, Hq, 1, hd); k (B, Hkv, S, hd); qk (B, Hq, 1, S); max_kv_len: 1-element
+    device tensor (e.g. written by launch_update_q_kv_lens)."""
+    _dev(q, k, kv_lens, max_kv_len, qk)
+    _same(q, k, "decode_attention_scores")
+    _same(q, qk, "decode_attention_scores")
+    b, hq, one, hd = q.shape
+    hkv, s = k.shape[1], k.shape[2]
+    _require(one == 1 and tuple(qk.shape) == (b, hq, 1, s), "Incorrect q / qk size")
+    capi.call("l2k_decode_attention_scores", q.data_ptr(), k.data_ptr(), kv_lens.data_ptr(), max_kv_len.data_ptr(),
+              qk.data_ptr(), b, hq, hkv, s, hd, _code(q), _stream())
+
+
+def prefill_attention_scores(q, k, q_lens, kv_lens, max_q_len, max_kv_len, qk):
+    """Fused QK^T + scale + causal mask + softmax for q_len query rows per sequence."""
+    _dev(q, k, q_lens, kv_lens, qk)
+    _same(q, k, "prefill_attention_scores")
+    _same(q, qk, "prefill_attention_scores")
+    b, hq, qc, hd = q.shape
+    hkv, s = k.shape[1], k.shape[2]
+    _require(tuple(qk.shape) == (b, hq, qc, s), "Incorrect qk size")
+    capi.call("l2k_prefill_attention_scores", q.data_ptr(), k.data_ptr(), q_lens.data_ptr(), kv_lens.data_ptr(),
+              int(max_q_len), int(max_kv_len), qk.data_ptr(), b, hq, hkv, qc, s, hd, _code(q), _stream())

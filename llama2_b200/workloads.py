@@ -1,0 +1,127 @@
+"""Workload definitions (Llama-2 layer-kernel shapes) and seeded synthetic inputs.
+
+The five workloads are the reference path's benchmark configurations:
+
+  tiny      dim 288, 6 heads of 48, hidden 768, cache 256, batch 1, fp32 decode
+  7b-b1     Llama-2-7B dims (4096, 32 x 128, hidden 11008), cache 4096, batch 1, fp32 decode
+  7b-b64    7B dims, batch 64 decode (fp32, or bf16 I/O)
+  7b-prefill 7B dims, 8 x 2048-token prefill, bf16 I/O, causal scores [8,32,2048,2048]
+  13b-b256  Llama-2-13B dims (5120, 40 x 128, hidden 13824), batch 256 decode, fp16
+
+Inputs follow the stated distributions: token ids U[0, 32000), embedding
+table N(0, 0.02), RMSNorm weight U(0.5, 1.5), q/k/v and gate/up activations
+N(0, 1) (standing in for the projection outputs), KV cache N(0, 1), and one
+position per sequence uniform in [1, 4095] ([0, 255] for tiny). Generated on
+the host with numpy's seeded Generator (so CPU oracles see identical bits)
+and copied once to the device.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import numpy as np
+
+
+@dataclasses.dataclass(frozen=True)
+class Workload:
+    name: str
+    dim: int
+    heads: int
+    head_dim: int
+    hidden: int
+    vocab: int
+    kv_cache_len: int
+    batch: int
+    dtype: str          # "f32" | "bf16" | "f16"
+    pairing: int        # 0 interleaved, 1 half (the reference's "_llama2")
+    prefill_len: int = 0  # tokens per sequence for prefill workloads (0 = decode)
+    pos_lo: int = 1
+    pos_hi: int = 4095
+
+    @property
+    def decode(self) -> bool:
+        return self.prefill_len == 0
+
+    @property
+    def tokens(self) -> int:
+        return self.batch * (self.prefill_len or 1)
+
+
+WORKLOADS = {
+    "tiny": Workload("tiny", 288, 6, 48, 768, 32000, 256, 1, "f32", 0, pos_lo=0, pos_hi=255),
+    "7b-b1": Workload("7b-b1", 4096, 32, 128, 11008, 32000, 4096, 1, "f32", 1),
+    "7b-b64": Workload("7b-b64", 4096, 32, 128, 11008, 32000, 4096, 64, "f32", 1),
+    "7b-b64-bf16": Workload("7b-b64-bf16", 4096, 32, 128, 11008, 32000, 4096, 64, "bf16", 1),
+    "7b-prefill": Workload("7b-prefill", 4096, 32, 128, 11008, 32000, 2048, 8, "bf16", 1, prefill_len=2048),
+    "13b-b256": Workload("13b-b256", 5120, 40, 128, 13824, 32000, 4096, 256, "f16", 1),
+}
+
+
+def with_batch(w: Workload, batch: int) -> Workload:
+    return dataclasses.replace(w, batch=batch)
+
+
+def np_dtype(dt: str):
+    return np.float32
+
+
+def host_inputs(w: Workload, seed: int = 0, rank: int = 0, kv_cache: bool = True) -> dict:
+    """Seeded float32 / uint32 host arrays for one step of workload `w`.
+
+    Decode: positions p ~ U[pos_lo, pos_hi]; kv_lens holds p (the length
+    before this step's token), and the length update makes it p + 1.
+    Prefill: a fresh prefill (kv_lens = 0 before the update, q_lens = prefill_len).
+    """
+    rng = np.random.default_rng([seed, rank])
+    d, h, hd, f, s = w.dim, w.heads, w.head_dim, w.hidden, w.kv_cache_len
+    t = w.tokens
+    out = {
+        "embed_table": (rng.standard_normal((w.vocab, d), dtype=np.float32) * np.float32(0.02)),
+        "norm_weight": rng.uniform(0.5, 1.5, d).astype(np.float32),
+        "ids": rng.integers(0, w.vocab, t, dtype=np.uint32),
+        "qkv": rng.standard_normal((t, 3 * d), dtype=np.float32),
+        "gate_up": rng.standard_normal((t, 2 * f), dtype=np.float32),
+        "is_done": np.zeros(w.batch, np.uint8),
+    }
+    if w.decode:
+        out["q_lens"] = np.ones(w.batch, np.uint32)
+        out["kv_lens"] = rng.integers(w.pos_lo, w.pos_hi + 1, w.batch, dtype=np.uint32)
+    else:
+        out["q_lens"] = np.full(w.batch, w.prefill_len, np.uint32)
+        out["kv_lens"] = np.zeros(w.batch, np.uint32)
+    if kv_cache:
+        out["k_cache"] = rng.standard_normal((w.batch, h, s, hd), dtype=np.float32)
+        out["v_cache"] = rng.standard_normal((w.batch, h, s, hd), dtype=np.float32)
+    else:
+        out["cache_seed"] = seed * 1000003 + rank
+    return out
+
+
+def host_cache_ok(w: Workload, limit_elems: int = 1 << 28) -> bool:
+    """Whether the KV cache is small enough to draw on the host (<= 1 GiB fp32 each)."""
+    return w.batch * w.heads * w.kv_cache_len * w.head_dim <= limit_elems
+
+
+def algorithmic_bytes(w: Workload, kv_lens_after: np.ndarray) -> int:
+    """Mandatory HBM bytes of one chain step (reads + writes, no intermediates):
+    embedding 2*D*s per token, RMSNorm 2*D*s per token + D*s weight,
+    RoPE/KV 6*D*s per token (read q, k, v; write q, k row, v row), scores
+    D*s (q) + K rows 0..pos (D*s per key) + H*s per score written (all keys
+    < max_kv of each row are written), SwiGLU 3*F*s per token."""
+    s = 2 if w.dtype in ("bf16", "f16") else 4
+    d, f, h = w.dim, w.hidden, w.heads
+    t = w.tokens
+    kv = np.asarray(kv_lens_after, np.int64)
+    max_kv = int(kv.max()) if kv.size else 0
+    per_tok = 2 * d * s + 2 * d * s + 6 * d * s + 3 * f * s
+    total = t * per_tok + d * s
+    if w.decode:
+        total += w.batch * d * s                  # q read by the scores
+        total += int(kv.sum()) * d * s            # K rows 0..pos of every head
+        total += w.batch * h * max_kv * s         # score rows written
+    else:
+        q = w.prefill_len
+        total += t * d * s                        # q read
+        total += w.batch * max_kv * d * s         # K read
+        total += w.batch * h * q * max_kv * s     # score matrix written (zeros included)
+    return int(total)

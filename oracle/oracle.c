@@ -113,6 +113,13 @@ static void orc_rotate_head(int pairing, const float *head, int64_t head_dim,
     }
 }
 
+/* One head rotated as above (exported for the CPU chain runner). */
+void orc_rotate_one_head(int pairing, const float *head, int64_t head_dim, uint32_t pos, uint32_t seq_len,
+                         float *out)
+{
+    orc_rotate_head(pairing, head, head_dim, pos, seq_len, out);
+}
+
 /* ------------------------------------------------------------------------
  * Decode RoPE + KV-cache append.
  * Follows compute_expected_decode, test_fused_reshape_rope_kvcache_decode.cu:37-97

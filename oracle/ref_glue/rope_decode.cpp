@@ -13,3 +13,12 @@ extern "C" void ref_rope_kvcache_decode(const float *input, const unsigned char 
     ref_glue_out(ek, k);
     ref_glue_out(ev, v);
 }
+
+// One head rotated by the reference's own apply_rotation_decode (:14-35),
+// without compute_expected_decode's whole-cache output buffers.
+extern "C" void ref_rotate_head(const float *head, unsigned int hd, unsigned int pos, unsigned int seq_len, float *out)
+{
+    std::vector<float> o;
+    apply_rotation_decode(ref_glue_vec(head, hd), hd, pos, seq_len, o);
+    ref_glue_out(o, out);
+}

@@ -13,3 +13,13 @@ extern "C" void ref_rope_kvcache_llama2_decode(const float *input, const unsigne
     ref_glue_out(ek, k);
     ref_glue_out(ev, v);
 }
+
+// One head rotated by the reference's own apply_rotation_llama2_decode (:14-36),
+// without compute_expected_decode's whole-cache output buffers.
+extern "C" void ref_rotate_head_llama2(const float *head, unsigned int hd, unsigned int pos, unsigned int seq_len,
+                                       float *out)
+{
+    std::vector<float> o;
+    apply_rotation_llama2_decode(ref_glue_vec(head, hd), hd, pos, seq_len, o);
+    ref_glue_out(o, out);
+}

@@ -1,0 +1,85 @@
+"""The C-ABI library on the CPU: it loads, exports every entry point that
+include/llama2_b200.h declares, and rejects bad arguments before launching
+anything (these calls never reach the GPU)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from llama2_b200 import capi
+from oracle import port
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "llama2_b200.h")
+
+
+def declared_names():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(l2k_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_names()
+    assert "l2k_embedding" in names and "l2k_decode_attention_scores" in names
+    assert len(names) >= 20
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(capi.LIB_PATH)
+    missing = [n for n in declared_names() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_covers_every_declared_symbol():
+    assert sorted(capi.exported_names()) == declared_names()
+
+
+def test_status_strings():
+    lib = capi.lib()
+    assert lib.l2k_status_string(0) == b"ok"
+    assert lib.l2k_status_string(3) == b"unsupported shape"
+    assert lib.l2k_abi_version() == 1
+
+
+@pytest.mark.parametrize("call,args,status", [
+    ("l2k_embedding", (None, -1, None, 10, 8, None, 0, None), 1),
+    ("l2k_embedding", (None, 4, None, 10, 8, None, 7, None), 1),
+    ("l2k_swiglu", (None, None, 2, -4, 0, None), 1),
+    ("l2k_swiglu", (None, None, 2, 4, 0, None), 1),
+    ("l2k_fused_add_residual_rmsnorm", (None, None, None, 2, 8, 0, 0, None), 1),
+    ("l2k_fused_reshape_rope_kvcache_decode", (None, None, None, None, None, None, 1, 2, 2, 7, 8, None, 0, 0, None), 1),
+    ("l2k_build_causal_mask", (5, 2, None, None, None, 1, 4, 4, None), 1),
+    ("l2k_build_padding_index_maps", (4, None, 20000, 4, None, None, None), 3),
+    ("l2k_decode_attention_scores", (None, None, None, None, None, 1, 3, 2, 16, 8, 0, None), 1),
+    ("l2k_prefill_attention_scores", (None, None, None, None, 9, 4, None, 1, 2, 2, 8, 8, 16, 0, None), 1),
+    ("l2k_compute_masked_attention_score", (16, 4, 4, None, None, None, 1, 1, 4, 4, 9, None), 1),
+])
+def test_bad_arguments_are_rejected(call, args, status):
+    with pytest.raises(capi.L2KError) as e:
+        capi.call(call, *args)
+    assert e.value.status == status
+    assert capi.lib().l2k_last_error_message()
+
+
+def test_empty_inputs_are_noops():
+    # Zero-sized work returns before touching any pointer or the device.
+    capi.call("l2k_embedding", None, 0, None, 10, 8, None, 0, None)
+    capi.call("l2k_swiglu", None, None, 0, 16, 2, None)
+    capi.call("l2k_fused_add_residual_rmsnorm", None, None, None, 0, 64, 1, 1, None)
+
+
+@pytest.mark.parametrize("hd", [2, 4, 48, 64, 128])
+def test_rope_table_matches_oracle_bitwise(hd):
+    n_pos = 512
+    n = capi.lib().l2k_rope_table_floats(hd, n_pos)
+    assert n == n_pos * hd
+    t = np.zeros(n, np.float32)
+    capi.call("l2k_rope_table_fill", t.ctypes.data, hd, n_pos)
+    t = t.reshape(n_pos, hd // 2, 2)
+    for pos in range(0, n_pos, 37):
+        for i in range(hd // 2):
+            c, s = port.rope_cos_sin(i, hd, pos, pos + 1)
+            assert t[pos, i, 0] == np.float32(c) and t[pos, i, 1] == np.float32(s), (pos, i)
