@@ -265,6 +265,16 @@ int l2k_prefill_attention_scores(const void *q, const void *k, const uint32_t *q
                                  int64_t q_head_num, int64_t kv_head_num, int64_t q_cache_len,
                                  int64_t kv_cache_len, int64_t head_dim, int dtype, l2k_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Device-side error code recorded by kernels that wait on mbarriers (the
+ * tcgen05 prefill scores): 0 = none. Every such wait is bounded; a wait that
+ * expires records its code here and the kernel exits instead of hanging.
+ * Synchronizes with the device. clear != 0 resets the code. Returns -1 if
+ * the code could not be read. (No counterpart in the reference, which has
+ * no such waits.)
+ * ------------------------------------------------------------------------ */
+int l2k_device_error(int clear);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,6 +48,7 @@ SIGNATURES = {
     "l2k_swiglu": [vp, vp, i64, i64, cint, vp],
     "l2k_decode_attention_scores": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],
     "l2k_prefill_attention_scores": [vp, vp, vp, vp, u32, u32, vp, i64, i64, i64, i64, i64, i64, cint, vp],
+    "l2k_device_error": ([cint], cint),
 }
 
 _lib = None

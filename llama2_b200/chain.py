@@ -80,14 +80,31 @@ class Chain:
         self._pinned = None
 
     # ------------------------------------------------------------------
-    def step(self):
-        """Enqueue one chain step on the current stream."""
+    def step(self, branches=None):
+        """Enqueue one chain step on the current stream.
+
+        branches: optional pair of side streams. The lengths update (and the
+        padding maps) run first on the current stream; then embedding ->
+        RMSNorm runs on branches[0], SwiGLU on branches[1] and RoPE -> scores
+        on the current stream, which finally waits for both branches. The
+        three sub-chains share no data, so the step's critical path is the
+        longest of them instead of their sum."""
         w = self.w
+        main = torch.cuda.current_stream(self.device)
         ops.launch_update_q_kv_lens(self.q_lens, self.kv_lens, self.max_lens[0:1], self.max_lens[1:2])
         if not w.decode:
             ops.launch_build_padding_index_maps(w.tokens, self.q_lens, self.unpad_to_pad, self.seq_offsets)
-        ops.launch_embedding(self.ids, self.embed_table, self.x)
-        ops.launch_fused_add_residual_rmsnorm(self.norm_weight, self.x, self.normed, False)
+        if branches:
+            for s in branches:
+                s.wait_stream(main)
+            with torch.cuda.stream(branches[0]):
+                ops.launch_embedding(self.ids, self.embed_table, self.x)
+                ops.launch_fused_add_residual_rmsnorm(self.norm_weight, self.x, self.normed, False)
+            with torch.cuda.stream(branches[1]):
+                ops.launch_swiglu(self.gate_up, self.ffn_out)
+        else:
+            ops.launch_embedding(self.ids, self.embed_table, self.x)
+            ops.launch_fused_add_residual_rmsnorm(self.norm_weight, self.x, self.normed, False)
         if w.decode:
             rope = (ops.launch_fused_reshape_rope_kvcache_llama2_decode if w.pairing
                     else ops.launch_fused_reshape_rope_kvcache_decode)
@@ -100,7 +117,11 @@ class Chain:
                  use_table=self.use_table)
             ops.prefill_attention_scores(self.q, self.k_cache, self.q_lens, self.kv_lens, self.max_q, self.max_kv,
                                          self.qk)
-        ops.launch_swiglu(self.gate_up, self.ffn_out)
+        if branches:
+            for s in branches:
+                main.wait_stream(s)
+        else:
+            ops.launch_swiglu(self.gate_up, self.ffn_out)
 
     def kernels_per_step(self) -> int:
         """Kernel launches of this library per step (the prefill scores may be two)."""
@@ -111,7 +132,8 @@ class Chain:
         self.kv_lens.copy_(self.kv_lens_initial, non_blocking=True)
 
     def capture(self):
-        """Record step() as a CUDA graph; replay() then launches it."""
+        """Record step() as a CUDA graph with its three independent sub-chains as
+        parallel branches; replay() then launches the whole step at once."""
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
@@ -119,8 +141,9 @@ class Chain:
             self.reset_lengths()
         torch.cuda.current_stream(self.device).wait_stream(s)
         g = torch.cuda.CUDAGraph()
+        branches = (torch.cuda.Stream(device=self.device), torch.cuda.Stream(device=self.device))
         with torch.cuda.graph(g):
-            self.step()
+            self.step(branches)
         self.graph = g
         self.reset_lengths()
         return g

@@ -1,20 +1,16 @@
-// Fused decode attention scores: QK^T + 1/sqrt(hd) + length mask + softmax
-// in one pass over the K cache.
+// Attention score rows: QK^T + 1/sqrt(hd) + causal/length mask + softmax in
+// one pass over the K cache — the fused decode operator, and the prefill
+// operator for shapes the tensor-core kernel does not take.
 //
-// Layout: one (seq, q head) score row is split over a thread-block cluster
-// of C CTAs; CTA c owns keys [c*chunk, (c+1)*chunk). Each CTA
-//   1. streams its K rows (contiguous in the (B, Hkv, S, hd) cache) with
-//      16-byte read-once loads: a K row spans LPR = hd*sizeof(T)/16 lanes,
-//      a warp issues R row-loads per iteration (4 KB in flight per warp) and
-//      folds the R partial dot products with a transpose-reduce
-//      (R - 1 + log2(LPR/R) shuffles for R rows instead of R*log2(LPR));
-//   2. keeps the scaled logits of its keys in shared memory and reduces its
-//      local max m_c and sum l_c = sum exp(s - m_c);
-//   3. reads every peer's (m_c, l_c) through distributed shared memory after
-//      one cluster barrier, forms the row max and denominator, and writes its
-//      normalized probabilities once.
-// HBM traffic is the K rows 0..kv_len-1, q, and the score row: no logits
-// round trip, no mask tensor, no second kernel.
+// A score row is (seq, q head, query row). Its keys are cut into 16 KB
+// blocks of whole K rows (contiguous in the (B, Hkv, S, hd) cache) and spread
+// over a thread-block cluster of C CTAs (block g -> rank g % C). Each CTA
+// streams its blocks with cp.async.bulk (TMA) into a 4-stage shared-memory
+// ring, computes the logits of its keys from shared memory, reduces its
+// local max and sum of exponentials, exchanges them with its peers through
+// distributed shared memory after one cluster barrier, and writes its
+// normalized probabilities once. HBM traffic: the visible K rows, q, and
+// the score row — no logits round trip, no mask tensor, no second kernel.
 //
 // Reference composition: QK^T via cuBLAS batched GEMM (src/kernel/linear.cu:96-128)
 // + masked softmax (src/kernel/compute_masked_attention_score.cu:12-103)
@@ -146,74 +142,223 @@ __device__ __forceinline__ void finish_row(cg::cluster_group &cluster, const flo
     cluster.sync(); // peers may still be reading stats[0]
 }
 
+// ---------------------------------------------------------------------------
+// Streaming kernel (head_dim * sizeof(T) in {64, 128, 256, 512} bytes).
+// Keys are cut into 16 KB blocks of whole K rows (contiguous in the cache);
+// global block g belongs to cluster rank g % C, so every CTA of the cluster
+// has work whatever kv_len is. Per CTA, warp 4 is the producer: one lane
+// issues cp.async.bulk copies of the CTA's blocks into a 4-stage shared
+// ring (mbarrier full/empty pairs, bounded waits); warps 0..3 consume stage
+// w: each lane holds a 16-byte slice of q, reads the matching slice of R K
+// rows from shared memory per step and folds the R partial dot products with
+// multi_reduce. Logits stay in shared memory for the cluster softmax.
+// ---------------------------------------------------------------------------
+constexpr int kNS = 4;                 // ring stages == consumer warps
+constexpr int kBlockBytes = 16384;     // one key block
+constexpr int kStreamThreads = 32 * (kNS + 1);
+constexpr long long kWaitCycles = 4000000000LL; // ~2 s
+
+__device__ int g_scores_error = 0;     // first timeout code of this file's kernels
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity)
+{
+    const long long t0 = clock64();
+    while (true)
+    {
+        uint32_t done;
+        asm volatile("{\n\t.reg .pred p;\n\t"
+                     "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done)
+                     : "r"(bar), "r"(parity)
+                     : "memory");
+        if (done)
+            return true;
+        if (clock64() - t0 > kWaitCycles)
+            return false;
+    }
+}
+
 template <typename T, int LPR>
-__global__ void __launch_bounds__(kThreads) decode_scores_kernel(const DecodeArgs a)
+__global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const DecodeArgs a)
 {
     constexpr int N = Vec16<T>::N;
+    constexpr int ROW_BYTES = LPR * 16;
+    constexpr int KB = kBlockBytes / ROW_BYTES; // K rows per block
     constexpr int R = LPR < 8 ? LPR : 8;
-    constexpr int RPL = 32 / LPR; // K rows per warp-wide load
-    constexpr int ROWS = R * RPL; // K rows per warp iteration
-    extern __shared__ float logits[];
+    constexpr int RPL = 32 / LPR;               // K rows per warp-wide read
+    constexpr int ROWS = R * RPL;               // K rows per multi_reduce step
+    static_assert(KB % ROWS == 0, "block must hold whole steps");
+    extern __shared__ __align__(128) uint8_t stream_smem[];
+    uint8_t *smem = stream_smem;
+    float *logits = reinterpret_cast<float *>(smem + kNS * kBlockBytes);
+    __shared__ __align__(8) uint64_t full[kNS], empty[kNS];
     __shared__ float2 stats[2];
     __shared__ float scratch[32];
+    __shared__ int abort_flag;
 
     cg::cluster_group cluster = cg::this_cluster();
     const int C = (int)cluster.num_blocks();
-    const int64_t c = cluster.block_rank();
+    const int c = (int)cluster.block_rank();
     const int64_t row = blockIdx.x / C;
     const RowInfo ri = row_info(a, row);
     if (!ri.active)
         return; // the whole cluster shares the row and leaves together
     const int64_t kvh = ri.h / a.group;
-    const int64_t S = a.S;
-    const int64_t j0 = c * a.chunk;
-    const int64_t n_valid = max((int64_t)0, min(j0 + a.chunk, ri.limit + 1) - j0);
-    const int64_t n_write = max((int64_t)0, min(j0 + a.chunk, ri.M) - j0);
+    const int64_t n_keys = max((int64_t)0, ri.limit + 1);
+    const int64_t n_blk = (n_keys + KB - 1) / KB;                 // blocks holding valid keys
+    const int n_mine = n_blk > c ? (int)((n_blk - c + C - 1) / C) : 0;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    if (n_valid > 0)
+    if (tid == 0)
     {
-        const int sub = lane % LPR; // 16-byte slice of the row this lane reads
+        for (int i = 0; i < kNS; ++i)
+        {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[i])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&empty[i])) : "memory");
+        }
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    const char *kbase = static_cast<const char *>(a.k) + (ri.b * a.Hkv + kvh) * a.S * (int64_t)ROW_BYTES;
+    int n_issued = 0; // producer lane only
+    if (warp == kNS)
+    {
+        if (lane == 0)
+        {
+            for (int i = 0; i < n_mine && !abort_flag; ++i)
+            {
+                const int st = i % kNS;
+                if (i >= kNS && !bar_wait(smem_addr(&empty[st]), ((i / kNS) - 1) & 1))
+                {
+                    atomicCAS(&g_scores_error, 0, 0x201);
+                    abort_flag = 1;
+                    break;
+                }
+                const int64_t g = c + (int64_t)C * i;
+                const uint32_t bytes = (uint32_t)(min((int64_t)KB, n_keys - g * KB) * ROW_BYTES);
+                const uint32_t bar = smem_addr(&full[st]);
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                                 smem_addr(smem + st * kBlockBytes)),
+                             "l"(kbase + g * KB * ROW_BYTES), "r"(bytes), "r"(bar)
+                             : "memory");
+                n_issued = i + 1;
+            }
+        }
+    }
+    else
+    {
+        const int sub = lane % LPR;
         const T *qrow = static_cast<const T *>(a.q) + row * a.hd;
         const Vec16<T> qv = as_vec<T>(ldg_keep(qrow + sub * N));
         float qf[N];
 #pragma unroll
         for (int e = 0; e < N; ++e)
             qf[e] = to_f(qv.v[e]);
-        const T *kbase = static_cast<const T *>(a.k) + ((ri.b * a.Hkv + kvh) * S + j0) * a.hd + sub * N;
-        for (int64_t base = (int64_t)warp * ROWS; base < n_valid; base += (int64_t)nwarps * ROWS)
+        const uint8_t *stage = smem + warp * kBlockBytes + sub * 16;
+        for (int i = warp; i < n_mine; i += kNS)
         {
-            float part[R];
-            uint4 raw[R];
-#pragma unroll
-            for (int i = 0; i < R; ++i)
+            if (!bar_wait(smem_addr(&full[warp]), (i / kNS) & 1))
             {
-                const int64_t r = base + i * RPL + lane / LPR;
-                if (r < n_valid)
-                    raw[i] = ldg_stream(kbase + r * a.hd);
-                else
-                    raw[i] = make_uint4(0, 0, 0, 0);
+                atomicCAS(&g_scores_error, 0, 0x202);
+                abort_flag = 1;
+                break;
             }
-#pragma unroll
-            for (int i = 0; i < R; ++i)
+            const int64_t g = c + (int64_t)C * i;
+            const int rows = (int)min((int64_t)KB, n_keys - g * KB);
+#pragma unroll 1
+            for (int base = 0; base < KB; base += ROWS)
             {
-                const Vec16<T> kv = as_vec<T>(raw[i]);
-                float s = 0.f;
+                float part[R];
 #pragma unroll
-                for (int e = 0; e < N; ++e)
-                    s = fmaf(to_f(kv.v[e]), qf[e], s);
-                part[i] = s;
+                for (int j = 0; j < R; ++j)
+                {
+                    const int rr = base + j * RPL + lane / LPR;
+                    float sacc = 0.f;
+                    if (rr < rows)
+                    {
+                        const Vec16<T> kv = as_vec<T>(*reinterpret_cast<const uint4 *>(stage + rr * ROW_BYTES));
+#pragma unroll
+                        for (int e = 0; e < N; ++e)
+                            sacc = fmaf(to_f(kv.v[e]), qf[e], sacc);
+                    }
+                    part[j] = sacc;
+                }
+                int idx;
+                const float dot = multi_reduce<R, LPR>(part, lane, idx);
+                const int rr = base + idx * RPL + lane / LPR;
+                if ((lane & (LPR / R - 1)) == 0)
+                    logits[i * KB + rr] = rr < rows ? __fmul_rn(dot, a.scale) : -INFINITY;
             }
-            int idx;
-            const float dot = multi_reduce<R, LPR>(part, lane, idx);
-            const int64_t r = base + idx * RPL + lane / LPR;
-            if ((lane & (LPR / R - 1)) == 0 && r < n_valid)
-                logits[r] = __fmul_rn(dot, a.scale);
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&empty[warp])) : "memory");
         }
     }
     __syncthreads();
-    T *out_row = static_cast<T *>(a.qk) + row * S;
-    finish_row<T>(cluster, logits, stats, scratch, j0, n_valid, n_write, out_row);
+    if (abort_flag && warp == kNS && lane == 0)
+    {
+        // A wait expired: let this CTA's copies still in flight land before it
+        // leaves (each wait bounded again).
+        for (int i = max(0, n_issued - kNS); i < n_issued; ++i)
+            bar_wait(smem_addr(&full[i % kNS]), (i / kNS) & 1);
+    }
+    __syncthreads();
+
+    // CTA statistics over its logits, cluster-wide combination, normalized store.
+    const int64_t n_log = (int64_t)n_mine * KB;
+    float m = -INFINITY;
+    for (int64_t i = tid; i < n_log; i += blockDim.x)
+        m = fmaxf(m, logits[i]);
+    m = block_max(m, scratch);
+    float l = 0.f;
+    for (int64_t i = tid; i < n_log; i += blockDim.x)
+    {
+        const float x = logits[i];
+        l += x == -INFINITY ? 0.f : expf(__fsub_rn(x, m));
+    }
+    l = block_sum(l, scratch);
+    float M = m, denom = __fadd_rn(l, kSoftmaxEps);
+    if (C > 1)
+    {
+        if (tid == 0)
+            stats[0] = make_float2(m, l);
+        cluster.sync();
+        if (tid < 32)
+        {
+            float2 sp = make_float2(-INFINITY, 0.f);
+            if (tid < C)
+                sp = *cluster.map_shared_rank(stats, tid);
+            const float Mx = warp_max(sp.y > 0.f ? sp.x : -INFINITY);
+            const float L = warp_sum(sp.y > 0.f ? sp.y * expf(__fsub_rn(sp.x, Mx)) : 0.f);
+            if (tid == 0)
+                stats[1] = make_float2(Mx, __fadd_rn(L, kSoftmaxEps));
+        }
+        __syncthreads();
+        M = stats[1].x;
+        denom = stats[1].y;
+    }
+    T *out_row = static_cast<T *>(a.qk) + row * a.S;
+    const int64_t n_wblk = (ri.M + KB - 1) / KB; // blocks with keys < M
+    for (int64_t g = c; g < n_wblk; g += C)
+    {
+        const int64_t i = (g - c) / C;
+        for (int r = tid; r < KB; r += blockDim.x)
+        {
+            const int64_t j = g * KB + r;
+            if (j >= ri.M)
+                break;
+            const float p = (i < n_mine && j < n_keys) ? __fdiv_rn(expf(__fsub_rn(logits[i * KB + r], M)), denom) : 0.f;
+            out_row[j] = from_f<T>(p);
+        }
+    }
+    if (C > 1)
+        cluster.sync(); // peers may still be reading stats[0]
 }
 
 // Any head_dim / alignment: one thread per key, q staged in shared memory.
@@ -256,7 +401,8 @@ __global__ void __launch_bounds__(kThreads) decode_scores_generic_kernel(const D
 }
 
 template <typename K>
-cudaError_t launch_clustered(K kernel, int C, int64_t rows, size_t smem, cudaStream_t stream, const DecodeArgs &a)
+cudaError_t launch_clustered(K kernel, int C, int64_t rows, size_t smem, cudaStream_t stream, const DecodeArgs &a,
+                             int threads)
 {
     if (smem > 48 * 1024)
     {
@@ -272,7 +418,7 @@ cudaError_t launch_clustered(K kernel, int C, int64_t rows, size_t smem, cudaStr
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(rows * C));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -289,36 +435,63 @@ template <typename T>
 int launch_score_rows(DecodeArgs a, int64_t batch, cudaStream_t stream)
 {
     const int64_t rows = batch * a.Hq * a.Qc;
-    // Cluster size: enough CTAs for two waves over the SMs, chunks <= kMaxChunk.
-    int C = rows * 8 >= 2LL * num_sms() ? 8 : 16;
-    C = (int)std::min<int64_t>(C, std::max<int64_t>(1, ceil_div(a.S, 64)));
-    while (ceil_div(a.S, C) > kMaxChunk && C < 16)
-        C *= 2;
-    L2K_REQUIRE_SHAPE(ceil_div(a.S, C) <= kMaxChunk, "l2k_decode_attention_scores: kv_cache_len %lld > %d",
-                      (long long)a.S, 16 * kMaxChunk);
-    a.chunk = ceil_div(a.S, C);
     const int64_t row_bytes = a.hd * (int64_t)sizeof(T);
     const bool vec = row_bytes % 16 == 0 && is_aligned(a.q, 16) && is_aligned(a.k, 16);
     const int lpr = (int)(row_bytes / 16);
+    const bool stream_ok = vec && (lpr == 4 || lpr == 8 || lpr == 16 || lpr == 32);
     cudaError_t e;
-    const size_t smem = (size_t)a.chunk * sizeof(float);
-    if (vec && lpr == 32)
-        e = launch_clustered(decode_scores_kernel<T, 32>, C, rows, smem, stream, a);
-    else if (vec && lpr == 16)
-        e = launch_clustered(decode_scores_kernel<T, 16>, C, rows, smem, stream, a);
-    else if (vec && lpr == 8)
-        e = launch_clustered(decode_scores_kernel<T, 8>, C, rows, smem, stream, a);
-    else if (vec && lpr == 4)
-        e = launch_clustered(decode_scores_kernel<T, 4>, C, rows, smem, stream, a);
+    if (stream_ok)
+    {
+        // Cluster size: enough CTAs for ~3 per SM, at most one block per CTA-rank.
+        const int64_t kb = kBlockBytes / row_bytes;
+        const int64_t blocks_per_row = ceil_div(a.S, kb);
+        int C = 1;
+        while (C < 8 && rows * C < 3LL * num_sms() && C * 2 <= blocks_per_row)
+            C *= 2;
+        const int64_t logit_bytes = ceil_div(blocks_per_row, C) * kb * (int64_t)sizeof(float);
+        L2K_REQUIRE_SHAPE(logit_bytes <= 128 * 1024, "score rows: kv_cache_len %lld too long", (long long)a.S);
+        const size_t smem = (size_t)kNS * kBlockBytes + (size_t)logit_bytes;
+        if (lpr == 32)
+            e = launch_clustered(score_rows_stream_kernel<T, 32>, C, rows, smem, stream, a, kStreamThreads);
+        else if (lpr == 16)
+            e = launch_clustered(score_rows_stream_kernel<T, 16>, C, rows, smem, stream, a, kStreamThreads);
+        else if (lpr == 8)
+            e = launch_clustered(score_rows_stream_kernel<T, 8>, C, rows, smem, stream, a, kStreamThreads);
+        else
+            e = launch_clustered(score_rows_stream_kernel<T, 4>, C, rows, smem, stream, a, kStreamThreads);
+    }
     else
-        e = launch_clustered(decode_scores_generic_kernel<T>, C, rows, smem + (size_t)a.hd * sizeof(float), stream,
-                             a);
+    {
+        int C = rows * 8 >= 2LL * num_sms() ? 8 : 16;
+        C = (int)std::min<int64_t>(C, std::max<int64_t>(1, ceil_div(a.S, 64)));
+        while (ceil_div(a.S, C) > kMaxChunk && C < 16)
+            C *= 2;
+        L2K_REQUIRE_SHAPE(ceil_div(a.S, C) <= kMaxChunk, "score rows: kv_cache_len %lld > %d", (long long)a.S,
+                          16 * kMaxChunk);
+        a.chunk = ceil_div(a.S, C);
+        const size_t smem = (size_t)a.chunk * sizeof(float) + (size_t)a.hd * sizeof(float);
+        e = launch_clustered(decode_scores_generic_kernel<T>, C, rows, smem, stream, a, kThreads);
+    }
     if (e != cudaSuccess)
-        return set_error(L2K_ERR_CUDA, "l2k_decode_attention_scores: %s", cudaGetErrorString(e));
-    return check_launch("l2k_decode_attention_scores");
+        return set_error(L2K_ERR_CUDA, "attention score rows: %s", cudaGetErrorString(e));
+    return check_launch("attention score rows");
 }
 
 } // namespace
+
+int read_scores_error(bool clear)
+{
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_scores_error, sizeof(int)) != cudaSuccess)
+        return -1;
+    if (clear && v)
+    {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(g_scores_error, &zero, sizeof(int)) != cudaSuccess)
+            return -1;
+    }
+    return v;
+}
 
 // Prefill score rows through the same cluster kernel (one cluster per query
 // row): logits stay fp32 until the final store. Used by scores.cu for the

@@ -1,7 +1,9 @@
 // Fused prefill attention scores entry point.
 //
-// Dispatch: BF16/F16 run the cluster score-row kernel (decode_scores.cu) with
-// one cluster per query row, fp32 logits until the final store. F32 runs
+// Dispatch: BF16/F16 with head_dim 128 run the tcgen05 kernel
+// (prefill_scores_tc.cu). Other BF16/F16 shapes run the cluster score-row
+// kernel (decode_scores.cu) with one cluster per query row, fp32 logits until
+// the final store. F32 runs
 // QK^T on the CUDA cores (gemm.cu) followed by the causal masked softmax
 // (masked_softmax.cu): two kernels, the fp32 scores round-trip through HBM.
 #include "common.cuh"
@@ -17,6 +19,11 @@ int masked_softmax_causal(void *qk, const uint32_t *q_lens, const uint32_t *kv_l
 int prefill_score_rows(const void *q, const void *k, const uint32_t *q_lens, const uint32_t *kv_lens,
                        uint32_t max_kv, void *qk, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc, int64_t S,
                        int64_t hd, int dtype, cudaStream_t stream);
+bool prefill_tc_supported(int dtype, int64_t head_dim, int64_t S, int64_t Qc, const void *q, const void *k,
+                          const void *qk, int64_t grid);
+int prefill_scores_tc(const void *q, const void *k, const uint32_t *q_lens, const uint32_t *kv_lens, uint32_t max_q,
+                      uint32_t max_kv, void *qk, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc, int64_t S,
+                      int dtype, cudaStream_t stream);
 } // namespace l2k
 
 extern "C" int l2k_prefill_attention_scores(const void *q, const void *k, const uint32_t *q_lens,
@@ -38,6 +45,10 @@ extern "C" int l2k_prefill_attention_scores(const void *q, const void *k, const 
                 "l2k_prefill_attention_scores: q_head_num must be a multiple of kv_head_num");
     L2K_REQUIRE(q && k && q_lens && kv_lens && qk, "l2k_prefill_attention_scores: null pointer");
     L2K_REQUIRE_SHAPE(batch <= 65535 && q_head_num <= 65535, "l2k_prefill_attention_scores: grid too large");
+    const int64_t tc_grid = ceil_div(max_q_len, 128) * batch * q_head_num;
+    if (prefill_tc_supported(dtype, head_dim, kv_cache_len, q_cache_len, q, k, qk, tc_grid))
+        return prefill_scores_tc(q, k, q_lens, kv_lens, max_q_len, max_kv_len, qk, batch, q_head_num, kv_head_num,
+                                 q_cache_len, kv_cache_len, dtype, stream);
     if (dtype != L2K_F32)
     {
         // 16-bit storage: keep the logits in fp32 until the final store (a QK^T
