@@ -153,9 +153,10 @@ __device__ __forceinline__ void finish_row(cg::cluster_group &cluster, const flo
 // rows from shared memory per step and folds the R partial dot products with
 // multi_reduce. Logits stay in shared memory for the cluster softmax.
 // ---------------------------------------------------------------------------
-constexpr int kNS = 4;                 // ring stages == consumer warps
+constexpr int kNS = 4;                 // ring stages
+constexpr int kCW = 8;                 // consumer warps (two per stage, one half-block each)
 constexpr int kBlockBytes = 16384;     // one key block
-constexpr int kStreamThreads = 32 * (kNS + 1);
+constexpr int kStreamThreads = 32 * (kCW + 1);
 constexpr long long kWaitCycles = 4000000000LL; // ~2 s
 
 __device__ int g_scores_error = 0;     // first timeout code of this file's kernels
@@ -187,10 +188,11 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
     constexpr int N = Vec16<T>::N;
     constexpr int ROW_BYTES = LPR * 16;
     constexpr int KB = kBlockBytes / ROW_BYTES; // K rows per block
+    constexpr int HALF = KB / 2;                // rows per consumer warp per block
     constexpr int R = LPR < 8 ? LPR : 8;
     constexpr int RPL = 32 / LPR;               // K rows per warp-wide read
     constexpr int ROWS = R * RPL;               // K rows per multi_reduce step
-    static_assert(KB % ROWS == 0, "block must hold whole steps");
+    static_assert(HALF % ROWS == 0, "half block must hold whole steps");
     extern __shared__ __align__(128) uint8_t stream_smem[];
     uint8_t *smem = stream_smem;
     float *logits = reinterpret_cast<float *>(smem + kNS * kBlockBytes);
@@ -217,7 +219,8 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
         for (int i = 0; i < kNS; ++i)
         {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&full[i])) : "memory");
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&empty[i])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(&empty[i])), "r"(kCW / kNS)
+                         : "memory");
         }
         abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -226,7 +229,7 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
 
     const char *kbase = static_cast<const char *>(a.k) + (ri.b * a.Hkv + kvh) * a.S * (int64_t)ROW_BYTES;
     int n_issued = 0; // producer lane only
-    if (warp == kNS)
+    if (warp == kCW)
     {
         if (lane == 0)
         {
@@ -239,8 +242,10 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
                     abort_flag = 1;
                     break;
                 }
+                // Whole blocks (up to the cache end): rows past kv_len are computed and masked,
+                // which keeps the consumers' inner loop free of bounds checks.
                 const int64_t g = c + (int64_t)C * i;
-                const uint32_t bytes = (uint32_t)(min((int64_t)KB, n_keys - g * KB) * ROW_BYTES);
+                const uint32_t bytes = (uint32_t)(min((int64_t)KB, a.S - g * KB) * ROW_BYTES);
                 const uint32_t bar = smem_addr(&full[st]);
                 asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
                 asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -253,6 +258,7 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
     }
     else
     {
+        const int st = warp % kNS, hf = warp / kNS; // ring stage, half of the block
         const int sub = lane % LPR;
         const T *qrow = static_cast<const T *>(a.q) + row * a.hd;
         const Vec16<T> qv = as_vec<T>(ldg_keep(qrow + sub * N));
@@ -260,70 +266,70 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
 #pragma unroll
         for (int e = 0; e < N; ++e)
             qf[e] = to_f(qv.v[e]);
-        const uint8_t *stage = smem + warp * kBlockBytes + sub * 16;
-        for (int i = warp; i < n_mine; i += kNS)
+        const uint8_t *stage = smem + st * kBlockBytes + (hf * HALF + lane / LPR) * ROW_BYTES + sub * 16;
+        for (int i = st; i < n_mine; i += kNS)
         {
-            if (!bar_wait(smem_addr(&full[warp]), (i / kNS) & 1))
+            if (!bar_wait(smem_addr(&full[st]), (i / kNS) & 1))
             {
                 atomicCAS(&g_scores_error, 0, 0x202);
                 abort_flag = 1;
                 break;
             }
             const int64_t g = c + (int64_t)C * i;
-            const int rows = (int)min((int64_t)KB, n_keys - g * KB);
-#pragma unroll 1
-            for (int base = 0; base < KB; base += ROWS)
+            const int64_t valid = n_keys - g * KB - hf * HALF; // rows of this half below kv_len
+#pragma unroll
+            for (int base = 0; base < HALF; base += ROWS)
             {
                 float part[R];
 #pragma unroll
                 for (int j = 0; j < R; ++j)
                 {
-                    const int rr = base + j * RPL + lane / LPR;
+                    const Vec16<T> kv =
+                        as_vec<T>(*reinterpret_cast<const uint4 *>(stage + (base + j * RPL) * ROW_BYTES));
                     float sacc = 0.f;
-                    if (rr < rows)
-                    {
-                        const Vec16<T> kv = as_vec<T>(*reinterpret_cast<const uint4 *>(stage + rr * ROW_BYTES));
 #pragma unroll
-                        for (int e = 0; e < N; ++e)
-                            sacc = fmaf(to_f(kv.v[e]), qf[e], sacc);
-                    }
+                    for (int e = 0; e < N; ++e)
+                        sacc = fmaf(to_f(kv.v[e]), qf[e], sacc);
                     part[j] = sacc;
                 }
                 int idx;
                 const float dot = multi_reduce<R, LPR>(part, lane, idx);
                 const int rr = base + idx * RPL + lane / LPR;
                 if ((lane & (LPR / R - 1)) == 0)
-                    logits[i * KB + rr] = rr < rows ? __fmul_rn(dot, a.scale) : -INFINITY;
+                    logits[i * KB + hf * HALF + rr] = rr < valid ? __fmul_rn(dot, a.scale) : -INFINITY;
             }
             __syncwarp();
             if (lane == 0)
-                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&empty[warp])) : "memory");
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&empty[st])) : "memory");
         }
     }
     __syncthreads();
-    if (abort_flag && warp == kNS && lane == 0)
+    if (abort_flag && warp == kCW && lane == 0)
     {
         // A wait expired: let this CTA's copies still in flight land before it
         // leaves (each wait bounded again).
         for (int i = max(0, n_issued - kNS); i < n_issued; ++i)
             bar_wait(smem_addr(&full[i % kNS]), (i / kNS) & 1);
     }
-    __syncthreads();
 
-    // CTA statistics over its logits, cluster-wide combination, normalized store.
+    // CTA statistics over its logits (one expf per logit, kept in place),
+    // cluster-wide combination, normalized store.
     const int64_t n_log = (int64_t)n_mine * KB;
     float m = -INFINITY;
     for (int64_t i = tid; i < n_log; i += blockDim.x)
         m = fmaxf(m, logits[i]);
-    m = block_max(m, scratch);
+    m = block_max(m, scratch); // (its barriers also order the abort drain above)
     float l = 0.f;
     for (int64_t i = tid; i < n_log; i += blockDim.x)
     {
         const float x = logits[i];
-        l += x == -INFINITY ? 0.f : expf(__fsub_rn(x, m));
+        const float e = x == -INFINITY ? 0.f : expf(__fsub_rn(x, m));
+        logits[i] = e;
+        l += e;
     }
     l = block_sum(l, scratch);
-    float M = m, denom = __fadd_rn(l, kSoftmaxEps);
+    // p = e * exp(m - M) / (L + eps), M, L over the whole row
+    float factor = 1.f, denom = __fadd_rn(l, kSoftmaxEps);
     if (C > 1)
     {
         if (tid == 0)
@@ -340,9 +346,10 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
                 stats[1] = make_float2(Mx, __fadd_rn(L, kSoftmaxEps));
         }
         __syncthreads();
-        M = stats[1].x;
         denom = stats[1].y;
+        factor = l > 0.f ? expf(__fsub_rn(m, stats[1].x)) : 0.f;
     }
+    const float scale_out = __fdiv_rn(factor, denom);
     T *out_row = static_cast<T *>(a.qk) + row * a.S;
     const int64_t n_wblk = (ri.M + KB - 1) / KB; // blocks with keys < M
     for (int64_t g = c; g < n_wblk; g += C)
@@ -353,7 +360,7 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
             const int64_t j = g * KB + r;
             if (j >= ri.M)
                 break;
-            const float p = (i < n_mine && j < n_keys) ? __fdiv_rn(expf(__fsub_rn(logits[i * KB + r], M)), denom) : 0.f;
+            const float p = (i < n_mine && j < n_keys) ? __fmul_rn(logits[i * KB + r], scale_out) : 0.f;
             out_row[j] = from_f<T>(p);
         }
     }

@@ -1,24 +1,29 @@
 // Fused prefill attention scores on the 5th-generation tensor cores:
 //   P = softmax_causal(Q K^T / sqrt(128)),  bf16/f16 in, fp32 accumulate, bf16/f16 out.
 //
-// One CTA owns 128 query rows of one (seq, head). Key tiles are 128 wide.
-//   * TMA (cp.async.bulk.tensor, 128-byte swizzle) stages the Q tile once and
-//     K tiles through a 2-deep ring; one thread issues tcgen05.mma
-//     (M=128, N=128, K=16 x 8) with both operands in shared memory and the
-//     fp32 accumulator in tensor memory (2 x 128 columns, double buffered),
-//     and tcgen05.commit signals an mbarrier when a tile is done.
-//   * Phase A walks the causally visible key tiles and keeps an online row
-//     max / sum of exponentials (in log2 units) per row; phase B recomputes
-//     each tile and writes P = 2^(s*c - m) / (sum + 1e-6) once, through a
-//     shared-memory staging buffer and TMA stores. The MMA of tile t+1 and the
-//     TMA load of tile t+2 run while the 8 warps work on tile t.
-//   * Key tiles beyond the causal limit are written as zeros by TMA stores
-//     from a zeroed shared buffer, issued at the start so they overlap the
-//     math. Columns >= max_kv are clipped by the store tensor map.
-//   * Tiles whose rows straddle q_len store rows < q_len directly.
+// One CTA owns 128 query rows of one (seq, head); key tiles are 64 wide.
+// Warp roles (288 threads, two CTAs per SM):
+//   * warp 8 (control): TMA (cp.async.bulk.tensor, 128-byte swizzle) of the
+//     Q tile once and of K tiles through a 2-stage ring; tcgen05.mma
+//     (M=128, N=64, K=16 x 8) with both operands in shared memory and the
+//     fp32 accumulator in tensor memory (2 x 64 columns, double buffered);
+//     tcgen05.commit signals "tile ready" on an mbarrier.
+//   * warps 0-7 (epilogue): warp w reads TMEM lanes 32*(w%4).. (its rows) and
+//     columns 32*(w/4).. of each tile with tcgen05.ld.
+//     Phase A walks the causally visible key tiles keeping an online row max
+//     and sum of exponentials (log2 units, ex2); phase B re-runs the MMAs
+//     and writes P = 2^(s*c - m) / (sum + 1e-6) once, through a swizzled
+//     shared staging buffer and TMA stores. Each finished tile frees its TMEM
+//     buffer through an mbarrier, so the MMA of the next tile overlaps.
+//   * Key tiles beyond the causal limit are TMA-stored from a zeroed staging
+//     buffer at the start (overlapping phase A). Keys >= max_kv are never
+//     written (the store map's extent; its 16-byte-rounded tail is written
+//     directly); tiles whose rows straddle q_len are written directly.
+// CTA order is (seq, head)-major so the query tiles of one head run together
+// and share its K tiles in L2.
 // Every mbarrier wait is bounded (~2 s of clock cycles); on expiry the kernel
-// records an error code in l2k_device_error and leaves after draining its
-// own copies, so a defect shows up as an error, not a hung GPU.
+// records an error code (l2k_device_error) and leaves after draining its own
+// copies, so a defect shows up as an error, not a hung GPU.
 //
 // Reference composition: cuBLAS QK^T (src/kernel/linear.cu:96-128) + masked
 // softmax (src/kernel/compute_masked_attention_score.cu:12-103) with the mask
@@ -36,30 +41,34 @@
 namespace l2k
 {
 
-__device__ int g_device_error = 0; // first error code recorded by a kernel
+__device__ int g_device_error = 0; // first error code recorded by a kernel of this file
 
 namespace
 {
 
-constexpr int BM = 128, BN = 128, HD = 128, KH = 64; // KH: elements per 128-byte swizzle row
-constexpr int kThreads = 256;
-constexpr uint32_t kHalfTile = 128 * 128;            // bytes of a 128-row x 64-col bf16 box
-constexpr uint32_t kOffQ = 0;                         // 2 halves
-constexpr uint32_t kOffK = kOffQ + 2 * kHalfTile;     // 2 stages x 2 halves
-constexpr uint32_t kOffP = kOffK + 4 * kHalfTile;     // 2 buffers x 2 halves
-constexpr uint32_t kOffZ = kOffP + 4 * kHalfTile;     // 1 zero box
-constexpr uint32_t kOffBar = kOffZ + kHalfTile;       // mbarriers
-constexpr uint32_t kOffMisc = kOffBar + 64;           // tmem slot, abort flag
-constexpr uint32_t kOffStats = kOffMisc + 64;         // 2 x 128 float2
+constexpr int BM = 128, BN = 64, HD = 128, KH = 64; // KH: elements per 128-byte swizzle row
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (kEpiWarps + 1);
+constexpr int kCtl = kEpiWarps;                        // control warp index
+constexpr uint32_t kQBox = 128 * 128;                  // 128 rows x 128 B
+constexpr uint32_t kKBox = 64 * 128;                   // 64 rows x 128 B
+constexpr uint32_t kOffQ = 0;                          // 2 boxes (hd halves)
+constexpr uint32_t kOffK = kOffQ + 2 * kQBox;          // 2 stages x 2 boxes
+constexpr uint32_t kOffP = kOffK + 4 * kKBox;          // 2 staging buffers of one 128x64 box
+constexpr uint32_t kOffBar = kOffP + 2 * kQBox;        // mbarriers
+constexpr uint32_t kOffMisc = kOffBar + 128;           // tmem slot, abort flag
+constexpr uint32_t kOffStats = kOffMisc + 64;          // 2 x 128 float2
 constexpr uint32_t kSmemBytes = kOffStats + 2 * 128 * 8 + 1024; // + alignment slack
-constexpr long long kWaitCycles = 4000000000LL;       // ~2 s at 2 GHz
+constexpr uint32_t kTmemCols = 2 * BN;
+constexpr long long kWaitCycles = 4000000000LL;        // ~2 s at 2 GHz
 constexpr float kNegBig = -1e30f;
 
 enum DevError
 {
     ERR_WAIT_Q = 0x101,
     ERR_WAIT_K = 0x102,
-    ERR_WAIT_MMA = 0x103
+    ERR_WAIT_MMA = 0x103,
+    ERR_WAIT_TMEM = 0x104
 };
 
 struct TcArgs
@@ -69,7 +78,7 @@ struct TcArgs
     void *qk;
     int64_t Hq, group, Hkv, Qc, S;
     int64_t M;     // keys written per row: min(max_kv, S)
-    int64_t M8;    // keys written by TMA stores: M rounded down to 8 (16 bytes); the rest directly
+    int64_t M8;    // keys written by TMA stores: M rounded down to 8 (16 bytes)
     int n_qt;      // query tiles per (seq, head)
     int n_kt;      // key tiles covering [0, M)
     float c;       // scale * log2(e)
@@ -88,8 +97,15 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
 {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// Bounded wait on phase `parity`; false when the time limit expired.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity)
+__device__ __forceinline__ void mbar_arrive(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Bounded wait on phase `parity`; false when the time limit expired or when
+// another thread of the CTA has already given up (abort), so that after a
+// failure every warp runs through its remaining steps quickly and still meets
+// every barrier it shares with the others.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const volatile int *abort_flag)
 {
     const long long t0 = clock64();
     while (true)
@@ -103,7 +119,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity)
                      : "memory");
         if (done)
             return true;
-        if (clock64() - t0 > kWaitCycles)
+        if (*abort_flag || clock64() - t0 > kWaitCycles)
             return false;
     }
 }
@@ -122,8 +138,11 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t sr
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Named barrier among the epilogue warps only.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kEpiWarps) : "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -135,7 +154,7 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr)
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// kind::f16 instruction descriptor: D f32, A/B bf16 (1) or f16 (0), both K-major, M=128, N=128.
+// kind::f16 instruction descriptor: D f32, A/B bf16 (1) or f16 (0), both K-major, M=128, N=BN.
 __host__ __device__ constexpr uint32_t instr_desc(uint32_t ab_format)
 {
     return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -194,11 +213,19 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b)
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+__device__ __forceinline__ uint16_t half_of(uint32_t w, int hi) { return (uint16_t)(hi ? (w >> 16) : (w & 0xFFFF)); }
+
+__device__ __forceinline__ void fail(int code, volatile int *abort_flag)
+{
+    atomicCAS(&g_device_error, 0, code);
+    *abort_flag = 1;
+}
+
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     prefill_scores_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_p, const TcArgs a)
 {
@@ -206,15 +233,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar_q = sbase + kOffBar;
-    const uint32_t bar_k0 = bar_q + 8;        // + 8 * stage
-    const uint32_t bar_m0 = bar_q + 24;       // + 8 * buffer
+    const uint32_t bar_kfull = bar_q + 8;    // + 8 * stage
+    const uint32_t bar_mma = bar_q + 24;     // + 8 * buffer: tile in TMEM buffer is ready
+    const uint32_t bar_tfree = bar_q + 40;   // + 8 * buffer: epilogue finished with TMEM buffer
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffMisc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kOffMisc + 8);
     float2 *stats = reinterpret_cast<float2 *>(smem + kOffStats); // [2][128]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // (seq, head)-major order: the query tiles of one head run at about the
-    // same time and share its K tiles in L2; within a head, heaviest first.
     const int64_t bh = blockIdx.x / a.n_qt;
     const int qt = a.n_qt - 1 - (int)(blockIdx.x % a.n_qt);
     const int64_t b = bh / a.Hq, h = bh - b * a.Hq;
@@ -226,8 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (row0 >= q_len)
         return; // no output rows in this tile (uniform over the CTA)
     const int rows_valid = (int)min((int64_t)BM, q_len - row0);
-    // TMA stores need whole 128-row tiles; their tensor map covers keys [0, M8)
-    // (TMA clips a store at 16-byte granularity), keys [M8, M) are stored directly.
+    // TMA stores need whole 128-row tiles; their map covers keys [0, M8).
     const bool full_rows = rows_valid == BM && a.M8 > 0;
     const int64_t max_lim = min(kv_len - 1, hist + row0 + rows_valid - 1);
     const int64_t min_lim = min(kv_len - 1, hist + row0);
@@ -240,21 +265,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(bar_q, 1);
         for (int i = 0; i < 2; ++i)
         {
-            mbar_init(bar_k0 + 8 * i, 1);
-            mbar_init(bar_m0 + 8 * i, 1);
+            mbar_init(bar_kfull + 8 * i, 1);
+            mbar_init(bar_mma + 8 * i, 1);
+            mbar_init(bar_tfree + 8 * i, kEpiWarps);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0)
+    if (warp == kCtl)
     {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(256));
+                     "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     {
-        uint4 *z = reinterpret_cast<uint4 *>(smem + kOffZ);
-        for (int i = tid; i < (int)(kHalfTile / 16); i += kThreads)
+        // staging buffer 0 starts as the zero tile
+        uint4 *z = reinterpret_cast<uint4 *>(smem + kOffP);
+        for (int i = tid; i < (int)(kQBox / 16); i += kThreads)
             z[i] = make_uint4(0, 0, 0, 0);
     }
     fence_proxy_async();
@@ -263,244 +290,224 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // Zero tiles beyond the causal limit (full-row tiles only; others store directly).
-    if (tid == 0 && full_rows)
+    if (warp == kCtl)
     {
-        for (int kt = n_a; kt < a.n_kt; ++kt)
-            for (int ch = 0; ch < 2; ++ch)
-                tma_store_3d(&tm_p, sbase + kOffZ, kt * BN + ch * KH, (int)row0, (int)bh);
-        bulk_commit();
-    }
-
-    const uint32_t idesc = instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u);
-    auto issue_k = [&](int t) { // TMA of the key tile of pipeline step t into stage t % 2
-        const int kt = t % n_a, st = t & 1;
-        const uint32_t dst = sbase + kOffK + st * 2 * kHalfTile;
-        mbar_expect_tx(bar_k0 + 8 * st, 2 * kHalfTile);
-        for (int ch = 0; ch < 2; ++ch)
-            tma_load_3d(dst + ch * kHalfTile, &tm_k, ch * KH, kt * BN, (int)(b * a.Hkv + kvh), bar_k0 + 8 * st);
-    };
-    auto issue_mma = [&](int t) { // tile t into TMEM buffer t % 2
-        const int st = t & 1;
-        const uint32_t kbase = sbase + kOffK + st * 2 * kHalfTile;
-        const uint32_t d = tmem + (uint32_t)(st * BN);
-#pragma unroll
-        for (int k = 0; k < HD / 16; ++k)
+        // ================= control warp =================
+        if (lane == 0 && n_steps > 0)
         {
-            const uint32_t off = (uint32_t)((k & 3) * 32) + (uint32_t)(k >> 2) * kHalfTile;
-            mma_f16(d, smem_desc(sbase + kOffQ + off), smem_desc(kbase + off), idesc, k > 0 ? 1u : 0u);
-        }
-        mma_commit(bar_m0 + 8 * st);
-    };
-
-    bool ok = true;
-    if (tid == 0 && n_steps > 0)
-    {
-        mbar_expect_tx(bar_q, 2 * kHalfTile);
-        for (int ch = 0; ch < 2; ++ch)
-            tma_load_3d(sbase + kOffQ + ch * kHalfTile, &tm_q, ch * KH, (int)row0, (int)bh, bar_q);
-        issue_k(0);
-        if (n_steps > 1)
-            issue_k(1);
-        if (!mbar_wait(bar_q, 0) || !mbar_wait(bar_k0, 0))
-        {
-            atomicCAS(&g_device_error, 0, ERR_WAIT_Q);
-            *abort_flag = 1;
-            ok = false;
-        }
-        else
-            issue_mma(0);
-    }
-    __syncthreads();
-
-    // -------- per-thread row state --------
-    const int quad = warp & 3, ch = warp >> 2; // TMEM lanes 32*quad.., columns 64*ch..
-    const int r = quad * 32 + lane;            // row within the tile
-    const int64_t lim_r = min(kv_len - 1, hist + row0 + r);
-    float m = kNegBig, l = 0.f;                // log2-domain running max / sum
-    float inv = 0.f;
-
-    for (int t = 0; t < n_steps && !*abort_flag; ++t)
-    {
-        const int st = t & 1;
-        if (tid == 0 && ok && t + 1 < n_steps)
-        {
-            if (!mbar_wait(bar_k0 + 8 * ((t + 1) & 1), ((t + 1) >> 1) & 1))
+            const uint32_t idesc = instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u);
+            const int kz = (int)(b * a.Hkv + kvh);
+            auto issue_k = [&](int t) {
+                const int kt = t % n_a, st = t & 1;
+                const uint32_t dst = sbase + kOffK + st * 2 * kKBox;
+                mbar_expect_tx(bar_kfull + 8 * st, 2 * kKBox);
+                for (int hf = 0; hf < 2; ++hf)
+                    tma_load_3d(dst + hf * kKBox, &tm_k, hf * KH, kt * BN, kz, bar_kfull + 8 * st);
+            };
+            mbar_expect_tx(bar_q, 2 * kQBox);
+            for (int hf = 0; hf < 2; ++hf)
+                tma_load_3d(sbase + kOffQ + hf * kQBox, &tm_q, hf * KH, (int)row0, (int)bh, bar_q);
+            issue_k(0);
+            if (n_steps > 1)
+                issue_k(1);
+            if (!mbar_wait(bar_q, 0, abort_flag))
+                fail(ERR_WAIT_Q, abort_flag);
+            for (int t = 0; t < n_steps && !*abort_flag; ++t)
             {
-                atomicCAS(&g_device_error, 0, ERR_WAIT_K);
-                *abort_flag = 1;
-                ok = false;
-            }
-            else
-            {
+                const int st = t & 1;
+                if (!mbar_wait(bar_kfull + 8 * st, (t >> 1) & 1, abort_flag))
+                {
+                    fail(ERR_WAIT_K, abort_flag);
+                    break;
+                }
+                if (t >= 2 && !mbar_wait(bar_tfree + 8 * st, ((t >> 1) - 1) & 1, abort_flag))
+                {
+                    fail(ERR_WAIT_TMEM, abort_flag);
+                    break;
+                }
                 tc_fence_after();
-                issue_mma(t + 1);
+                const uint32_t kb = sbase + kOffK + st * 2 * kKBox;
+                const uint32_t d = tmem + (uint32_t)(st * BN);
+#pragma unroll
+                for (int k = 0; k < HD / 16; ++k)
+                {
+                    const uint32_t offa = (uint32_t)((k & 3) * 32) + (uint32_t)(k >> 2) * kQBox;
+                    const uint32_t offb = (uint32_t)((k & 3) * 32) + (uint32_t)(k >> 2) * kKBox;
+                    mma_f16(d, smem_desc(sbase + kOffQ + offa), smem_desc(kb + offb), idesc, k > 0 ? 1u : 0u);
+                }
+                mma_commit(bar_mma + 8 * st);
+                if (t + 2 < n_steps)
+                {
+                    // the K stage is free once this tile's MMAs have read it
+                    if (!mbar_wait(bar_mma + 8 * st, (t >> 1) & 1, abort_flag))
+                    {
+                        fail(ERR_WAIT_MMA, abort_flag);
+                        break;
+                    }
+                    issue_k(t + 2);
+                }
             }
         }
-        if (!mbar_wait(bar_m0 + 8 * st, (t >> 1) & 1))
-        {
-            atomicCAS(&g_device_error, 0, ERR_WAIT_MMA);
-            *abort_flag = 1;
-        }
-        tc_fence_after();
-        if (tid == 0 && ok && t + 2 < n_steps)
-            issue_k(t + 2);
+    }
+    else
+    {
+        // ================= epilogue warps =================
+        const int quad = warp & 3, ch = warp >> 2; // TMEM lanes 32*quad.., columns 32*ch..
+        const int r = quad * 32 + lane;            // row within the tile
+        const int64_t lim_r = min(kv_len - 1, hist + row0 + r);
+        float m = kNegBig, l = 0.f, inv = 0.f;     // log2-domain running max / sum
+        uint16_t *qk16 = static_cast<uint16_t *>(a.qk);
+        const int64_t row_off = (bh * a.Qc + row0 + r) * a.S;
 
-        const bool phase_b = t >= n_a;
-        const int kt = phase_b ? t - n_a : t;
-        const int64_t key0 = (int64_t)kt * BN + ch * KH;
-        const bool masked = (int64_t)kt * BN + BN - 1 > min_lim;
-        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(st * BN + ch * KH);
-        if (!phase_b)
+        if (tid == 0 && full_rows)
         {
-            float tmax = -INFINITY;
-            float v[2][32];
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh)
-            {
-                tmem_ld32(taddr + hh * 32, v[hh]);
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                {
-                    const bool keep = !masked || key0 + hh * 32 + j <= lim_r;
-                    v[hh][j] = keep ? v[hh][j] : -INFINITY;
-                    tmax = fmaxf(tmax, v[hh][j]);
-                }
-            }
-            const float m_new = fmaxf(m, tmax * a.c);
-            float sum = 0.f;
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    sum += ex2(fmaf(v[hh][j], a.c, -m_new));
-            l = l * ex2(m - m_new) + sum;
-            m = m_new;
-            if (t == n_a - 1)
-                stats[ch * 128 + r] = make_float2(m, l);
+            // zero key tiles beyond the causal limit, from staging buffer 0
+            for (int kt = n_a; kt < a.n_kt; ++kt)
+                tma_store_3d(&tm_p, sbase + kOffP, kt * BN, (int)row0, (int)bh);
+            bulk_commit();
         }
-        else
+
+        for (int t = 0; t < n_steps; ++t)
         {
-            if (t == n_a)
+            const int st = t & 1;
+            // After a failure the remaining steps run on whatever TMEM holds (the
+            // error is recorded); no warp leaves early, so the named barriers below
+            // are met by all epilogue warps.
+            if (!mbar_wait(bar_mma + 8 * st, (t >> 1) & 1, abort_flag))
+                fail(ERR_WAIT_MMA, abort_flag);
+            tc_fence_after();
+            const bool phase_b = t >= n_a;
+            const int kt = phase_b ? t - n_a : t;
+            const int64_t key0 = (int64_t)kt * BN + ch * 32;
+            const bool masked = (int64_t)kt * BN + BN - 1 > min_lim;
+            float v[32];
+            tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(st * BN + ch * 32), v);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(bar_tfree + 8 * st); // the TMEM buffer may take the next tile
+            if (masked)
             {
-                // combine the two column halves' statistics of this row
-                const float2 s0 = stats[r], s1 = stats[128 + r];
-                const float M = fmaxf(s0.x, s1.x);
-                const float L = s0.y * ex2(s0.x - M) + s1.y * ex2(s1.x - M);
-                m = M;
-                inv = __frcp_rn(__fadd_rn(L, 1e-6f));
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    v[j] = key0 + j <= lim_r ? v[j] : -INFINITY;
             }
-            uint32_t packed[32];
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh)
+            if (!phase_b)
             {
-                float v[32];
-                tmem_ld32(taddr + hh * 32, v);
+                float tmax = -INFINITY;
 #pragma unroll
-                for (int j = 0; j < 32; j += 2)
+                for (int j = 0; j < 32; ++j)
+                    tmax = fmaxf(tmax, v[j]);
+                const float m_new = fmaxf(m, tmax * a.c);
+                float sum = 0.f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    sum += ex2(fmaf(v[j], a.c, -m_new));
+                l = l * ex2(m - m_new) + sum;
+                m = m_new;
+                if (t == n_a - 1)
                 {
-                    const bool k0 = !masked || key0 + hh * 32 + j <= lim_r;
-                    const bool k1 = !masked || key0 + hh * 32 + j + 1 <= lim_r;
-                    const float p0 = k0 ? ex2(fmaf(v[j], a.c, -m)) * inv : 0.f;
-                    const float p1 = k1 ? ex2(fmaf(v[j + 1], a.c, -m)) * inv : 0.f;
-                    packed[hh * 16 + j / 2] = pack2<T>(p0, p1);
+                    stats[ch * 128 + r] = make_float2(m, l);
+                    if (tid == 0)
+                        bulk_wait_read_0(); // the zero-tile stores are done with staging buffer 0
+                    epi_sync();
+                    const float2 s0 = stats[r], s1 = stats[128 + r];
+                    const float Mx = fmaxf(s0.x, s1.x);
+                    const float L = s0.y * ex2(s0.x - Mx) + s1.y * ex2(s1.x - Mx);
+                    m = Mx;
+                    inv = __frcp_rn(__fadd_rn(L, 1e-6f));
                 }
+                continue;
             }
+            uint32_t packed[16];
+#pragma unroll
+            for (int j = 0; j < 32; j += 2)
+                packed[j / 2] = pack2<T>(ex2(fmaf(v[j], a.c, -m)) * inv, ex2(fmaf(v[j + 1], a.c, -m)) * inv);
             if (full_rows)
             {
-                // 128-byte swizzled staging row: 16-byte chunk c at (c ^ (r % 8))
-                uint8_t *dst = smem + kOffP + (uint32_t)(st * 2 + ch) * kHalfTile + (uint32_t)r * 128;
+                // 128-byte swizzled staging row: 16-byte chunk c at (c ^ (r % 8)); this
+                // warp fills chunks 4*ch .. 4*ch+3 of row r.
+                const int sb = (t - n_a) & 1;
+                uint8_t *dst = smem + kOffP + (uint32_t)sb * kQBox + (uint32_t)r * 128;
 #pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) * 16)) =
-                        make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-                fence_proxy_async();
-                if (key0 + KH > a.M8 && key0 < a.M)
+                for (int c4 = 0; c4 < 4; ++c4)
                 {
-                    // keys [M8, M) are beyond the store map: write them directly
-                    uint16_t *out = reinterpret_cast<uint16_t *>(static_cast<T *>(a.qk) +
-                                                                 ((bh * a.Qc + row0 + r) * a.S + key0));
-                    for (int e = (int)max((int64_t)0, a.M8 - key0); e < KH && key0 + e < a.M; ++e)
-                    {
-                        const uint32_t w2 = packed[e / 2];
-                        out[e] = (uint16_t)((e & 1) ? (w2 >> 16) : (w2 & 0xFFFF));
-                    }
+                    const int c = ch * 4 + c4;
+                    *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) * 16)) =
+                        make_uint4(packed[4 * c4], packed[4 * c4 + 1], packed[4 * c4 + 2], packed[4 * c4 + 3]);
                 }
+                if (key0 + 32 > a.M8 && key0 < a.M)
+                {
+                    // keys [M8, M) are beyond the store map: written directly
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (key0 + e >= a.M8 && key0 + e < a.M)
+                            qk16[row_off + key0 + e] = half_of(packed[e / 2], e & 1);
+                }
+                fence_proxy_async();
+                epi_sync();
+                if (tid == 0)
+                {
+                    tma_store_3d(&tm_p, sbase + kOffP + (uint32_t)sb * kQBox, kt * BN, (int)row0, (int)bh);
+                    bulk_commit();
+                    bulk_wait_read_1(); // the previous tile's store has read the other staging buffer
+                }
+                epi_sync();
             }
             else if (r < rows_valid)
             {
-                T *out = static_cast<T *>(a.qk) + ((bh * a.Qc + row0 + r) * a.S + key0);
-                for (int c = 0; c < 8; ++c)
+#pragma unroll
+                for (int c4 = 0; c4 < 4; ++c4)
                 {
-                    const int64_t col = key0 + c * 8;
+                    const int64_t col = key0 + c4 * 8;
                     if (col + 8 <= a.M)
-                        *reinterpret_cast<uint4 *>(out + c * 8) =
-                            make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+                        *reinterpret_cast<uint4 *>(qk16 + row_off + col) =
+                            make_uint4(packed[4 * c4], packed[4 * c4 + 1], packed[4 * c4 + 2], packed[4 * c4 + 3]);
                     else
-                        for (int e = 0; e < 8 && col + e < a.M; ++e)
-                        {
-                            const uint32_t w2 = packed[4 * c + e / 2];
-                            const uint16_t bits = (uint16_t)((e & 1) ? (w2 >> 16) : (w2 & 0xFFFF));
-                            reinterpret_cast<uint16_t *>(out)[c * 8 + e] = bits;
-                        }
+                    {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            if (col + e < a.M)
+                                qk16[row_off + col + e] = half_of(packed[4 * c4 + e / 2], e & 1);
+                    }
                 }
             }
         }
-        tc_fence_before();
-        __syncthreads(); // TMEM buffer st and (phase B) staging buffer st are complete
-        if (phase_b && full_rows)
-        {
-            if (tid == 0)
-            {
-                for (int c2 = 0; c2 < 2; ++c2)
-                    tma_store_3d(&tm_p, sbase + kOffP + (uint32_t)(st * 2 + c2) * kHalfTile, kt * BN + c2 * KH,
-                                 (int)row0, (int)bh);
-                bulk_commit();
-                bulk_wait_read_1(); // the store of step t-1 has read staging buffer (t+1) % 2
-            }
-            __syncthreads();
-        }
-    }
 
-    // Zero tiles of full-row tiles: keys [M8, M) are beyond the store map.
-    if (full_rows && a.M8 < a.M && n_a * BN < a.M)
-    {
-        T *out = static_cast<T *>(a.qk) + ((bh * a.Qc + row0 + r) * a.S);
-        for (int64_t j = max(a.M8, (int64_t)n_a * BN) + ch; j < a.M; j += 2)
-            out[j] = from_f<T>(0.f);
-    }
-    // Rows that straddle q_len: zero tiles stored directly.
-    if (!full_rows && r < rows_valid)
-    {
-        for (int kt = n_a; kt < a.n_kt; ++kt)
+        // Zero tails: keys [M8, M) of the zero tiles of full-row tiles, and
+        // every zero key of tiles whose rows straddle q_len.
+        if (full_rows && a.M8 < a.M && (int64_t)n_a * BN < a.M)
         {
-            T *out = static_cast<T *>(a.qk) + ((bh * a.Qc + row0 + r) * a.S + (int64_t)kt * BN + ch * KH);
-            for (int e = 0; e < KH; ++e)
-                if ((int64_t)kt * BN + ch * KH + e < a.M)
-                    out[e] = from_f<T>(0.f);
+            for (int64_t j = max(a.M8, (int64_t)n_a * BN) + ch; j < a.M; j += 2)
+                qk16[row_off + j] = 0;
         }
+        if (!full_rows && r < rows_valid)
+        {
+            for (int64_t j = (int64_t)n_a * BN + ch; j < a.M; j += 2)
+                qk16[row_off + j] = 0;
+        }
+        epi_sync();
+        if (tid == 0)
+            bulk_wait_all();
     }
 
     // -------- teardown --------
-    if (tid == 0)
+    if (warp == kCtl && lane == 0 && *abort_flag)
     {
-        if (*abort_flag)
+        // Drain whatever this CTA may still have in flight, each wait bounded.
+        const int quiet = 0; // these waits must not stop early on the abort flag
+        for (int i = 0; i < 2; ++i)
         {
-            // Drain whatever this CTA still has in flight, with the same bound.
-            for (int i = 0; i < 2; ++i)
-            {
-                mbar_wait(bar_k0 + 8 * i, 0);
-                mbar_wait(bar_m0 + 8 * i, 0);
-            }
+            mbar_wait(bar_kfull + 8 * i, 0, &quiet);
+            mbar_wait(bar_mma + 8 * i, 0, &quiet);
         }
-        bulk_wait_all();
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0)
+    if (warp == kCtl)
     {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
 }
 
@@ -524,14 +531,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 }
 
 bool make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
-              uint64_t stride1_bytes, uint64_t stride2_bytes)
+              uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box_rows)
 {
     auto fn = encode_fn();
     if (!fn)
         return false;
     const cuuint64_t dims[3] = {d0, d1, d2};
     const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
-    const cuuint32_t box[3] = {KH, BM, 1};
+    const cuuint32_t box[3] = {KH, box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -547,9 +554,9 @@ int launch_tc(const void *q, const void *k, const uint32_t *q_lens, const uint32
         std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int64_t M = std::min<int64_t>(max_kv, S);
     CUtensorMap mq, mk, mp;
-    if (!make_map(&mq, dt, q, HD, Qc, batch * Hq, HD * 2, Qc * HD * 2) ||
-        !make_map(&mk, dt, k, HD, S, batch * Hkv, HD * 2, S * HD * 2) ||
-        !make_map(&mp, dt, qk, std::max<int64_t>(M & ~int64_t(7), 8), Qc, batch * Hq, S * 2, Qc * S * 2))
+    if (!make_map(&mq, dt, q, HD, Qc, batch * Hq, HD * 2, Qc * HD * 2, BM) ||
+        !make_map(&mk, dt, k, HD, S, batch * Hkv, HD * 2, S * HD * 2, BN) ||
+        !make_map(&mp, dt, qk, std::max<int64_t>(M & ~int64_t(7), 8), Qc, batch * Hq, S * 2, Qc * S * 2, BM))
         return set_error(L2K_ERR_CUDA, "l2k_prefill_attention_scores: tensor map encoding failed");
     // c = (1/sqrtf(128)) * log2(e): the oracle's fp32 scale, moved to base 2 for ex2.
     TcArgs a{q_lens, kv_lens, qk, Hq, Hq / Hkv, Hkv, Qc, S, M, M & ~int64_t(7), (int)ceil_div(max_q, BM),
@@ -583,12 +590,9 @@ int prefill_scores_tc(const void *q, const void *k, const uint32_t *q_lens, cons
     return launch_tc<__half>(q, k, q_lens, kv_lens, max_q, max_kv, qk, batch, Hq, Hkv, Qc, S, stream);
 }
 
-} // namespace l2k
-
-namespace l2k
-{
 int read_scores_error(bool clear); // decode_scores.cu
-}
+
+} // namespace l2k
 
 extern "C" int l2k_device_error(int clear)
 {
