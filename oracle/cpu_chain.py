@@ -62,7 +62,13 @@ class CpuChain:
         else:
             list(self.pool.map(fn, items))
 
-    def step(self, sample=None):
+    def step(self, sample=None, row_stride=1):
+        """One chain step on the sample. row_stride > 1 computes the scores of
+        every row_stride-th query row only (prefill); self.last_times then
+        holds the seconds spent outside and inside the scores, so a caller can
+        extrapolate the full step as other + scores * row_stride."""
+        import time as _time
+        t_start = _time.perf_counter()
         w = self.w
         lib = self.lib
         sample = self._sample if sample is None else sample
@@ -117,6 +123,8 @@ class CpuChain:
             si, hh = item
             kvl = int(kv[si])
             hist = kvl - int(q_lens[si])
+            if not self._rope_only:
+                return score_work(si, hh, kvl, hist)
             for ti in range(int(q_lens[si])):
                 pos = hist + ti
                 row = qkv[si * qlen + ti]
@@ -139,9 +147,11 @@ class CpuChain:
                     q[si, hh, ti] = qo
                     self.k[si, hh, pos] = ko
                 self.v[si, hh, pos] = vh
+
+        def score_work(si, hh, kvl, hist):
             # scores: QK^T over keys < max_kv, intended mask, softmax
             kslice = np.ascontiguousarray(self.k[si, hh, :max_kv])
-            for ti in range(int(q_lens[si])):
+            for ti in range(0, int(q_lens[si]), row_stride):
                 qrow = np.ascontiguousarray(q[si, hh, ti])
                 logits = np.zeros(max_kv, np.float32)
                 mask = np.zeros(max_kv, np.uint8)
@@ -163,7 +173,12 @@ class CpuChain:
                                                    ctypes.c_int64(hd))
                     qk[si, hh, ti, :max_kv] = logits
 
+        self._rope_only = True
         self._map(head_work, [(si, hh) for si in range(nb) for hh in range(h)])
+        t_scores = _time.perf_counter()
+        self._rope_only = False
+        self._map(head_work, [(si, hh) for si in range(nb) for hh in range(h)])
+        t_scores_end = _time.perf_counter()
         # SwiGLU (row blocks)
         ffn = np.empty((t, f), np.float32)
 
@@ -177,5 +192,8 @@ class CpuChain:
                 lib.orc_swiglu(P(gb), ctypes.c_int64(r1 - r0), ctypes.c_int64(f), P(ob))
 
         self._map(swiglu, blocks)
+        t_end = _time.perf_counter()
         self.last = {"normed": normed, "q": q, "qk": qk, "ffn_out": ffn, "kv_lens": kv}
+        self.last_times = {"other": (t_scores - t_start) + (t_end - t_scores_end),
+                           "scores": t_scores_end - t_scores}
         return nb * qlen
