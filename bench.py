@@ -34,7 +34,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from llama2_b200.workloads import WORKLOADS, algorithmic_bytes, host_cache_ok, host_inputs  # noqa: E402
+from llama2_b200.workloads import WORKLOADS, algorithmic_bytes, host_cache_ok, host_inputs, with_batch  # noqa: E402
 
 FALLBACK_HBM_GBS = 6650.0
 
@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the workload's per-GPU batch (small cases for profiling)")
+    ap.add_argument("--unfused", action="store_true",
+                    help="run a decode step as the operator sequence instead of the one-launch fused step")
     return ap.parse_args()
 
 
@@ -154,8 +158,10 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     w = WORKLOADS[args.workload]
+    if args.batch:
+        w = with_batch(w, args.batch)
     inputs = host_inputs(w, seed=0, rank=rank, kv_cache=host_cache_ok(w))
-    chain = Chain(w, inputs, device=dev)
+    chain = Chain(w, inputs, device=dev, fused=not args.unfused)
 
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     flush = torch.empty(max(2 * l2, 256 << 20) // 4, dtype=torch.float32, device=dev)
@@ -164,25 +170,29 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
-    # The dominant kernel (fused scores) is bracketed inside the graph by
-    # external event-record nodes so its duration is measured in every step.
+    # Two graphs of the same step: `chain.graph` (timed per step) and a copy
+    # whose dominant kernel (the fused step, or the fused scores) is
+    # bracketed by external event-record nodes, replayed in a separate loop
+    # so that the event nodes do not add to the step time.
     kev = (torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
-    capture_with_kernel_events(chain, kev)
+    kernel_graph = capture_with_kernel_events(chain, kev)
+    chain.capture()
 
     stream = torch.cuda.current_stream(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
 
-    def one_step(i=None, timed=False):
+    def one_step(graph, i=None):
         chain.reset_lengths()
         flush.zero_()
-        if timed:
+        if i is not None:
             ev[i][0].record(stream)
-        chain.graph.replay()
-        if timed:
+        graph.replay()
+        if i is not None:
             ev[i][1].record(stream)
 
     for _ in range(max(args.warmup, 3)):
-        one_step()
+        one_step(chain.graph)
+        one_step(kernel_graph)
     torch.cuda.synchronize()
 
     clocks = ClockSampler(local_rank)
@@ -191,7 +201,10 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     clocks.start()
     for i in range(args.steps):
-        one_step(i, timed=True)
+        one_step(chain.graph, i)
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        one_step(kernel_graph)
         kev[1].synchronize()
         kernel_ms.append(kev[0].elapsed_time(kev[1]))
     torch.cuda.synchronize()
@@ -221,7 +234,13 @@ def run_ours(args, rank, world, local_rank):
 
     kv_after = inputs["kv_lens"].astype(np.int64) + inputs["q_lens"].astype(np.int64)
     chain_bytes = algorithmic_bytes(w, kv_after)
-    score_bytes = scores_bytes(w, kv_after)
+    # The timed kernel: the fused step (the whole chain) or the fused scores.
+    if chain.fused:
+        kernel_name, kernel_key, kernel_bytes = "fused decode step", "decode_step", chain_bytes
+    else:
+        kernel_name = "fused decode scores" if w.decode else "fused prefill scores"
+        kernel_key = "score_rows_stream" if w.decode else "prefill_scores_tc"
+        kernel_bytes = scores_bytes(w, kv_after)
 
     if world > 1:
         t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
@@ -233,7 +252,7 @@ def run_ours(args, rank, world, local_rank):
         tokens = w.tokens * world * args.steps
         peak, peak_kind = peaks()
         kmean = float(np.mean(kernel_ms)) if kernel_ms else None
-        achieved = score_bytes / (kmean * 1e-3) / 1e9 if kmean else None
+        achieved = kernel_bytes / (kmean * 1e-3) / 1e9 if kmean else None
         result = {
             "metric": "layer-kernel tokens/s at Llama-2-7B dims",
             "value": tokens / (total_ms * 1e-3),
@@ -254,11 +273,11 @@ def run_ours(args, rank, world, local_rank):
             "chain_hbm": {"algorithmic_bytes_per_step": chain_bytes,
                           "achieved_gbs": chain_bytes / (total_ms / args.steps * 1e-3) / 1e9,
                           "frac_of_peak": chain_bytes / (total_ms / args.steps * 1e-3) / 1e9 / peak},
-            "roofline": {"kernel": "fused decode scores" if w.decode else "fused prefill scores",
+            "roofline": {"kernel": kernel_name,
                          "bound": "hbm", "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": achieved / peak if achieved else None,
-                         "algorithmic_bytes_per_launch": score_bytes, "mean_launch_ms": kmean,
-                         "traffic": profiled_traffic(w.name)},
+                         "algorithmic_bytes_per_launch": kernel_bytes, "mean_launch_ms": kmean,
+                         "traffic": profiled_traffic(kernel_key, w.name)},
             "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": chain.kernels_per_step() * args.steps,
@@ -270,11 +289,12 @@ def run_ours(args, rank, world, local_rank):
 
 
 def capture_with_kernel_events(chain, kev):
-    """Capture chain.step() as a graph with event-record nodes around the scores kernel."""
-    import torch
+    """Capture chain.step() as a graph with event-record nodes around the
+    dominant kernel (the fused decode step, or the fused scores)."""
     from llama2_b200 import ops
 
-    orig_dec, orig_pre = ops.decode_attention_scores, ops.prefill_attention_scores
+    names = ("decode_step", "decode_attention_scores", "prefill_attention_scores")
+    orig = {n: getattr(ops, n) for n in names}
 
     def wrap(fn):
         def inner(*a, **k):
@@ -283,11 +303,13 @@ def capture_with_kernel_events(chain, kev):
             kev[1].record()
         return inner
 
-    ops.decode_attention_scores, ops.prefill_attention_scores = wrap(orig_dec), wrap(orig_pre)
+    for n in names:
+        setattr(ops, n, wrap(orig[n]))
     try:
-        chain.capture()
+        return chain.capture()
     finally:
-        ops.decode_attention_scores, ops.prefill_attention_scores = orig_dec, orig_pre
+        for n in names:
+            setattr(ops, n, orig[n])
 
 
 def scores_bytes(w, kv_after):
@@ -301,12 +323,13 @@ def scores_bytes(w, kv_after):
     return int(w.tokens * w.dim * s + kv.sum() * w.dim * s + w.batch * w.heads * q * max_kv * s)
 
 
-def profiled_traffic(workload):
-    """DRAM bytes per launch of the scores kernel from the committed ncu summary, if any."""
+def profiled_traffic(kernel_key, workload):
+    """DRAM bytes (read + write) per launch of the timed kernel on this
+    workload, from the committed ncu summaries; None if not profiled."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get(workload)
+            return json.load(f).get(f"{kernel_key}:{workload}")
     except Exception:
         return None
 

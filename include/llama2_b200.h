@@ -266,8 +266,80 @@ int l2k_prefill_attention_scores(const void *q, const void *k, const uint32_t *q
                                  int64_t kv_cache_len, int64_t head_dim, int dtype, l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Fused decode step: the whole decode chain of one layer step in one launch,
+ * with the results of running, in order,
+ *   l2k_update_q_kv_lens (kv_lens += q_lens; max_lens[0] = max q_len,
+ *                         max_lens[1] = max kv_len, on the device),
+ *   l2k_embedding (x = embed_table[input_ids]),
+ *   l2k_fused_add_residual_rmsnorm without add (normed = RMSNorm(x)),
+ *   l2k_fused_reshape_rope_kvcache_decode (pairing L2K_ROPE_INTERLEAVED) or
+ *     ..._llama2_decode (L2K_ROPE_HALF): q, and K/V rows appended at
+ *     kv_len - 1, skipping sequences with is_done set,
+ *   l2k_decode_attention_scores (qk over keys 0..kv_len-1, max_kv_len =
+ *     max_lens[1]),
+ *   l2k_swiglu (ffn_out from gate_up),
+ * one token per sequence. It composes the reference's update_q_kv_lens,
+ * embedding, fused_add_residual_rmsnorm, fused_reshape_rope_kvcache[_llama2]_decode,
+ * QK^T (launch_linear) + compute_masked_attention_score and swiglu
+ * operators; the reference has no fused step.
+ *
+ * workspace: l2k_decode_step_workspace_bytes() bytes of device memory,
+ * zero before the first call; every completed call leaves it zero again. It
+ * holds the counter through which the last CTA of the grid performs the
+ * length update, so two steps that may run at the same time (different
+ * streams) need different workspaces.
+ *
+ * Supported: head_dim * element size of 64, 128, 256 or 512 bytes; dim and
+ * hidden multiples of 16 bytes of elements; 16-byte aligned tensors; for the
+ * half pairing head_dim / 2 a multiple of 16 bytes of elements. Other shapes
+ * return L2K_ERR_UNSUPPORTED_SHAPE (run the separate operators instead);
+ * l2k_decode_step_supported answers without launching.
+ * ------------------------------------------------------------------------ */
+typedef struct l2k_decode_step_args
+{
+    /* lengths, u32 [batch]; kv_lens is updated in place; max_lens is u32 [2] */
+    const uint32_t *q_lens;
+    uint32_t *kv_lens;
+    uint32_t *max_lens;
+    /* embedding + RMSNorm */
+    const uint32_t *input_ids; /* [batch] */
+    const void *embed_table;   /* [vocab_size, dim] */
+    const void *norm_weight;   /* [dim] */
+    void *x;                   /* [batch, dim] */
+    void *normed;              /* [batch, dim] */
+    /* RoPE + KV append + attention scores */
+    const void *qkv;           /* [batch, (q_head_num + 2 kv_head_num) * head_dim] */
+    const uint8_t *is_done;    /* [batch] */
+    void *q;                   /* (batch, q_head_num, 1, head_dim) */
+    void *k_cache;             /* (batch, kv_head_num, kv_cache_len, head_dim) */
+    void *v_cache;             /* same */
+    void *qk;                  /* (batch, q_head_num, 1, kv_cache_len) */
+    const float *rope_table;   /* l2k_rope_table_fill layout, or NULL */
+    int64_t rope_table_positions;
+    /* SwiGLU */
+    const void *gate_up;       /* [batch, 2 * hidden] */
+    void *ffn_out;             /* [batch, hidden] */
+    /* sizes */
+    int64_t batch;
+    int64_t vocab_size;
+    int64_t dim;
+    int64_t q_head_num;
+    int64_t kv_head_num;
+    int64_t head_dim;
+    int64_t kv_cache_len;
+    int64_t hidden;
+    int pairing; /* l2k_rope_pairing */
+    int dtype;   /* l2k_dtype */
+} l2k_decode_step_args;
+
+int64_t l2k_decode_step_workspace_bytes(void);
+int l2k_decode_step_supported(const l2k_decode_step_args *args);
+int l2k_decode_step(const l2k_decode_step_args *args, uint32_t *workspace, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Device-side error code recorded by kernels that wait on mbarriers (the
- * tcgen05 prefill scores): 0 = none. Every such wait is bounded; a wait that
+ * tcgen05 prefill scores, the streaming score rows, the fused decode step):
+ * 0 = none. Every such wait is bounded; a wait that
  * expires records its code here and the kernel exits instead of hanging.
  * Synchronizes with the device. clear != 0 resets the code. Returns -1 if
  * the code could not be read. (No counterpart in the reference, which has

@@ -21,6 +21,21 @@ i64 = ctypes.c_int64
 u32 = ctypes.c_uint32
 cint = ctypes.c_int
 
+
+class DecodeStepArgs(ctypes.Structure):
+    """l2k_decode_step_args (include/llama2_b200.h), field for field."""
+    _fields_ = [
+        ("q_lens", vp), ("kv_lens", vp), ("max_lens", vp),
+        ("input_ids", vp), ("embed_table", vp), ("norm_weight", vp), ("x", vp), ("normed", vp),
+        ("qkv", vp), ("is_done", vp), ("q", vp), ("k_cache", vp), ("v_cache", vp), ("qk", vp),
+        ("rope_table", vp), ("rope_table_positions", i64),
+        ("gate_up", vp), ("ffn_out", vp),
+        ("batch", i64), ("vocab_size", i64), ("dim", i64), ("q_head_num", i64), ("kv_head_num", i64),
+        ("head_dim", i64), ("kv_cache_len", i64), ("hidden", i64),
+        ("pairing", cint), ("dtype", cint),
+    ]
+
+
 # name -> argument types (restype int unless noted)
 SIGNATURES = {
     "l2k_status_string": ([cint], ctypes.c_char_p),
@@ -48,6 +63,9 @@ SIGNATURES = {
     "l2k_swiglu": [vp, vp, i64, i64, cint, vp],
     "l2k_decode_attention_scores": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],
     "l2k_prefill_attention_scores": [vp, vp, vp, vp, u32, u32, vp, i64, i64, i64, i64, i64, i64, cint, vp],
+    "l2k_decode_step_workspace_bytes": ([], i64),
+    "l2k_decode_step_supported": [ctypes.POINTER(DecodeStepArgs)],
+    "l2k_decode_step": [ctypes.POINTER(DecodeStepArgs), vp, vp],
     "l2k_device_error": ([cint], cint),
 }
 

@@ -9,7 +9,9 @@ This composes the operators in the order the reference's tests exercise them
            -> prefill RoPE + KV append -> fused prefill scores -> SwiGLU
 
 The q/k/v and gate/up activations are inputs (the projection GEMMs are not
-on this path). All buffers live on one device; ``step()`` only enqueues
+on this path). A decode step runs as ONE launch (ops.decode_step, the fused
+decode-step kernel) whenever its shapes are supported, else as the operator
+sequence above. All buffers live on one device; ``step()`` only enqueues
 work on the current stream, and ``capture()`` records the step as a CUDA
 graph so a step costs one graph launch. ``step_e2e()`` is the host-facing
 form: copy this step's inputs from pinned host memory, run, copy the results
@@ -27,7 +29,7 @@ _TORCH = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
 
 
 class Chain:
-    def __init__(self, w: Workload, inputs: dict, device="cuda", use_table: bool = True):
+    def __init__(self, w: Workload, inputs: dict, device="cuda", use_table: bool = True, fused: bool = True):
         self.w = w
         self.device = torch.device(device)
         dt = _TORCH[w.dtype]
@@ -76,8 +78,21 @@ class Chain:
         self.use_table = use_table
         if use_table:
             ops.rope_table(hd, self.device)  # build before any graph capture
+        # Decode runs as one fused launch (ops.decode_step) whenever the shapes
+        # allow it; otherwise, and for prefill, as the sequence of operators.
+        self.fused = False
+        if w.decode and fused:
+            self.workspace = ops.decode_step_workspace(self.device)
+            self.fused = ops.decode_step_supported(**self._step_tensors())
         self.graph = None
         self._pinned = None
+
+    def _step_tensors(self) -> dict:
+        return dict(q_lens=self.q_lens, kv_lens=self.kv_lens, max_lens=self.max_lens, input_ids=self.ids,
+                    embed_table=self.embed_table, norm_weight=self.norm_weight, x=self.x, normed=self.normed,
+                    qkv=self.qkv, is_done=self.is_done, q=self.q, k_cache=self.k_cache, v_cache=self.v_cache,
+                    qk=self.qk, gate_up=self.gate_up, ffn_out=self.ffn_out, pairing=self.w.pairing,
+                    use_table=self.use_table)
 
     # ------------------------------------------------------------------
     def step(self, branches=None):
@@ -90,6 +105,9 @@ class Chain:
         three sub-chains share no data, so the step's critical path is the
         longest of them instead of their sum."""
         w = self.w
+        if self.fused:
+            ops.decode_step(**self._step_tensors(), workspace=self.workspace)
+            return
         main = torch.cuda.current_stream(self.device)
         ops.launch_update_q_kv_lens(self.q_lens, self.kv_lens, self.max_lens[0:1], self.max_lens[1:2])
         if not w.decode:
@@ -124,8 +142,13 @@ class Chain:
             ops.launch_swiglu(self.gate_up, self.ffn_out)
 
     def kernels_per_step(self) -> int:
-        """Kernel launches of this library per step (the prefill scores may be two)."""
-        return 6 if self.w.decode else 7
+        """Kernel launches of this library per step."""
+        if self.fused:
+            return 1
+        if self.w.decode:
+            return 6
+        # lens, maps, embedding, norm, rope, scores (+ masked softmax for fp32), swiglu
+        return 8 if self.w.dtype == "f32" else 7
 
     def reset_lengths(self):
         """Restore the pre-step kv_lens (so a step can be repeated)."""

@@ -135,6 +135,14 @@ __device__ __forceinline__ uint4 as_u4(const Vec16<T> &v)
     return r;
 }
 
+// silu(g) * u as the reference's SwiGLU oracle evaluates it:
+// (g * (1 / (1 + exp(-g)))) * u, IEEE reciprocal, full-precision expf.
+__device__ __forceinline__ float silu_mul(float g, float u)
+{
+    const float sig = __frcp_rn(__fadd_rn(1.0f, expf(-g)));
+    return __fmul_rn(__fmul_rn(g, sig), u);
+}
+
 // ---------------------------------------------------------------------------
 // Reductions.
 // ---------------------------------------------------------------------------

@@ -591,6 +591,7 @@ int prefill_scores_tc(const void *q, const void *k, const uint32_t *q_lens, cons
 }
 
 int read_scores_error(bool clear); // decode_scores.cu
+int read_step_error(bool clear);   // decode_step.cu
 
 } // namespace l2k
 
@@ -607,7 +608,8 @@ extern "C" int l2k_device_error(int clear)
             return -1;
     }
     const int v2 = l2k::read_scores_error(clear != 0);
-    if (v2 < 0)
+    const int v3 = l2k::read_step_error(clear != 0);
+    if (v2 < 0 || v3 < 0)
         return -1;
-    return v ? v : v2;
+    return v ? v : (v2 ? v2 : v3);
 }

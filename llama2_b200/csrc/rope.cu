@@ -23,6 +23,7 @@
 // src/kernel/fused_pad_reshape_transpose_rope_kvcache.cu:11-83,
 // src/kernel/fused_pad_reshape_transpose_rope_kvcache_llama2.cu:11-75.
 #include "common.cuh"
+#include "rope_math.cuh"
 
 #include <algorithm>
 
@@ -118,18 +119,6 @@ __device__ __forceinline__ void store_elems(T *p, const float (&in)[CNT])
         for (int e = 0; e < CNT; ++e)
             p[e] = tmp[e];
     }
-}
-
-// Reference angle formula on the device (include/kernel/rope.cuh:14-17).
-__device__ __forceinline__ void rope_cos_sin_device(int64_t i, int64_t hd, uint32_t pos, uint32_t seq_len, float &c,
-                                                    float &s)
-{
-    const float theta = __fdiv_rn(1.f, powf(10000.f, __fdiv_rn(2.f * (float)i, (float)hd)));
-    const float ratio = __fdiv_rn((float)seq_len, 4096.f);
-    const float alpha = __fdiv_rn(1.f, powf(fmaxf(1.f, ratio), __fdiv_rn(2.f * (float)i, (float)(uint32_t)(hd - 2))));
-    const float angle = __fmul_rn(__fmul_rn((float)pos, alpha), theta);
-    c = cosf(angle);
-    s = sinf(angle);
 }
 
 template <typename T, int PAIRING, int VP, bool PREFILL>

@@ -17,12 +17,6 @@ namespace l2k
 namespace
 {
 
-__device__ __forceinline__ float silu_mul(float g, float u)
-{
-    const float sig = __frcp_rn(__fadd_rn(1.0f, expf(-g)));
-    return __fmul_rn(__fmul_rn(g, sig), u);
-}
-
 template <typename T>
 __global__ void __launch_bounds__(256) swiglu_vec_kernel(const T *__restrict__ in, T *__restrict__ out,
                                                          int64_t n_rows, int64_t inter)

@@ -13,6 +13,7 @@ torch.int32, read as unsigned); masks and done flags are torch.uint8.
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import torch
@@ -314,3 +315,61 @@ def prefill_attention_scores(q, k, q_lens, kv_lens, max_q_len, max_kv_len, qk):
     _require(tuple(qk.shape) == (b, hq, qc, s), "Incorrect qk size")
     capi.call("l2k_prefill_attention_scores", q.data_ptr(), k.data_ptr(), q_lens.data_ptr(), kv_lens.data_ptr(),
               int(max_q_len), int(max_kv_len), qk.data_ptr(), b, hq, hkv, qc, s, hd, _code(q), _stream())
+
+
+# --------------------------------------------------------------------------
+# Fused decode step (one launch for the whole decode chain)
+# --------------------------------------------------------------------------
+def decode_step_workspace(device) -> torch.Tensor:
+    """Zeroed workspace for decode_step (one per step that may run concurrently)."""
+    n = int(capi.lib().l2k_decode_step_workspace_bytes())
+    return torch.zeros((n + 3) // 4, dtype=torch.uint32, device=device)
+
+
+def _decode_step_args(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done, q,
+                      k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table):
+    _dev(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done, q, k_cache, v_cache,
+         qk, gate_up, ffn_out)
+    for t, n in ((q_lens, "q_lens"), (kv_lens, "kv_lens"), (max_lens, "max_lens"), (input_ids, "input_ids")):
+        _u32(t, n)
+    for t in (norm_weight, x, normed, qkv, q, k_cache, v_cache, qk, gate_up, ffn_out):
+        _same(embed_table, t, "decode_step")
+    b = input_ids.numel()
+    vocab, dim = embed_table.shape
+    _, hq, one, hd = q.shape
+    hkv, s = k_cache.shape[1], k_cache.shape[2]
+    hidden = ffn_out.shape[-1]
+    _require(one == 1 and q.shape[0] == b, "Incorrect q size")
+    _require(tuple(k_cache.shape) == (b, hkv, s, hd) and tuple(v_cache.shape) == (b, hkv, s, hd),
+             "Incorrect k/v cache size")
+    _require(tuple(qk.shape) == (b, hq, 1, s), "Incorrect qk size")
+    _require(qkv.numel() == b * (hq + 2 * hkv) * hd, "Incorrect qkv size")
+    _require(x.numel() == b * dim and normed.numel() == b * dim and norm_weight.numel() == dim, "Incorrect x size")
+    _require(gate_up.numel() == 2 * b * hidden and ffn_out.numel() == b * hidden, "Incorrect gate_up size")
+    _require(q_lens.numel() == b and kv_lens.numel() == b and is_done.numel() == b and max_lens.numel() >= 2,
+             "Incorrect lens size")
+    table = rope_table(hd, q.device) if use_table else None
+    return capi.DecodeStepArgs(
+        q_lens.data_ptr(), kv_lens.data_ptr(), max_lens.data_ptr(), input_ids.data_ptr(), embed_table.data_ptr(),
+        norm_weight.data_ptr(), x.data_ptr(), normed.data_ptr(), qkv.data_ptr(), is_done.data_ptr(), q.data_ptr(),
+        k_cache.data_ptr(), v_cache.data_ptr(), qk.data_ptr(), table.data_ptr() if table is not None else None,
+        ROPE_TABLE_POSITIONS if table is not None else 0, gate_up.data_ptr(), ffn_out.data_ptr(), b, vocab, dim, hq,
+        hkv, hd, s, hidden, int(pairing), _code(embed_table))
+
+
+def decode_step(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done, q,
+                k_cache, v_cache, qk, gate_up, ffn_out, workspace, pairing, use_table=True):
+    """The decode chain of one layer step in one launch (l2k_decode_step):
+    lengths update, embedding, RMSNorm, RoPE + KV append, fused scores, SwiGLU.
+    max_lens: 2-element u32 device tensor (max q_len, max kv_len)."""
+    args = _decode_step_args(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done,
+                             q, k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table)
+    _dev(workspace)
+    capi.call("l2k_decode_step", ctypes.byref(args), workspace.data_ptr(), _stream())
+
+
+def decode_step_supported(**kw) -> bool:
+    """Whether decode_step takes these tensors (shape and alignment support)."""
+    kw.pop("workspace", None)
+    args = _decode_step_args(**kw)
+    return capi.lib().l2k_decode_step_supported(ctypes.byref(args)) == 0

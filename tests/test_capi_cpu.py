@@ -83,3 +83,45 @@ def test_rope_table_matches_oracle_bitwise(hd):
         for i in range(hd // 2):
             c, s = port.rope_cos_sin(i, hd, pos, pos + 1)
             assert t[pos, i, 0] == np.float32(c) and t[pos, i, 1] == np.float32(s), (pos, i)
+
+
+def _step_args(**over):
+    """l2k_decode_step_args with fake 16-byte aligned (never dereferenced) pointers."""
+    a = capi.DecodeStepArgs()
+    for i, (name, typ) in enumerate(capi.DecodeStepArgs._fields_):
+        if typ is capi.vp:
+            setattr(a, name, 0x10000 + 0x100 * i)
+    a.batch, a.vocab_size, a.dim, a.q_head_num, a.kv_head_num = 1, 32000, 4096, 32, 32
+    a.head_dim, a.kv_cache_len, a.hidden, a.pairing, a.dtype = 128, 4096, 11008, 1, 0
+    a.rope_table_positions = 4096
+    for k, v in over.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("over,status", [
+    (dict(head_dim=48), 3),               # 192-byte K rows: not a streaming row size
+    (dict(head_dim=96, dtype=2), 3),      # 192-byte rows in bf16
+    (dict(dim=4094), 3),                  # dim not a multiple of 16 bytes
+    (dict(qkv=0x10008), 3),               # misaligned tensor
+    (dict(kv_head_num=5), 1),             # q_head_num not a multiple of kv_head_num
+    (dict(head_dim=127), 1),              # odd head_dim
+    (dict(dtype=9), 1),
+    (dict(pairing=2), 1),
+    (dict(kv_lens=None), 1),
+    (dict(normed=0x10000, x=0x10000), 1), # x and normed alias
+])
+def test_decode_step_rejects_before_launch(over, status):
+    assert capi.lib().l2k_decode_step_supported(ctypes.byref(_step_args(**over))) == status
+    assert capi.lib().l2k_last_error_message()
+
+
+def test_decode_step_null_args_and_workspace():
+    assert capi.lib().l2k_decode_step(None, None, None) == 1
+    assert capi.lib().l2k_decode_step(ctypes.byref(_step_args()), None, None) == 1
+    assert capi.lib().l2k_decode_step_workspace_bytes() >= 4
+
+
+def test_decode_step_empty_batch_is_noop():
+    ws = np.zeros(4, np.uint32)
+    assert capi.lib().l2k_decode_step(ctypes.byref(_step_args(batch=0)), ws.ctypes.data, None) == 0

@@ -29,7 +29,7 @@ def _lib(cuda_lib):
 
 def run_and_check(w, seed=0, fused=True):
     inp = host_inputs(w, seed=seed)
-    ch = Chain(w, inp)
+    ch = Chain(w, inp, fused=fused)
     ch.step()
     torch.cuda.synchronize()
     ref = ochain.decode_step(w, inp) if w.decode else ochain.prefill_step(w, inp)
@@ -56,21 +56,30 @@ def test_tiny_decode_fp32():
     run_and_check(WORKLOADS["tiny"])
 
 
+# fused=True runs the one-launch decode step, fused=False the operator sequence.
+@pytest.mark.parametrize("fused", [True, False])
 @pytest.mark.parametrize("seed", [0, 1])
-def test_7b_b1_decode_fp32(seed):
-    run_and_check(WORKLOADS["7b-b1"], seed=seed)
+def test_7b_b1_decode_fp32(seed, fused):
+    ch, _ = run_and_check(WORKLOADS["7b-b1"], seed=seed, fused=fused)
+    assert ch.fused == fused
 
 
-def test_7b_batched_decode_fp32():
-    run_and_check(with_batch(WORKLOADS["7b-b64"], 4))
+@pytest.mark.parametrize("fused", [True, False])
+def test_7b_batched_decode_fp32(fused):
+    ch, _ = run_and_check(with_batch(WORKLOADS["7b-b64"], 4), fused=fused)
+    assert ch.fused == fused
 
 
-def test_7b_batched_decode_bf16():
-    run_and_check(with_batch(WORKLOADS["7b-b64-bf16"], 4))
+@pytest.mark.parametrize("fused", [True, False])
+def test_7b_batched_decode_bf16(fused):
+    ch, _ = run_and_check(with_batch(WORKLOADS["7b-b64-bf16"], 4), fused=fused)
+    assert ch.fused == fused
 
 
-def test_13b_decode_fp16():
-    run_and_check(with_batch(WORKLOADS["13b-b256"], 2))
+@pytest.mark.parametrize("fused", [True, False])
+def test_13b_decode_fp16(fused):
+    ch, _ = run_and_check(with_batch(WORKLOADS["13b-b256"], 2), fused=fused)
+    assert ch.fused == fused
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
@@ -79,21 +88,24 @@ def test_prefill_small(dtype):
     run_and_check(w)
 
 
-def test_decode_interleaved_pairs_hd128():
+@pytest.mark.parametrize("fused", [True, False])
+def test_decode_interleaved_pairs_hd128(fused):
     w = dataclasses.replace(with_batch(WORKLOADS["7b-b64"], 2), pairing=0)
-    run_and_check(w)
+    run_and_check(w, fused=fused)
 
 
-def test_decode_done_sequences_untouched():
+@pytest.mark.parametrize("fused", [True, False])
+def test_decode_done_sequences_untouched(fused):
     w = with_batch(WORKLOADS["7b-b64"], 3)
     inp = host_inputs(w, seed=5)
     inp["is_done"] = np.array([0, 1, 0], np.uint8)
-    ch = Chain(w, inp)
+    ch = Chain(w, inp, fused=fused)
     ch.step()
     torch.cuda.synchronize()
     ref = ochain.decode_step(w, inp)
     assert bits_equal(host(ch.k_cache), ref["k"]) and bits_equal(host(ch.v_cache), ref["v"])
     assert bits_equal(host(ch.q), ref["q"])
+    assert max_rel_err(host(ch.qk), ref["qk"]) <= 1e-5
 
 
 def test_graph_replay_matches_eager():
