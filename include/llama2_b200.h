@@ -337,6 +337,26 @@ int l2k_decode_step_supported(const l2k_decode_step_args *args);
 int l2k_decode_step(const l2k_decode_step_args *args, uint32_t *workspace, l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * l2k_decode_step without a workspace argument, for callers that cannot
+ * provide device memory (for example a binding whose host side only passes
+ * the tensors it already has and owns no device allocator). The workspace is
+ * a 256-byte scratch array inside this library, one per device; nothing is
+ * allocated. (No counterpart in the reference, which has no fused step.)
+ *  - The first call on a device looks the scratch up (cudaGetSymbolAddress,
+ *    with that device current); make it before any stream capture.
+ *  - The scratch is zero when the library loads and every completed call
+ *    leaves it zero; a call that did not complete (a CUDA error) can leave it
+ *    nonzero, and the library must then be reloaded.
+ *  - Calls on one device share the scratch: two steps that may run at the
+ *    same time (different streams) race and give wrong lengths. Use
+ *    l2k_decode_step with separate workspaces for that.
+ *  - Returns L2K_ERR_UNSUPPORTED_SHAPE if the step's workspace
+ *    (l2k_decode_step_workspace_bytes) exceeds the 256-byte scratch or the
+ *    device ordinal is >= 64.
+ * ------------------------------------------------------------------------ */
+int l2k_decode_step_no_alloc(const l2k_decode_step_args *args, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Device-side error code recorded by kernels that wait on mbarriers (the
  * tcgen05 prefill scores, the streaming score rows, the fused decode step):
  * 0 = none. Every such wait is bounded; a wait that

@@ -39,6 +39,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 
 namespace l2k
 {
@@ -344,4 +345,57 @@ extern "C" int l2k_decode_step_supported(const l2k_decode_step_args *args)
 extern "C" int l2k_decode_step(const l2k_decode_step_args *args, uint32_t *workspace, l2k_stream_t stream)
 {
     return l2k::step_entry(args, workspace, stream, true);
+}
+
+// ---------------------------------------------------------------------------
+// l2k_decode_step_no_alloc: the same launch with its workspace in a
+// file-scope device array instead of caller memory. The array is 256 bytes
+// (the step needs l2k_decode_step_workspace_bytes() of them); each device
+// has its own copy, zero when the module loads, and every completed step
+// leaves it zero again. Its address is looked up once per device with
+// cudaGetSymbolAddress (the first call on a device, with that device
+// current) and cached; nothing is allocated.
+// ---------------------------------------------------------------------------
+namespace l2k
+{
+constexpr int kStepScratchBytes = 256;
+constexpr int kMaxScratchDevices = 64;
+static __device__ __align__(256) uint32_t g_step_scratch[kStepScratchBytes / 4];
+
+namespace
+{
+std::mutex g_scratch_mutex;
+uint32_t *g_scratch_ptr[kMaxScratchDevices] = {};
+} // namespace
+} // namespace l2k
+
+extern "C" int l2k_decode_step_no_alloc(const l2k_decode_step_args *args, l2k_stream_t stream)
+{
+    using namespace l2k;
+    if (l2k_decode_step_workspace_bytes() > kStepScratchBytes)
+        return set_error(L2K_ERR_UNSUPPORTED_SHAPE,
+                         "l2k_decode_step_no_alloc: the step needs %lld bytes of scratch, the static scratch holds %d",
+                         (long long)l2k_decode_step_workspace_bytes(), kStepScratchBytes);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return set_error(L2K_ERR_CUDA, "l2k_decode_step_no_alloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxScratchDevices)
+        return set_error(L2K_ERR_UNSUPPORTED_SHAPE, "l2k_decode_step_no_alloc: device %d >= %d", dev,
+                         kMaxScratchDevices);
+    uint32_t *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_scratch_mutex);
+        if (!g_scratch_ptr[dev])
+        {
+            void *p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_step_scratch);
+            if (e != cudaSuccess)
+                return set_error(L2K_ERR_CUDA, "l2k_decode_step_no_alloc: cudaGetSymbolAddress: %s",
+                                 cudaGetErrorString(e));
+            g_scratch_ptr[dev] = static_cast<uint32_t *>(p);
+        }
+        scratch = g_scratch_ptr[dev];
+    }
+    return step_entry(args, scratch, stream, true);
 }

@@ -368,6 +368,16 @@ def decode_step(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weigh
     capi.call("l2k_decode_step", ctypes.byref(args), workspace.data_ptr(), _stream())
 
 
+def decode_step_no_alloc(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv,
+                         is_done, q, k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table=True):
+    """decode_step with the library's own static scratch as workspace
+    (l2k_decode_step_no_alloc): no workspace argument, nothing allocated;
+    steps on one device must not overlap."""
+    args = _decode_step_args(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done,
+                             q, k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table)
+    capi.call("l2k_decode_step_no_alloc", ctypes.byref(args), _stream())
+
+
 def decode_step_supported(**kw) -> bool:
     """Whether decode_step takes these tensors (shape and alignment support)."""
     kw.pop("workspace", None)
