@@ -242,20 +242,16 @@ def run_ours(args, rank, world, local_rank):
         kernel_key = "score_rows_stream" if w.decode else "prefill_scores_tc"
         kernel_bytes = scores_bytes(w, kv_after)
 
-    if world > 1:
-        t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, e2e_ms = t.tolist()
+    total_ms, e2e_ms = max_over_ranks([total_ms, e2e_ms], world, dev)
 
     result = None
     if rank == 0:
-        tokens = w.tokens * world * args.steps
         peak, peak_kind = peaks()
         kmean = float(np.mean(kernel_ms)) if kernel_ms else None
         achieved = kernel_bytes / (kmean * 1e-3) / 1e9 if kmean else None
         result = {
             "metric": "layer-kernel tokens/s at Llama-2-7B dims",
-            "value": tokens / (total_ms * 1e-3),
+            "value": job_tokens_per_s(w.tokens, world, args.steps, total_ms),
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
@@ -278,7 +274,8 @@ def run_ours(args, rank, world, local_rank):
                          "unit": "GB/s", "frac": achieved / peak if achieved else None,
                          "algorithmic_bytes_per_launch": kernel_bytes, "mean_launch_ms": kmean,
                          "traffic": profiled_traffic(kernel_key, w.name)},
-            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "e2e": {"value": job_tokens_per_s(w.tokens, world, args.steps, e2e_ms), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": chain.kernels_per_step() * args.steps,
             "clocks": clocks.summary(),
@@ -286,6 +283,23 @@ def run_ours(args, rank, world, local_rank):
         if not args.no_cpu_baseline and world == 1:
             result["cpu_baseline"] = cpu_chain_rate(w, inputs, args.cpu_sample_seconds, impl="port")
     return result
+
+
+def max_over_ranks(values, world, device):
+    """Element-wise maximum over all ranks of a list of floats (every rank
+    calls it, in the same order): the job's time is its slowest rank's."""
+    if world == 1:
+        return list(values)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def job_tokens_per_s(tokens_per_rank_step, world, steps, max_ms):
+    """Whole-job throughput: every rank's tokens over the slowest rank's time."""
+    return tokens_per_rank_step * world * steps / (max_ms * 1e-3)
 
 
 def capture_with_kernel_events(chain, kev):

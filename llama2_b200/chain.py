@@ -28,6 +28,27 @@ from .workloads import Workload
 _TORCH = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}
 
 
+class Packed:
+    """Several tensors as 256-byte aligned views of one contiguous buffer, so
+    that a step's inputs (or results) cross PCIe in one copy."""
+
+    def __init__(self, specs, device, pin=False):
+        offs, off = [], 0
+        for _, shape, dt in specs:
+            off = (off + 255) // 256 * 256
+            n = int(np.prod(shape)) * torch.empty((), dtype=dt).element_size()
+            offs.append((off, n))
+            off += n
+        self.buf = torch.zeros(off, dtype=torch.uint8, device=device)
+        if pin:
+            self.buf = self.buf.pin_memory()
+        self.views = {name: self.buf[o:o + n].view(dt).view(shape)
+                      for (name, shape, dt), (o, n) in zip(specs, offs)}
+
+    def __getitem__(self, name):
+        return self.views[name]
+
+
 class Chain:
     def __init__(self, w: Workload, inputs: dict, device="cuda", use_table: bool = True, fused: bool = True):
         self.w = w
@@ -53,22 +74,25 @@ class Chain:
             g.manual_seed(int(inputs.get("cache_seed", 0)))
             self.k_cache = torch.randn(b, h, s, hd, generator=g, dtype=dt, device=self.device)
             self.v_cache = torch.randn(b, h, s, hd, generator=g, dtype=dt, device=self.device)
-        # per-step inputs
-        self.ids = put(inputs["ids"])
-        self.q_lens = put(inputs["q_lens"])
-        self.kv_lens = put(inputs["kv_lens"])
-        self.kv_lens_initial = self.kv_lens.clone()
-        self.is_done = put(inputs["is_done"])
-        self.qkv = put(inputs["qkv"], dt)
-        self.gate_up = put(inputs["gate_up"], dt)
-        # outputs / intermediates
-        self.x = torch.empty(t, d, dtype=dt, device=self.device)
-        self.normed = torch.empty(t, d, dtype=dt, device=self.device)
+        # per-step inputs, packed (one host-to-device copy per step)
         qc = w.prefill_len or 1
+        self.in_specs = [("ids", (t,), torch.uint32), ("q_lens", (b,), torch.uint32),
+                         ("kv_lens", (b,), torch.uint32), ("is_done", (b,), torch.uint8),
+                         ("qkv", (t, 3 * d), dt), ("gate_up", (t, 2 * f), dt)]
+        self.inputs = Packed(self.in_specs, self.device)
+        for name, _, tdt in self.in_specs:
+            self.inputs[name].copy_(torch.from_numpy(np.ascontiguousarray(inputs[name])).to(tdt))
+        self.ids, self.q_lens, self.kv_lens = self.inputs["ids"], self.inputs["q_lens"], self.inputs["kv_lens"]
+        self.is_done, self.qkv, self.gate_up = self.inputs["is_done"], self.inputs["qkv"], self.inputs["gate_up"]
+        self.kv_lens_initial = self.kv_lens.clone()
+        # results, packed (one device-to-host copy per step), and intermediates
+        self.out_specs = [("max_lens", (2,), torch.uint32), ("normed", (t, d), dt), ("ffn_out", (t, f), dt),
+                          ("qk", (b, h, qc, s), dt)]
+        self.outputs = Packed(self.out_specs, self.device)
+        self.max_lens, self.normed = self.outputs["max_lens"], self.outputs["normed"]
+        self.ffn_out, self.qk = self.outputs["ffn_out"], self.outputs["qk"]
+        self.x = torch.empty(t, d, dtype=dt, device=self.device)
         self.q = torch.zeros(b, h, qc, hd, dtype=dt, device=self.device)
-        self.qk = torch.zeros(b, h, qc, s, dtype=dt, device=self.device)
-        self.ffn_out = torch.empty(t, f, dtype=dt, device=self.device)
-        self.max_lens = torch.zeros(2, dtype=torch.uint32, device=self.device)
         if not w.decode:
             self.unpad_to_pad = torch.zeros(b, qc, dtype=torch.uint32, device=self.device)
             self.seq_offsets = torch.zeros(b, dtype=torch.uint32, device=self.device)
@@ -178,37 +202,24 @@ class Chain:
 
     # ------------------------------------------------------------------
     def host_buffers(self, inputs: dict):
-        """Pinned host copies of the per-step inputs and the step's results."""
-        pin = lambda a, dt=None: (torch.from_numpy(np.ascontiguousarray(a)).to(dt) if dt else
-                                  torch.from_numpy(np.ascontiguousarray(a))).pin_memory()
-        ins = {
-            "ids": pin(inputs["ids"]), "q_lens": pin(inputs["q_lens"]), "kv_lens": pin(inputs["kv_lens"]),
-            "is_done": pin(inputs["is_done"]), "qkv": pin(inputs["qkv"], self.dtype),
-            "gate_up": pin(inputs["gate_up"], self.dtype),
-        }
-        outs = {
-            "normed": torch.empty_like(self.normed, device="cpu").pin_memory(),
-            "qk": torch.empty_like(self.qk, device="cpu").pin_memory(),
-            "ffn_out": torch.empty_like(self.ffn_out, device="cpu").pin_memory(),
-            "max_lens": torch.empty_like(self.max_lens, device="cpu").pin_memory(),
-        }
-        self._pinned = (ins, outs)
-        return ins, outs
+        """Pinned host images of the packed per-step inputs (filled from
+        `inputs`) and of the packed results."""
+        hin = Packed(self.in_specs, "cpu", pin=True)
+        for name, _, tdt in self.in_specs:
+            hin[name].copy_(torch.from_numpy(np.ascontiguousarray(inputs[name])).to(tdt))
+        hout = Packed(self.out_specs, "cpu", pin=True)
+        self._pinned = (hin, hout)
+        return hin, hout
 
     def e2e_bytes(self):
-        ins, outs = self._pinned
-        return (sum(t.numel() * t.element_size() for t in ins.values()),
-                sum(t.numel() * t.element_size() for t in outs.values()))
+        hin, hout = self._pinned
+        return hin.buf.numel(), hout.buf.numel()
 
     def step_e2e(self):
-        """H2D of the step inputs, the chain (graph replay), D2H of the results."""
-        ins, outs = self._pinned
-        dsts = {"ids": self.ids, "q_lens": self.q_lens, "kv_lens": self.kv_lens, "is_done": self.is_done,
-                "qkv": self.qkv, "gate_up": self.gate_up}
-        for k, t in ins.items():
-            dsts[k].copy_(t, non_blocking=True)
+        """One copy of the step's inputs to the device, the step (graph
+        replay), one copy of its results (lengths maxima, normed rows, scores,
+        SwiGLU output) back to pinned host memory."""
+        hin, hout = self._pinned
+        self.inputs.buf.copy_(hin.buf, non_blocking=True)
         self.replay()
-        outs["normed"].copy_(self.normed, non_blocking=True)
-        outs["qk"].copy_(self.qk, non_blocking=True)
-        outs["ffn_out"].copy_(self.ffn_out, non_blocking=True)
-        outs["max_lens"].copy_(self.max_lens, non_blocking=True)
+        hout.buf.copy_(self.outputs.buf, non_blocking=True)

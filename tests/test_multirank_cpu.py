@@ -1,0 +1,67 @@
+"""The multi-rank host logic of bench.py on CPU: two gloo ranks (world 2).
+
+Each rank owns its own sequence-batch shard (seeded by rank, no exchange on
+the data path); the job's time is the maximum over ranks, and its throughput
+is every rank's tokens over that time."""
+import os
+import socket
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import bench
+from llama2_b200.workloads import WORKLOADS, host_inputs, with_batch
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # rank-dependent step times: the job's time is the slowest rank's
+        got = bench.max_over_ranks([1.0 + rank, 10.0 - rank], world, "cpu")
+        w = with_batch(WORKLOADS["tiny"], 2)
+        inp = host_inputs(w, seed=0, rank=rank)
+        digest = float(np.asarray(inp["qkv"], np.float64).sum())
+        d = torch.tensor([digest], dtype=torch.float64)
+        all_d = [torch.zeros(1, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(all_d, d)
+        out.put((rank, got, [x.item() for x in all_d]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks():
+    world, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, got, digests in res:
+        assert got == [2.0, 10.0]
+        assert digests[0] != digests[1]  # each rank has its own shard
+
+
+def test_shards_are_deterministic_per_rank():
+    w = with_batch(WORKLOADS["tiny"], 2)
+    a, b = host_inputs(w, seed=0, rank=1), host_inputs(w, seed=0, rank=1)
+    for k in ("ids", "qkv", "kv_lens", "k_cache"):
+        assert np.array_equal(a[k], b[k])
+
+
+def test_job_throughput_counts_every_rank():
+    # 4 ranks x 64 tokens x 10 steps over a slowest-rank time of 2 ms
+    assert bench.job_tokens_per_s(64, 4, 10, 2.0) == 64 * 4 * 10 / 2e-3
+    assert bench.max_over_ranks([3.0, 1.0], 1, "cpu") == [3.0, 1.0]
