@@ -4,7 +4,7 @@
 // One CTA owns 128 query rows of one (seq, head); key tiles are 64 wide.
 // Warp roles (288 threads, two CTAs per SM):
 //   * warp 8 (control): TMA (cp.async.bulk.tensor, 128-byte swizzle) of the
-//     Q tile once and of K tiles through a 2-stage ring; tcgen05.mma
+//     Q tile once and of K tiles through a 3-stage ring; tcgen05.mma
 //     (M=128, N=64, K=16 x 8) with both operands in shared memory and the
 //     fp32 accumulator in tensor memory (2 x 64 columns, double buffered);
 //     tcgen05.commit signals "tile ready" on an mbarrier.
@@ -12,11 +12,12 @@
 //     columns 32*(w/4).. of each tile with tcgen05.ld.
 //     Phase A walks the causally visible key tiles keeping an online row max
 //     and sum of exponentials (log2 units, ex2); phase B re-runs the MMAs
-//     and writes P = 2^(s*c - m) / (sum + 1e-6) once, through a swizzled
-//     shared staging buffer and TMA stores. Each finished tile frees its TMEM
-//     buffer through an mbarrier, so the MMA of the next tile overlaps.
-//   * Key tiles beyond the causal limit are TMA-stored from a zeroed staging
-//     buffer at the start (overlapping phase A). Keys >= max_kv are never
+//     and writes P = 2^(s*c - m) / (sum + 1e-6) once: each warp stages its
+//     32 x 32 block (64-byte swizzle) and TMA-stores it itself, so phase B
+//     has no CTA-wide barrier. Each finished tile frees its TMEM buffer
+//     through an mbarrier, so the MMA of the next tile overlaps.
+//   * Key tiles beyond the causal limit are TMA-stored from the zeroed staging
+//     region at the start (overlapping phase A). Keys >= max_kv are never
 //     written (the store map's extent; its 16-byte-rounded tail is written
 //     directly); tiles whose rows straddle q_len are written directly.
 // CTA order is (seq, head)-major so the query tiles of one head run together
@@ -52,10 +53,12 @@ constexpr int kThreads = 32 * (kEpiWarps + 1);
 constexpr int kCtl = kEpiWarps;                        // control warp index
 constexpr uint32_t kQBox = 128 * 128;                  // 128 rows x 128 B
 constexpr uint32_t kKBox = 64 * 128;                   // 64 rows x 128 B
+constexpr int kKStages = 3;                            // K ring depth
+constexpr uint32_t kWarpStage = 32 * 64;               // one warp's 32 x 32 block of P (64-byte rows)
 constexpr uint32_t kOffQ = 0;                          // 2 boxes (hd halves)
-constexpr uint32_t kOffK = kOffQ + 2 * kQBox;          // 2 stages x 2 boxes
-constexpr uint32_t kOffP = kOffK + 4 * kKBox;          // 2 staging buffers of one 128x64 box
-constexpr uint32_t kOffBar = kOffP + 2 * kQBox;        // mbarriers
+constexpr uint32_t kOffK = kOffQ + 2 * kQBox;          // kKStages stages x 2 boxes
+constexpr uint32_t kOffP = kOffK + kKStages * 2 * kKBox; // 8 warp blocks = one zeroed 128 x 64 box at the start
+constexpr uint32_t kOffBar = kOffP + kEpiWarps * kWarpStage; // mbarriers
 constexpr uint32_t kOffMisc = kOffBar + 128;           // tmem slot, abort flag
 constexpr uint32_t kOffStats = kOffMisc + 64;          // 2 x 128 float2
 constexpr uint32_t kSmemBytes = kOffStats + 2 * 128 * 8 + 1024; // + alignment slack
@@ -227,15 +230,16 @@ __device__ __forceinline__ void fail(int code, volatile int *abort_flag)
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_scores_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                             const __grid_constant__ CUtensorMap tm_p, const TcArgs a)
+                             const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_pw,
+                             const TcArgs a)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar_q = sbase + kOffBar;
-    const uint32_t bar_kfull = bar_q + 8;    // + 8 * stage
-    const uint32_t bar_mma = bar_q + 24;     // + 8 * buffer: tile in TMEM buffer is ready
-    const uint32_t bar_tfree = bar_q + 40;   // + 8 * buffer: epilogue finished with TMEM buffer
+    const uint32_t bar_kfull = bar_q + 8;    // + 8 * stage (kKStages)
+    const uint32_t bar_mma = bar_q + 32;     // + 8 * buffer: tile in TMEM buffer is ready
+    const uint32_t bar_tfree = bar_q + 48;   // + 8 * buffer: epilogue finished with TMEM buffer
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffMisc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kOffMisc + 8);
     float2 *stats = reinterpret_cast<float2 *>(smem + kOffStats); // [2][128]
@@ -263,9 +267,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (tid == 0)
     {
         mbar_init(bar_q, 1);
+        for (int i = 0; i < kKStages; ++i)
+            mbar_init(bar_kfull + 8 * i, 1);
         for (int i = 0; i < 2; ++i)
         {
-            mbar_init(bar_kfull + 8 * i, 1);
             mbar_init(bar_mma + 8 * i, 1);
             mbar_init(bar_tfree + 8 * i, kEpiWarps);
         }
@@ -279,9 +284,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     {
-        // staging buffer 0 starts as the zero tile
+        // the staging region starts as the zero 128 x 64 tile
         uint4 *z = reinterpret_cast<uint4 *>(smem + kOffP);
-        for (int i = tid; i < (int)(kQBox / 16); i += kThreads)
+        for (int i = tid; i < (int)(kEpiWarps * kWarpStage / 16); i += kThreads)
             z[i] = make_uint4(0, 0, 0, 0);
     }
     fence_proxy_async();
@@ -298,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint32_t idesc = instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u);
             const int kz = (int)(b * a.Hkv + kvh);
             auto issue_k = [&](int t) {
-                const int kt = t % n_a, st = t & 1;
+                const int kt = t % n_a, st = t % kKStages;
                 const uint32_t dst = sbase + kOffK + st * 2 * kKBox;
                 mbar_expect_tx(bar_kfull + 8 * st, 2 * kKBox);
                 for (int hf = 0; hf < 2; ++hf)
@@ -307,15 +312,14 @@ __global__ void __launch_bounds__(kThreads, 2)
             mbar_expect_tx(bar_q, 2 * kQBox);
             for (int hf = 0; hf < 2; ++hf)
                 tma_load_3d(sbase + kOffQ + hf * kQBox, &tm_q, hf * KH, (int)row0, (int)bh, bar_q);
-            issue_k(0);
-            if (n_steps > 1)
-                issue_k(1);
+            for (int t = 0; t < kKStages && t < n_steps; ++t)
+                issue_k(t);
             if (!mbar_wait(bar_q, 0, abort_flag))
                 fail(ERR_WAIT_Q, abort_flag);
             for (int t = 0; t < n_steps && !*abort_flag; ++t)
             {
-                const int st = t & 1;
-                if (!mbar_wait(bar_kfull + 8 * st, (t >> 1) & 1, abort_flag))
+                const int st = t & 1, ks = t % kKStages; // TMEM buffer, K stage
+                if (!mbar_wait(bar_kfull + 8 * ks, (t / kKStages) & 1, abort_flag))
                 {
                     fail(ERR_WAIT_K, abort_flag);
                     break;
@@ -326,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t kb = sbase + kOffK + st * 2 * kKBox;
+                const uint32_t kb = sbase + kOffK + ks * 2 * kKBox;
                 const uint32_t d = tmem + (uint32_t)(st * BN);
 #pragma unroll
                 for (int k = 0; k < HD / 16; ++k)
@@ -336,16 +340,18 @@ __global__ void __launch_bounds__(kThreads, 2)
                     mma_f16(d, smem_desc(sbase + kOffQ + offa), smem_desc(kb + offb), idesc, k > 0 ? 1u : 0u);
                 }
                 mma_commit(bar_mma + 8 * st);
-                if (t + 2 < n_steps)
+                if (t >= 1 && t + 2 < n_steps)
                 {
-                    // the K stage is free once this tile's MMAs have read it
-                    if (!mbar_wait(bar_mma + 8 * st, (t >> 1) & 1, abort_flag))
+                    // K stage (t - 1) % kKStages = (t + 2) % kKStages is free once
+                    // the previous tile's MMAs (long done) have read it
+                    if (!mbar_wait(bar_mma + 8 * ((t - 1) & 1), ((t - 1) >> 1) & 1, abort_flag))
                     {
                         fail(ERR_WAIT_MMA, abort_flag);
                         break;
                     }
                     issue_k(t + 2);
                 }
+
             }
         }
     }
@@ -425,17 +431,18 @@ __global__ void __launch_bounds__(kThreads, 2)
                 packed[j / 2] = pack2<T>(ex2(fmaf(v[j], a.c, -m)) * inv, ex2(fmaf(v[j + 1], a.c, -m)) * inv);
             if (full_rows)
             {
-                // 128-byte swizzled staging row: 16-byte chunk c at (c ^ (r % 8)); this
-                // warp fills chunks 4*ch .. 4*ch+3 of row r.
-                const int sb = (t - n_a) & 1;
-                uint8_t *dst = smem + kOffP + (uint32_t)sb * kQBox + (uint32_t)r * 128;
+                // This warp's 32 x 32 block (rows quad*32.., keys key0..) staged with
+                // the 64-byte swizzle (16-byte chunk c of row r at c ^ ((r / 2) % 4))
+                // and stored by the warp itself.
+                uint8_t *wst = smem + kOffP + (uint32_t)warp * kWarpStage;
+                if (lane == 0)
+                    bulk_wait_read_0(); // this warp's previous store has read the block
+                __syncwarp();
+                uint8_t *dst = wst + (uint32_t)lane * 64;
 #pragma unroll
                 for (int c4 = 0; c4 < 4; ++c4)
-                {
-                    const int c = ch * 4 + c4;
-                    *reinterpret_cast<uint4 *>(dst + ((c ^ (r & 7)) * 16)) =
+                    *reinterpret_cast<uint4 *>(dst + ((c4 ^ ((lane >> 1) & 3)) * 16)) =
                         make_uint4(packed[4 * c4], packed[4 * c4 + 1], packed[4 * c4 + 2], packed[4 * c4 + 3]);
-                }
                 if (key0 + 32 > a.M8 && key0 < a.M)
                 {
                     // keys [M8, M) are beyond the store map: written directly
@@ -445,14 +452,12 @@ __global__ void __launch_bounds__(kThreads, 2)
                             qk16[row_off + key0 + e] = half_of(packed[e / 2], e & 1);
                 }
                 fence_proxy_async();
-                epi_sync();
-                if (tid == 0)
+                __syncwarp();
+                if (lane == 0)
                 {
-                    tma_store_3d(&tm_p, sbase + kOffP + (uint32_t)sb * kQBox, kt * BN, (int)row0, (int)bh);
+                    tma_store_3d(&tm_pw, smem_u32(wst), (int)key0, (int)(row0 + quad * 32), (int)bh);
                     bulk_commit();
-                    bulk_wait_read_1(); // the previous tile's store has read the other staging buffer
                 }
-                epi_sync();
             }
             else if (r < rows_valid)
             {
@@ -486,9 +491,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             for (int64_t j = (int64_t)n_a * BN + ch; j < a.M; j += 2)
                 qk16[row_off + j] = 0;
         }
-        epi_sync();
-        if (tid == 0)
-            bulk_wait_all();
+        if (lane == 0)
+            bulk_wait_all(); // this warp's stores (and, for warp 0, the zero tiles)
     }
 
     // -------- teardown --------
@@ -496,11 +500,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     {
         // Drain whatever this CTA may still have in flight, each wait bounded.
         const int quiet = 0; // these waits must not stop early on the abort flag
-        for (int i = 0; i < 2; ++i)
-        {
+        for (int i = 0; i < kKStages; ++i)
             mbar_wait(bar_kfull + 8 * i, 0, &quiet);
+        for (int i = 0; i < 2; ++i)
             mbar_wait(bar_mma + 8 * i, 0, &quiet);
-        }
     }
     tc_fence_before();
     __syncthreads();
@@ -531,18 +534,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 }
 
 bool make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
-              uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box_rows)
+              uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box_rows, uint32_t box_cols = KH,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B)
 {
     auto fn = encode_fn();
     if (!fn)
         return false;
     const cuuint64_t dims[3] = {d0, d1, d2};
     const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
-    const cuuint32_t box[3] = {KH, box_rows, 1};
+    const cuuint32_t box[3] = {box_cols, box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
-    return fn(map, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return fn(map, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <typename T>
@@ -553,10 +556,12 @@ int launch_tc(const void *q, const void *k, const uint32_t *q_lens, const uint32
     const CUtensorMapDataType dt =
         std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int64_t M = std::min<int64_t>(max_kv, S);
-    CUtensorMap mq, mk, mp;
+    CUtensorMap mq, mk, mp, mpw;
+    const int64_t m8 = std::max<int64_t>(M & ~int64_t(7), 8);
     if (!make_map(&mq, dt, q, HD, Qc, batch * Hq, HD * 2, Qc * HD * 2, BM) ||
         !make_map(&mk, dt, k, HD, S, batch * Hkv, HD * 2, S * HD * 2, BN) ||
-        !make_map(&mp, dt, qk, std::max<int64_t>(M & ~int64_t(7), 8), Qc, batch * Hq, S * 2, Qc * S * 2, BM))
+        !make_map(&mp, dt, qk, m8, Qc, batch * Hq, S * 2, Qc * S * 2, BM) ||
+        !make_map(&mpw, dt, qk, m8, Qc, batch * Hq, S * 2, Qc * S * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
         return set_error(L2K_ERR_CUDA, "l2k_prefill_attention_scores: tensor map encoding failed");
     // c = (1/sqrtf(128)) * log2(e): the oracle's fp32 scale, moved to base 2 for ex2.
     TcArgs a{q_lens, kv_lens, qk, Hq, Hq / Hkv, Hkv, Qc, S, M, M & ~int64_t(7), (int)ceil_div(max_q, BM),
@@ -566,7 +571,7 @@ int launch_tc(const void *q, const void *k, const uint32_t *q_lens, const uint32
     if (e != cudaSuccess)
         return set_error(L2K_ERR_CUDA, "l2k_prefill_attention_scores: %s", cudaGetErrorString(e));
     const int64_t grid = (int64_t)a.n_qt * batch * Hq;
-    kernel<<<(unsigned)grid, kThreads, kSmemBytes, stream>>>(mq, mk, mp, a);
+    kernel<<<(unsigned)grid, kThreads, kSmemBytes, stream>>>(mq, mk, mp, mpw, a);
     return check_launch("l2k_prefill_attention_scores (tcgen05)");
 }
 
