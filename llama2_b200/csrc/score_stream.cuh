@@ -41,8 +41,8 @@ namespace
 namespace cg = cooperative_groups;
 
 constexpr float kSoftmaxEps = 1e-6f;
-constexpr int kNS = 4;                 // ring stages
-constexpr int kCW = 8;                 // consumer warps (two per stage, one half-block each)
+constexpr int kNS = 3;                 // ring stages (3 CTAs of 64 KB fit one SM)
+constexpr int kCW = 2 * kNS;            // consumer warps (two per stage, one half-block each)
 constexpr int kBlockBytes = 16384;     // one key block
 constexpr int kStreamThreads = 32 * (kCW + 1);
 constexpr long long kWaitCycles = 4000000000LL; // ~2 s
