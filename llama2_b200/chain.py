@@ -42,6 +42,7 @@ class Packed:
         self.buf = torch.zeros(off, dtype=torch.uint8, device=device)
         if pin:
             self.buf = self.buf.pin_memory()
+        self.offsets = {name: o for (name, _, _), (o, _) in zip(specs, offs)}
         self.views = {name: self.buf[o:o + n].view(dt).view(shape)
                       for (name, shape, dt), (o, n) in zip(specs, offs)}
 
@@ -85,7 +86,8 @@ class Chain:
         self.ids, self.q_lens, self.kv_lens = self.inputs["ids"], self.inputs["q_lens"], self.inputs["kv_lens"]
         self.is_done, self.qkv, self.gate_up = self.inputs["is_done"], self.inputs["qkv"], self.inputs["gate_up"]
         self.kv_lens_initial = self.kv_lens.clone()
-        # results, packed (one device-to-host copy per step), and intermediates
+        # results, packed (the small ones in one device-to-host copy per step,
+        # the score rows last), and intermediates
         self.out_specs = [("max_lens", (2,), torch.uint32), ("normed", (t, d), dt), ("ffn_out", (t, f), dt),
                           ("qk", (b, h, qc, s), dt)]
         self.outputs = Packed(self.out_specs, self.device)
@@ -208,18 +210,38 @@ class Chain:
         for name, _, tdt in self.in_specs:
             hin[name].copy_(torch.from_numpy(np.ascontiguousarray(inputs[name])).to(tdt))
         hout = Packed(self.out_specs, "cpu", pin=True)
+        # A step writes keys [0, M) of every score row, M = the largest updated length.
+        kv = np.asarray(inputs["kv_lens"], np.int64) + np.asarray(inputs["q_lens"], np.int64)
+        self._m_written = int(min(kv.max() if kv.size else 0, self.w.kv_cache_len))
         self._pinned = (hin, hout)
         return hin, hout
 
     def e2e_bytes(self):
         hin, hout = self._pinned
-        return hin.buf.numel(), hout.buf.numel()
+        qk = self.qk
+        small = hout.offsets["qk"]
+        rows = qk.shape[0] * qk.shape[1] * qk.shape[2]
+        return hin.buf.numel(), small + rows * self._m_written * qk.element_size()
 
     def step_e2e(self):
         """One copy of the step's inputs to the device, the step (graph
-        replay), one copy of its results (lengths maxima, normed rows, scores,
-        SwiGLU output) back to pinned host memory."""
+        replay), then its results back to pinned host memory: one copy of the
+        lengths maxima, normed rows and SwiGLU output, and one 2-D copy of the
+        written part (keys [0, M)) of every score row."""
+        from cuda.bindings import runtime as cudart
+
         hin, hout = self._pinned
         self.inputs.buf.copy_(hin.buf, non_blocking=True)
         self.replay()
-        hout.buf.copy_(self.outputs.buf, non_blocking=True)
+        small = hout.offsets["qk"]
+        hout.buf[:small].copy_(self.outputs.buf[:small], non_blocking=True)
+        qk, hqk = self.qk, hout["qk"]
+        es = qk.element_size()
+        rows = qk.shape[0] * qk.shape[1] * qk.shape[2]
+        if self._m_written and rows:
+            pitch = qk.shape[3] * es
+            err, = cudart.cudaMemcpy2DAsync(hqk.data_ptr(), pitch, qk.data_ptr(), pitch, self._m_written * es, rows,
+                                            cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost,
+                                            torch.cuda.current_stream(self.device).cuda_stream)
+            if err != cudart.cudaError_t.cudaSuccess:
+                raise RuntimeError(f"score rows device-to-host copy failed: {err}")

@@ -1,25 +1,30 @@
 // Fused prefill attention scores on the 5th-generation tensor cores:
 //   P = softmax_causal(Q K^T / sqrt(128)),  bf16/f16 in, fp32 accumulate, bf16/f16 out.
 //
-// One CTA owns 128 query rows of one (seq, head); key tiles are 64 wide.
-// Warp roles (288 threads, two CTAs per SM):
+// One CTA owns 128 query rows of one (seq, head); key tiles are 128 wide, so
+// each tcgen05.mma is 128 x 128 x 16 (wide enough to keep the tensor pipe
+// efficient; two CTAs per SM still fit: 112 KB of shared memory, 256 TMEM
+// columns each).
+// Warp roles (288 threads):
 //   * warp 8 (control): TMA (cp.async.bulk.tensor, 128-byte swizzle) of the
-//     Q tile once and of K tiles through a 3-stage ring; tcgen05.mma
-//     (M=128, N=64, K=16 x 8) with both operands in shared memory and the
-//     fp32 accumulator in tensor memory (2 x 64 columns, double buffered);
+//     Q tile once and of K tiles (2 x 16 KB boxes) through a 2-stage ring;
+//     tcgen05.mma with both operands in shared memory and the fp32
+//     accumulator in tensor memory (2 x 128 columns, double buffered);
 //     tcgen05.commit signals "tile ready" on an mbarrier.
 //   * warps 0-7 (epilogue): warp w reads TMEM lanes 32*(w%4).. (its rows) and
-//     columns 32*(w/4).. of each tile with tcgen05.ld.
+//     columns 64*(w/4).. of each tile (two tcgen05.ld of 32 columns).
 //     Phase A walks the causally visible key tiles keeping an online row max
 //     and sum of exponentials (log2 units, ex2); phase B re-runs the MMAs
-//     and writes P = 2^(s*c - m) / (sum + 1e-6) once: each warp stages its
-//     32 x 32 block (64-byte swizzle) and TMA-stores it itself, so phase B
-//     has no CTA-wide barrier. Each finished tile frees its TMEM buffer
-//     through an mbarrier, so the MMA of the next tile overlaps.
-//   * Key tiles beyond the causal limit are TMA-stored from the zeroed staging
-//     region at the start (overlapping phase A). Keys >= max_kv are never
-//     written (the store map's extent; its 16-byte-rounded tail is written
-//     directly); tiles whose rows straddle q_len are written directly.
+//     and writes P = 2^(s*c - m) / (sum + 1e-6) once: each warp transposes
+//     its 32 x 32 blocks through 2 KB of shared memory (64-byte swizzle) and
+//     writes them with coalesced 16-byte stores (64 contiguous bytes per row).
+//     Each tile frees its TMEM buffer through an mbarrier as soon as it is in
+//     registers, so the MMA of the next tile overlaps.
+//   * Key columns beyond the causal limit are TMA-stored (128 x 64 boxes)
+//     from the zeroed staging region at the start, overlapping phase A. Keys
+//     >= max_kv are never written (the store map's extent; its 16-byte-rounded
+//     tail is written directly); tiles whose rows straddle q_len write only
+//     their valid rows.
 // CTA order is (seq, head)-major so the query tiles of one head run together
 // and share its K tiles in L2.
 // Every mbarrier wait is bounded (~2 s of clock cycles); on expiry the kernel
@@ -47,22 +52,25 @@ __device__ int g_device_error = 0; // first error code recorded by a kernel of t
 namespace
 {
 
-constexpr int BM = 128, BN = 64, HD = 128, KH = 64; // KH: elements per 128-byte swizzle row
+constexpr int BM = 128, BN = 128, HD = 128, KH = 64; // KH: elements per 128-byte swizzle row
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (kEpiWarps + 1);
 constexpr int kCtl = kEpiWarps;                        // control warp index
+constexpr int kColGroups = kEpiWarps / 4;              // epilogue warps per TMEM lane quadrant
+constexpr int kColsPerWarp = BN / kColGroups;          // 64
 constexpr uint32_t kQBox = 128 * 128;                  // 128 rows x 128 B
-constexpr uint32_t kKBox = 64 * 128;                   // 64 rows x 128 B
-constexpr int kKStages = 3;                            // K ring depth
+constexpr uint32_t kKBox = BN * 128;                   // 128 rows x 128 B
+constexpr int kKStages = 2;                            // K ring depth (32 KB per stage)
 constexpr uint32_t kWarpStage = 32 * 64;               // one warp's 32 x 32 block of P (64-byte rows)
 constexpr uint32_t kOffQ = 0;                          // 2 boxes (hd halves)
 constexpr uint32_t kOffK = kOffQ + 2 * kQBox;          // kKStages stages x 2 boxes
-constexpr uint32_t kOffP = kOffK + kKStages * 2 * kKBox; // 8 warp blocks = one zeroed 128 x 64 box at the start
+constexpr uint32_t kOffP = kOffK + kKStages * 2 * kKBox; // 8 warp blocks; the zeroed 128 x 64 box at the start;
+                                                       // the phase-A statistics at its end
 constexpr uint32_t kOffBar = kOffP + kEpiWarps * kWarpStage; // mbarriers
 constexpr uint32_t kOffMisc = kOffBar + 128;           // tmem slot, abort flag
-constexpr uint32_t kOffStats = kOffMisc + 64;          // 2 x 128 float2
-constexpr uint32_t kSmemBytes = kOffStats + 2 * 128 * 8 + 1024; // + alignment slack
+constexpr uint32_t kSmemBytes = kOffMisc + 64;         // the dynamic base is 1024-aligned (checked)
 constexpr uint32_t kTmemCols = 2 * BN;
+static_assert(kColGroups * 128 * 8 <= kEpiWarps * kWarpStage, "statistics fit the staging region");
 constexpr long long kWaitCycles = 4000000000LL;        // ~2 s at 2 GHz
 constexpr float kNegBig = -1e30f;
 
@@ -71,7 +79,8 @@ enum DevError
     ERR_WAIT_Q = 0x101,
     ERR_WAIT_K = 0x102,
     ERR_WAIT_MMA = 0x103,
-    ERR_WAIT_TMEM = 0x104
+    ERR_WAIT_TMEM = 0x104,
+    ERR_SMEM_ALIGN = 0x105
 };
 
 struct TcArgs
@@ -140,7 +149,6 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t sr
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -157,10 +165,10 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr)
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// kind::f16 instruction descriptor: D f32, A/B bf16 (1) or f16 (0), both K-major, M=128, N=BN.
-__host__ __device__ constexpr uint32_t instr_desc(uint32_t ab_format)
+// kind::f16 instruction descriptor: D f32, A/B bf16 (1) or f16 (0), both K-major, M=128, N=n.
+__host__ __device__ constexpr uint32_t instr_desc(uint32_t ab_format, uint32_t n)
 {
-    return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+    return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
@@ -176,10 +184,10 @@ __device__ __forceinline__ void mma_commit(uint32_t bar)
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// 32 consecutive fp32 accumulator columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+// 32 consecutive fp32 accumulator columns of this thread's TMEM lane (no
+// wait: follow with tmem_wait_ld before using r).
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32])
 {
-    uint32_t r[32];
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
                  "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
@@ -188,11 +196,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
                    "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
                    "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                  : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-        v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ float ex2(float x)
 {
@@ -230,19 +235,24 @@ __device__ __forceinline__ void fail(int code, volatile int *abort_flag)
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_scores_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                             const __grid_constant__ CUtensorMap tm_p, const __grid_constant__ CUtensorMap tm_pw,
-                             const TcArgs a)
+                             const __grid_constant__ CUtensorMap tm_p, const TcArgs a)
 {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t sbase = smem_u32(smem);
+    if (sbase & 1023u)
+    {
+        // the 128-byte-swizzled TMA boxes need a 1024-byte aligned base
+        if (threadIdx.x == 0)
+            atomicCAS(&g_device_error, 0, ERR_SMEM_ALIGN);
+        return;
+    }
     const uint32_t bar_q = sbase + kOffBar;
     const uint32_t bar_kfull = bar_q + 8;    // + 8 * stage (kKStages)
     const uint32_t bar_mma = bar_q + 32;     // + 8 * buffer: tile in TMEM buffer is ready
     const uint32_t bar_tfree = bar_q + 48;   // + 8 * buffer: epilogue finished with TMEM buffer
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffMisc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kOffMisc + 8);
-    float2 *stats = reinterpret_cast<float2 *>(smem + kOffStats); // [2][128]
+    float2 *stats = reinterpret_cast<float2 *>(smem + kOffP); // [kColGroups][128], after the zero stores
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t bh = blockIdx.x / a.n_qt;
@@ -256,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (row0 >= q_len)
         return; // no output rows in this tile (uniform over the CTA)
     const int rows_valid = (int)min((int64_t)BM, q_len - row0);
-    // TMA stores need whole 128-row tiles; their map covers keys [0, M8).
+    // Zero columns go out as TMA stores of whole 128-row boxes; that map covers keys [0, M8).
     const bool full_rows = rows_valid == BM && a.M8 > 0;
     const int64_t max_lim = min(kv_len - 1, hist + row0 + rows_valid - 1);
     const int64_t min_lim = min(kv_len - 1, hist + row0);
@@ -284,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     {
-        // the staging region starts as the zero 128 x 64 tile
+        // the staging region starts zeroed: the source of the zero-column stores
         uint4 *z = reinterpret_cast<uint4 *>(smem + kOffP);
         for (int i = tid; i < (int)(kEpiWarps * kWarpStage / 16); i += kThreads)
             z[i] = make_uint4(0, 0, 0, 0);
@@ -300,7 +310,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         // ================= control warp =================
         if (lane == 0 && n_steps > 0)
         {
-            const uint32_t idesc = instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u);
+            const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+            const uint32_t idesc_full = instr_desc(fmt, BN), idesc_half = instr_desc(fmt, BN / 2);
             const int kz = (int)(b * a.Hkv + kvh);
             auto issue_k = [&](int t) {
                 const int kt = t % n_a, st = t % kKStages;
@@ -319,6 +330,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             for (int t = 0; t < n_steps && !*abort_flag; ++t)
             {
                 const int st = t & 1, ks = t % kKStages; // TMEM buffer, K stage
+                const int kt = t % n_a;
                 if (!mbar_wait(bar_kfull + 8 * ks, (t / kKStages) & 1, abort_flag))
                 {
                     fail(ERR_WAIT_K, abort_flag);
@@ -332,6 +344,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                 tc_fence_after();
                 const uint32_t kb = sbase + kOffK + ks * 2 * kKBox;
                 const uint32_t d = tmem + (uint32_t)(st * BN);
+                // keys [BN/2, BN) of the tile masked for every row: half-width MMAs
+                const uint32_t idesc = max_lim < (int64_t)kt * BN + BN / 2 ? idesc_half : idesc_full;
 #pragma unroll
                 for (int k = 0; k < HD / 16; ++k)
                 {
@@ -340,36 +354,35 @@ __global__ void __launch_bounds__(kThreads, 2)
                     mma_f16(d, smem_desc(sbase + kOffQ + offa), smem_desc(kb + offb), idesc, k > 0 ? 1u : 0u);
                 }
                 mma_commit(bar_mma + 8 * st);
-                if (t >= 1 && t + 2 < n_steps)
+                if (t + kKStages < n_steps)
                 {
-                    // K stage (t - 1) % kKStages = (t + 2) % kKStages is free once
-                    // the previous tile's MMAs (long done) have read it
-                    if (!mbar_wait(bar_mma + 8 * ((t - 1) & 1), ((t - 1) >> 1) & 1, abort_flag))
+                    // the K stage is free once this tile's MMAs have read it
+                    if (!mbar_wait(bar_mma + 8 * st, (t >> 1) & 1, abort_flag))
                     {
                         fail(ERR_WAIT_MMA, abort_flag);
                         break;
                     }
-                    issue_k(t + 2);
+                    issue_k(t + kKStages);
                 }
-
             }
         }
     }
     else
     {
         // ================= epilogue warps =================
-        const int quad = warp & 3, ch = warp >> 2; // TMEM lanes 32*quad.., columns 32*ch..
+        const int quad = warp & 3, cg = warp >> 2; // TMEM lanes 32*quad.., columns 64*cg..
         const int r = quad * 32 + lane;            // row within the tile
         const int64_t lim_r = min(kv_len - 1, hist + row0 + r);
         float m = kNegBig, l = 0.f, inv = 0.f;     // log2-domain running max / sum
         uint16_t *qk16 = static_cast<uint16_t *>(a.qk);
         const int64_t row_off = (bh * a.Qc + row0 + r) * a.S;
+        uint8_t *wst = smem + kOffP + (uint32_t)warp * kWarpStage; // this warp's transpose buffer
 
         if (tid == 0 && full_rows)
         {
-            // zero key tiles beyond the causal limit, from staging buffer 0
-            for (int kt = n_a; kt < a.n_kt; ++kt)
-                tma_store_3d(&tm_p, sbase + kOffP, kt * BN, (int)row0, (int)bh);
+            // zero columns beyond the causal limit, 128 x 64 boxes from the zeroed region
+            for (int64_t x = (int64_t)n_a * BN; x < a.M; x += KH)
+                tma_store_3d(&tm_p, sbase + kOffP, (int)x, (int)row0, (int)bh);
             bulk_commit();
         }
 
@@ -377,122 +390,139 @@ __global__ void __launch_bounds__(kThreads, 2)
         {
             const int st = t & 1;
             // After a failure the remaining steps run on whatever TMEM holds (the
-            // error is recorded); no warp leaves early, so the named barriers below
-            // are met by all epilogue warps.
+            // error is recorded); no warp leaves early, so the named barrier below
+            // is met by all epilogue warps.
             if (!mbar_wait(bar_mma + 8 * st, (t >> 1) & 1, abort_flag))
                 fail(ERR_WAIT_MMA, abort_flag);
             tc_fence_after();
             const bool phase_b = t >= n_a;
             const int kt = phase_b ? t - n_a : t;
-            const int64_t key0 = (int64_t)kt * BN + ch * 32;
-            const bool masked = (int64_t)kt * BN + BN - 1 > min_lim;
-            float v[32];
-            tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(st * BN + ch * 32), v);
+            const int64_t key0 = (int64_t)kt * BN + cg * kColsPerWarp;
+            uint32_t raw0[32], raw1[32];
+            const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(st * BN + cg * kColsPerWarp);
+            tmem_ld32_async(taddr, raw0);
+            tmem_ld32_async(taddr + 32, raw1);
+            tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(bar_tfree + 8 * st); // the TMEM buffer may take the next tile
-            if (masked)
-            {
+            float v[64];
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    v[j] = key0 + j <= lim_r ? v[j] : -INFINITY;
+            for (int j = 0; j < 32; ++j)
+            {
+                v[j] = __uint_as_float(raw0[j]);
+                v[32 + j] = __uint_as_float(raw1[j]);
+            }
+            if ((int64_t)kt * BN + BN - 1 > min_lim)
+            {
+                // keys past this row's limit (tile-uniform test, 32-bit compares)
+                const int64_t vis64 = lim_r - key0 + 1;
+                const int vis = (int)max((int64_t)0, min((int64_t)64, vis64));
+#pragma unroll
+                for (int j = 0; j < 64; ++j)
+                    v[j] = j < vis ? v[j] : -INFINITY;
             }
             if (!phase_b)
             {
                 float tmax = -INFINITY;
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
+                for (int j = 0; j < 64; ++j)
                     tmax = fmaxf(tmax, v[j]);
                 const float m_new = fmaxf(m, tmax * a.c);
-                float sum = 0.f;
+                float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    sum += ex2(fmaf(v[j], a.c, -m_new));
-                l = l * ex2(m - m_new) + sum;
+                for (int j = 0; j < 64; j += 2)
+                {
+                    sum0 += ex2(fmaf(v[j], a.c, -m_new));
+                    sum1 += ex2(fmaf(v[j + 1], a.c, -m_new));
+                }
+                l = l * ex2(m - m_new) + (sum0 + sum1);
                 m = m_new;
                 if (t == n_a - 1)
                 {
-                    stats[ch * 128 + r] = make_float2(m, l);
+                    // The statistics go to the staging region once the zero-column
+                    // stores have read it.
                     if (tid == 0)
-                        bulk_wait_read_0(); // the zero-tile stores are done with staging buffer 0
+                        bulk_wait_read_0();
                     epi_sync();
-                    const float2 s0 = stats[r], s1 = stats[128 + r];
-                    const float Mx = fmaxf(s0.x, s1.x);
-                    const float L = s0.y * ex2(s0.x - Mx) + s1.y * ex2(s1.x - Mx);
+                    stats[cg * 128 + r] = make_float2(m, l);
+                    epi_sync();
+                    float Mx = stats[r].x;
+#pragma unroll
+                    for (int g = 1; g < kColGroups; ++g)
+                        Mx = fmaxf(Mx, stats[g * 128 + r].x);
+                    float L = 0.f;
+#pragma unroll
+                    for (int g = 0; g < kColGroups; ++g)
+                    {
+                        const float2 sg = stats[g * 128 + r];
+                        L += sg.y * ex2(sg.x - Mx);
+                    }
                     m = Mx;
                     inv = __frcp_rn(__fadd_rn(L, 1e-6f));
+                    epi_sync(); // every row's statistics read before the region becomes staging again
                 }
                 continue;
             }
-            uint32_t packed[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2)
-                packed[j / 2] = pack2<T>(ex2(fmaf(v[j], a.c, -m)) * inv, ex2(fmaf(v[j + 1], a.c, -m)) * inv);
-            if (full_rows)
+            for (int hh = 0; hh < 2; ++hh)
             {
-                // This warp's 32 x 32 block (rows quad*32.., keys key0..) staged with
-                // the 64-byte swizzle (16-byte chunk c of row r at c ^ ((r / 2) % 4))
-                // and stored by the warp itself.
-                uint8_t *wst = smem + kOffP + (uint32_t)warp * kWarpStage;
-                if (lane == 0)
-                    bulk_wait_read_0(); // this warp's previous store has read the block
-                __syncwarp();
-                uint8_t *dst = wst + (uint32_t)lane * 64;
+                uint32_t packed[16];
+#pragma unroll
+                for (int j = 0; j < 32; j += 2)
+                    packed[j / 2] = pack2<T>(ex2(fmaf(v[hh * 32 + j], a.c, -m)) * inv,
+                                             ex2(fmaf(v[hh * 32 + j + 1], a.c, -m)) * inv);
+                // Transpose this 32 x 32 block through shared memory: lane = row,
+                // 16-byte chunk c of a row at c ^ ((row / 2) % 4) (conflict-free both ways),
+                // then each store instruction writes 8 rows x 64 contiguous bytes.
+                __syncwarp(); // the previous block has been read back
+                uint8_t *mine = wst + (uint32_t)lane * 64;
 #pragma unroll
                 for (int c4 = 0; c4 < 4; ++c4)
-                    *reinterpret_cast<uint4 *>(dst + ((c4 ^ ((lane >> 1) & 3)) * 16)) =
+                    *reinterpret_cast<uint4 *>(mine + ((c4 ^ ((lane >> 1) & 3)) * 16)) =
                         make_uint4(packed[4 * c4], packed[4 * c4 + 1], packed[4 * c4 + 2], packed[4 * c4 + 3]);
-                if (key0 + 32 > a.M8 && key0 < a.M)
-                {
-                    // keys [M8, M) are beyond the store map: written directly
-#pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (key0 + e >= a.M8 && key0 + e < a.M)
-                            qk16[row_off + key0 + e] = half_of(packed[e / 2], e & 1);
-                }
-                fence_proxy_async();
                 __syncwarp();
-                if (lane == 0)
-                {
-                    tma_store_3d(&tm_pw, smem_u32(wst), (int)key0, (int)(row0 + quad * 32), (int)bh);
-                    bulk_commit();
-                }
-            }
-            else if (r < rows_valid)
-            {
+                const int64_t col0 = key0 + hh * 32;
 #pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4)
+                for (int i = 0; i < 4; ++i)
                 {
-                    const int64_t col = key0 + c4 * 8;
-                    if (col + 8 <= a.M)
-                        *reinterpret_cast<uint4 *>(qk16 + row_off + col) =
-                            make_uint4(packed[4 * c4], packed[4 * c4 + 1], packed[4 * c4 + 2], packed[4 * c4 + 3]);
-                    else
+                    const int rr = i * 8 + (lane >> 2), c = lane & 3;
+                    const uint4 val = *reinterpret_cast<const uint4 *>(wst + rr * 64 + ((c ^ ((rr >> 1) & 3)) * 16));
+                    const int row = quad * 32 + rr;
+                    const int64_t col = col0 + c * 8;
+                    if (row < rows_valid && col < a.M)
                     {
+                        uint16_t *dst = qk16 + (bh * a.Qc + row0 + row) * a.S + col;
+                        if (col + 8 <= a.M)
+                            *reinterpret_cast<uint4 *>(dst) = val;
+                        else
+                        {
+                            const uint32_t w4[4] = {val.x, val.y, val.z, val.w};
 #pragma unroll
-                        for (int e = 0; e < 8; ++e)
-                            if (col + e < a.M)
-                                qk16[row_off + col + e] = half_of(packed[4 * c4 + e / 2], e & 1);
+                            for (int e = 0; e < 8; ++e)
+                                if (col + e < a.M)
+                                    dst[e] = half_of(w4[e / 2], e & 1);
+                        }
                     }
                 }
             }
         }
 
-        // Zero tails: keys [M8, M) of the zero tiles of full-row tiles, and
-        // every zero key of tiles whose rows straddle q_len.
+        // Zero tails: keys [M8, M) beyond the zero-column stores' map, and every
+        // zero key of tiles whose rows straddle q_len.
         if (full_rows && a.M8 < a.M && (int64_t)n_a * BN < a.M)
         {
-            for (int64_t j = max(a.M8, (int64_t)n_a * BN) + ch; j < a.M; j += 2)
+            for (int64_t j = max(a.M8, (int64_t)n_a * BN) + cg; j < a.M; j += kColGroups)
                 qk16[row_off + j] = 0;
         }
         if (!full_rows && r < rows_valid)
         {
-            for (int64_t j = (int64_t)n_a * BN + ch; j < a.M; j += 2)
+            for (int64_t j = (int64_t)n_a * BN + cg; j < a.M; j += kColGroups)
                 qk16[row_off + j] = 0;
         }
-        if (lane == 0)
-            bulk_wait_all(); // this warp's stores (and, for warp 0, the zero tiles)
+        if (tid == 0)
+            bulk_wait_all(); // the zero-column stores
     }
 
     // -------- teardown --------
@@ -556,12 +586,11 @@ int launch_tc(const void *q, const void *k, const uint32_t *q_lens, const uint32
     const CUtensorMapDataType dt =
         std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int64_t M = std::min<int64_t>(max_kv, S);
-    CUtensorMap mq, mk, mp, mpw;
+    CUtensorMap mq, mk, mp;
     const int64_t m8 = std::max<int64_t>(M & ~int64_t(7), 8);
     if (!make_map(&mq, dt, q, HD, Qc, batch * Hq, HD * 2, Qc * HD * 2, BM) ||
         !make_map(&mk, dt, k, HD, S, batch * Hkv, HD * 2, S * HD * 2, BN) ||
-        !make_map(&mp, dt, qk, m8, Qc, batch * Hq, S * 2, Qc * S * 2, BM) ||
-        !make_map(&mpw, dt, qk, m8, Qc, batch * Hq, S * 2, Qc * S * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+        !make_map(&mp, dt, qk, m8, Qc, batch * Hq, S * 2, Qc * S * 2, BM))
         return set_error(L2K_ERR_CUDA, "l2k_prefill_attention_scores: tensor map encoding failed");
     // c = (1/sqrtf(128)) * log2(e): the oracle's fp32 scale, moved to base 2 for ex2.
     TcArgs a{q_lens, kv_lens, qk, Hq, Hq / Hkv, Hkv, Qc, S, M, M & ~int64_t(7), (int)ceil_div(max_q, BM),
@@ -571,7 +600,7 @@ int launch_tc(const void *q, const void *k, const uint32_t *q_lens, const uint32
     if (e != cudaSuccess)
         return set_error(L2K_ERR_CUDA, "l2k_prefill_attention_scores: %s", cudaGetErrorString(e));
     const int64_t grid = (int64_t)a.n_qt * batch * Hq;
-    kernel<<<(unsigned)grid, kThreads, kSmemBytes, stream>>>(mq, mk, mp, mpw, a);
+    kernel<<<(unsigned)grid, kThreads, kSmemBytes, stream>>>(mq, mk, mp, a);
     return check_launch("l2k_prefill_attention_scores (tcgen05)");
 }
 

@@ -118,3 +118,26 @@ def test_graph_replay_matches_eager():
     ref = ochain.decode_step(w, inp)
     assert max_rel_err(host(ch.qk), ref["qk"]) <= 1e-5
     assert bits_equal(host(ch.k_cache), ref["k"])
+
+
+@pytest.mark.parametrize("name,batch", [("7b-b1", 1), ("7b-b64-bf16", 3)])
+def test_end_to_end_step_reads_back_results(name, batch):
+    """step_e2e: one packed upload, the step, the results back on the host —
+    the score rows' written keys [0, M) and the small outputs, equal to the
+    device's."""
+    w = with_batch(WORKLOADS[name], batch)
+    inp = host_inputs(w, seed=9)
+    ch = Chain(w, inp)
+    ch.capture()
+    hin, hout = ch.host_buffers(inp)
+    ch.step_e2e()
+    torch.cuda.synchronize()
+    m = ch._m_written
+    assert m == min(int((inp["kv_lens"].astype(np.int64) + 1).max()), w.kv_cache_len)
+    assert bits_equal(host(hout["qk"])[..., :m], host(ch.qk)[..., :m])
+    for n in ("normed", "ffn_out", "max_lens"):
+        assert bits_equal(host(hout[n]), host(getattr(ch, n))), n
+    ref = ochain.decode_step(w, inp)
+    assert max_rel_err(host(hout["qk"])[..., :m], ref["qk"][..., :m]) <= REL[w.dtype]
+    h2d, d2h = ch.e2e_bytes()
+    assert h2d == hin.buf.numel() and d2h < hout.buf.numel()
