@@ -15,7 +15,7 @@
 //     columns 64*(w/4).. of each tile (two tcgen05.ld of 32 columns).
 //     Phase A walks the causally visible key tiles keeping an online row max
 //     and sum of exponentials (log2 units, ex2); phase B re-runs the MMAs
-//     and writes P = 2^(s*c - m) / (sum + 1e-6) once: each warp transposes
+//     and writes P = 2^(s*c - m - log2(sum + 1e-6)) once: each warp transposes
 //     its 32 x 32 blocks through 2 KB of shared memory (64-byte swizzle) and
 //     writes them with coalesced 16-byte stores (64 contiguous bytes per row).
 //     Each tile frees its TMEM buffer through an mbarrier as soon as it is in
@@ -373,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int quad = warp & 3, cg = warp >> 2; // TMEM lanes 32*quad.., columns 64*cg..
         const int r = quad * 32 + lane;            // row within the tile
         const int64_t lim_r = min(kv_len - 1, hist + row0 + r);
-        float m = kNegBig, l = 0.f, inv = 0.f;     // log2-domain running max / sum
+        float m = kNegBig, l = 0.f;                // log2-domain running max / sum
         uint16_t *qk16 = static_cast<uint16_t *>(a.qk);
         const int64_t row_off = (bh * a.Qc + row0 + r) * a.S;
         uint8_t *wst = smem + kOffP + (uint32_t)warp * kWarpStage; // this warp's transpose buffer
@@ -459,8 +459,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                         const float2 sg = stats[g * 128 + r];
                         L += sg.y * ex2(sg.x - Mx);
                     }
-                    m = Mx;
-                    inv = __frcp_rn(__fadd_rn(L, 1e-6f));
+                    // phase B: p = 2^(s*c - m) / (L + eps) = 2^(s*c - (m + log2(L + eps)))
+                    m = __fadd_rn(Mx, log2f(__fadd_rn(L, 1e-6f)));
                     epi_sync(); // every row's statistics read before the region becomes staging again
                 }
                 continue;
@@ -471,8 +471,7 @@ __global__ void __launch_bounds__(kThreads, 2)
                 uint32_t packed[16];
 #pragma unroll
                 for (int j = 0; j < 32; j += 2)
-                    packed[j / 2] = pack2<T>(ex2(fmaf(v[hh * 32 + j], a.c, -m)) * inv,
-                                             ex2(fmaf(v[hh * 32 + j + 1], a.c, -m)) * inv);
+                    packed[j / 2] = pack2<T>(ex2(fmaf(v[hh * 32 + j], a.c, -m)), ex2(fmaf(v[hh * 32 + j + 1], a.c, -m)));
                 // Transpose this 32 x 32 block through shared memory: lane = row,
                 // 16-byte chunk c of a row at c ^ ((row / 2) % 4) (conflict-free both ways),
                 // then each store instruction writes 8 rows x 64 contiguous bytes.

@@ -284,6 +284,25 @@ __device__ __forceinline__ void step_ticket(const StepRowArgs &sa, int lane, boo
         step_update_lens(sa, lane, have, pq, pkv);
 }
 
+// L2 prefetch of this rank's first two key blocks of the (b, kv head) plane,
+// issued before the lengths are known (they are needed to know how many
+// blocks there are): the blocks exist whatever the length, and the copies
+// that follow find them in L2 instead of waiting a DRAM round trip.
+template <int KB, int ROW_BYTES>
+__device__ __forceinline__ void prefetch_first_blocks(const DecodeArgs &a, int64_t b, int64_t kvh, int c, int C)
+{
+    const char *plane = static_cast<const char *>(a.k) + (b * a.Hkv + kvh) * a.S * (int64_t)ROW_BYTES;
+    for (int i = 0; i < 2; ++i)
+    {
+        const int64_t g = c + (int64_t)C * i;
+        if (g * KB >= a.S)
+            break;
+        const uint32_t bytes = (uint32_t)(min((int64_t)KB, a.S - g * KB) * ROW_BYTES);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(plane + g * KB * ROW_BYTES), "r"(bytes)
+                     : "memory");
+    }
+}
+
 // One score row on this CTA's share of its keys (see the file comment).
 // head_dim * sizeof(T) = LPR * 16 bytes, LPR in {4, 8, 16, 32}. Every CTA of
 // the cluster calls it for the same row. `err` receives the first timeout
@@ -354,10 +373,15 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
             for (int64_t b = tid; b < sa.batch; b += kCW * 32)
                 mx_kv = max(mx_kv, sa.kv_lens[b] + sa.q_lens[b]);
         }
-        else if (sa.batch <= 32 && lane < sa.batch)
+        else
         {
-            pq = sa.q_lens[lane];
-            pkv = sa.kv_lens[lane];
+            if (sa.batch <= 32 && lane < sa.batch)
+            {
+                pq = sa.q_lens[lane];
+                pkv = sa.kv_lens[lane];
+            }
+            if (lane == 0)
+                prefetch_first_blocks<KB, ROW_BYTES>(a, ri.b, ri.h / a.group, c, C);
         }
         kv_new = kvl + ql;
         pos = kv_new - 1u;
@@ -368,6 +392,11 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
     }
     else
     {
+        if (warp == kCW && lane == 0)
+        {
+            const int64_t bh = row / a.Qc, b = bh / a.Hq;
+            prefetch_first_blocks<KB, ROW_BYTES>(a, b, (bh - b * a.Hq) / a.group, c, C);
+        }
         ri = row_info(a, row);
         if (!ri.active)
         {
