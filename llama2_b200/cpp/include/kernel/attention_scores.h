@@ -18,3 +18,20 @@ template <typename T>
 void launch_prefill_attention_scores(const Tensor<T> &q, const Tensor<T> &k, const Tensor<unsigned int> &q_lens,
                                      const Tensor<unsigned int> &kv_lens, const unsigned int max_q_len,
                                      const unsigned int max_kv_len, Tensor<T> &qk);
+
+// The whole decode chain of one layer step in one launch (no counterpart in
+// the reference): kv_lens += q_lens and max_lens = (max q_len, max kv_len);
+// x = embed_table[input_ids]; normed = RMSNorm(x) with norm_weight; RoPE of
+// q and k at kv_len - 1 ((i, i + hd/2) pairs when llama2_pairs, (2i, 2i+1)
+// otherwise) with the K/V rows appended to the caches (skipped for
+// is_done); qk = softmax over keys 0..kv_len-1; ffn_out = silu(gate) * up.
+// Same results as running those operators one after another. Uses the
+// library's static scratch (l2k_decode_step_no_alloc): steps on one device
+// must not overlap, which the legacy default stream guarantees.
+template <typename T>
+void launch_decode_step(const Tensor<unsigned int> &q_lens, Tensor<unsigned int> &kv_lens,
+                        Tensor<unsigned int> &max_lens, const Tensor<unsigned int> &input_ids,
+                        const Tensor<T> &embed_table, const Tensor<T> &norm_weight, Tensor<T> &x, Tensor<T> &normed,
+                        const Tensor<T> &qkv, const Tensor<unsigned char> &is_done, Tensor<T> &q, Tensor<T> &k_cache,
+                        Tensor<T> &v_cache, Tensor<T> &qk, const Tensor<T> &gate_up, Tensor<T> &ffn_out,
+                        bool llama2_pairs);

@@ -329,6 +329,51 @@ void launch_prefill_attention_scores(const Tensor<T> &q, const Tensor<T> &k, con
           "launch_prefill_attention_scores");
 }
 
+template <typename T>
+void launch_decode_step(const Tensor<unsigned int> &q_lens, Tensor<unsigned int> &kv_lens,
+                        Tensor<unsigned int> &max_lens, const Tensor<unsigned int> &input_ids,
+                        const Tensor<T> &embed_table, const Tensor<T> &norm_weight, Tensor<T> &x, Tensor<T> &normed,
+                        const Tensor<T> &qkv, const Tensor<unsigned char> &is_done, Tensor<T> &q, Tensor<T> &k_cache,
+                        Tensor<T> &v_cache, Tensor<T> &qk, const Tensor<T> &gate_up, Tensor<T> &ffn_out,
+                        bool llama2_pairs)
+{
+    const unsigned int b = input_ids.shape()[0];
+    const unsigned int hq = q.shape()[1], hd = q.shape()[3], hkv = k_cache.shape()[1], s = k_cache.shape()[2];
+    require(q.shape()[0] == b && q.shape()[2] == 1, "Incorrect q size");
+    require(qk.shape()[0] == b && qk.shape()[1] == hq && qk.shape()[3] == s, "Incorrect qk size");
+    require(max_lens.numel() >= 2, "max_lens needs two elements");
+    l2k_decode_step_args a = {};
+    a.q_lens = q_lens.data();
+    a.kv_lens = kv_lens.data();
+    a.max_lens = max_lens.data();
+    a.input_ids = input_ids.data();
+    a.embed_table = embed_table.data();
+    a.norm_weight = norm_weight.data();
+    a.x = x.data();
+    a.normed = normed.data();
+    a.qkv = qkv.data();
+    a.is_done = is_done.data();
+    a.q = q.data();
+    a.k_cache = k_cache.data();
+    a.v_cache = v_cache.data();
+    a.qk = qk.data();
+    a.rope_table = rope_table(hd);
+    a.rope_table_positions = kRopePositions;
+    a.gate_up = gate_up.data();
+    a.ffn_out = ffn_out.data();
+    a.batch = b;
+    a.vocab_size = embed_table.shape()[0];
+    a.dim = embed_table.shape()[1];
+    a.q_head_num = hq;
+    a.kv_head_num = hkv;
+    a.head_dim = hd;
+    a.kv_cache_len = s;
+    a.hidden = ffn_out.shape()[1];
+    a.pairing = llama2_pairs ? L2K_ROPE_HALF : L2K_ROPE_INTERLEAVED;
+    a.dtype = dtype_of<T>();
+    check(l2k_decode_step_no_alloc(&a, nullptr), "launch_decode_step");
+}
+
 // Explicit instantiations: float, half and bfloat16, as the reference
 // instantiates float and half (e.g. src/kernel/embedding.cu:51-56).
 #define L2K_INSTANTIATE(T)                                                                                          \
@@ -363,7 +408,12 @@ void launch_prefill_attention_scores(const Tensor<T> &q, const Tensor<T> &k, con
                                                     Tensor<T> &);                                                   \
     template void launch_prefill_attention_scores<T>(const Tensor<T> &, const Tensor<T> &,                          \
                                                      const Tensor<unsigned int> &, const Tensor<unsigned int> &,    \
-                                                     const unsigned int, const unsigned int, Tensor<T> &);
+                                                     const unsigned int, const unsigned int, Tensor<T> &);          \
+    template void launch_decode_step<T>(const Tensor<unsigned int> &, Tensor<unsigned int> &,                       \
+                                        Tensor<unsigned int> &, const Tensor<unsigned int> &, const Tensor<T> &,    \
+                                        const Tensor<T> &, Tensor<T> &, Tensor<T> &, const Tensor<T> &,             \
+                                        const Tensor<unsigned char> &, Tensor<T> &, Tensor<T> &, Tensor<T> &,       \
+                                        Tensor<T> &, const Tensor<T> &, Tensor<T> &, bool);
 
 L2K_INSTANTIATE(float)
 L2K_INSTANTIATE(half)

@@ -46,6 +46,8 @@ void orc_qk_scores(const float *, const float *, int64_t, int64_t, int64_t, int6
 void orc_masked_attention_score(float *, const uint8_t *, const uint32_t *, int64_t, int64_t, int64_t, int64_t,
                                 int64_t, int64_t);
 void orc_swiglu(const float *, int64_t, int64_t, float *);
+void orc_embedding(const uint32_t *, int64_t, const void *, int64_t, int64_t, void *);
+void orc_update_q_kv_lens(const uint32_t *, uint32_t *, int64_t, uint32_t *, uint32_t *);
 }
 
 // ---------------------------------------------------------------------------
@@ -409,6 +411,71 @@ TEST(DecodeAttentionScoresTest, Fp32)
     orc_build_intended_mask(ones.data(), kv.data(), b, 1, 1000, 1, s, mask.data());
     orc_masked_attention_score(e.data(), mask.data(), ones.data(), b, h, 1, s, 1000, hd);
     EXPECT_TRUE(max_rel(download(qk_d), e) <= 1e-5f);
+}
+
+TEST(DecodeStepTest, WholeChainOneLaunch)
+{
+    // The fused step against the oracle composition of the operators it replaces.
+    const unsigned int b = 2, h = 4, hd = 128, s = 256, d = h * hd, f = 768, vocab = 1000;
+    std::mt19937 gen(11);
+    std::normal_distribution<float> nd(0.f, 1.f);
+    auto rnd = [&](size_t n, float sc) {
+        std::vector<float> v(n);
+        for (auto &e : v)
+            e = nd(gen) * sc;
+        return v;
+    };
+    std::vector<float> table = rnd((size_t)vocab * d, 0.02f), w(d), qkv = rnd((size_t)b * 3 * d, 1.f),
+                       gate_up = rnd((size_t)b * 2 * f, 1.f), kc = rnd((size_t)b * h * s * hd, 1.f),
+                       vc = rnd((size_t)b * h * s * hd, 1.f);
+    for (unsigned int i = 0; i < d; ++i)
+        w[i] = 0.5f + (float)(i % 97) / 97.f;
+    std::vector<unsigned int> ids = {7, 998}, ql = {1, 1}, kv = {100, 255};
+    std::vector<unsigned char> done = {0, 0};
+    Tensor<float> table_d({vocab, d}, GPU), w_d({d}, GPU), x_d({b, d}, GPU), n_d({b, d}, GPU), qkv_d({b, 3 * d}, GPU),
+        q_d({b, h, 1, hd}, GPU), k_d({b, h, s, hd}, GPU), v_d({b, h, s, hd}, GPU), qk_d({b, h, 1, s}, GPU),
+        gu_d({b, 2 * f}, GPU), ffn_d({b, f}, GPU);
+    Tensor<unsigned int> ids_d({b}, GPU), ql_d({b}, GPU), kv_d({b}, GPU), ml_d({2}, GPU);
+    Tensor<unsigned char> done_d({b}, GPU);
+    upload(table_d, table);
+    upload(w_d, w);
+    upload(qkv_d, qkv);
+    upload(gu_d, gate_up);
+    upload(k_d, kc);
+    upload(v_d, vc);
+    upload(ids_d, ids);
+    upload(ql_d, ql);
+    upload(kv_d, kv);
+    upload(done_d, done);
+    launch_decode_step(ql_d, kv_d, ml_d, ids_d, table_d, w_d, x_d, n_d, qkv_d, done_d, q_d, k_d, v_d, qk_d, gu_d,
+                       ffn_d, true);
+    // expectations
+    std::vector<unsigned int> kv_e = kv, mq(1), mkv(1);
+    orc_update_q_kv_lens(ql.data(), kv_e.data(), b, mq.data(), mkv.data());
+    std::vector<float> x_e((size_t)b * d), res((size_t)b * d, 0.f), n_e((size_t)b * d);
+    orc_embedding(ids.data(), b, table.data(), d, 4, x_e.data());
+    std::vector<float> xa((size_t)b * d);
+    orc_fused_add_residual_rmsnorm(x_e.data(), res.data(), w.data(), b, d, 0, xa.data(), n_e.data());
+    std::vector<float> q_e((size_t)b * h * hd, 0.f), k_e = kc, v_e = vc;
+    orc_rope_kvcache_decode(1, qkv.data(), done.data(), kv_e.data(), b, h, h, hd, s, q_e.data(), k_e.data(),
+                            v_e.data());
+    std::vector<float> qk_e((size_t)b * h * s, 0.f);
+    orc_qk_scores(q_e.data(), k_e.data(), b, h, h, 1, s, hd, 1, mkv[0], qk_e.data());
+    std::vector<uint8_t> mask((size_t)b * s, 0);
+    orc_build_intended_mask(ql.data(), kv_e.data(), b, 1, mkv[0], 1, s, mask.data());
+    orc_masked_attention_score(qk_e.data(), mask.data(), ql.data(), b, h, 1, s, mkv[0], hd);
+    std::vector<float> ffn_e((size_t)b * f);
+    orc_swiglu(gate_up.data(), b, f, ffn_e.data());
+    EXPECT_TRUE(download(kv_d) == kv_e);
+    const std::vector<unsigned int> ml = download(ml_d);
+    EXPECT_TRUE(ml[0] == mq[0] && ml[1] == mkv[0]);
+    EXPECT_TRUE(download(x_d) == x_e);
+    EXPECT_TRUE(max_rel(download(n_d), n_e) <= 1e-5f);
+    EXPECT_TRUE(download(q_d) == q_e);
+    EXPECT_TRUE(download(k_d) == k_e);
+    EXPECT_TRUE(download(v_d) == v_e);
+    EXPECT_TRUE(max_rel(download(qk_d), qk_e) <= 1e-5f);
+    EXPECT_TRUE(max_rel(download(ffn_d), ffn_e) <= 1e-5f);
 }
 
 int main()
