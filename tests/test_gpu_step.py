@@ -160,3 +160,54 @@ def test_unsupported_head_size_runs_operator_sequence():
     ch = Chain(WORKLOADS["tiny"], host_inputs(WORKLOADS["tiny"], seed=0))
     assert not ch.fused
     assert ch.kernels_per_step() == 6
+
+
+@pytest.mark.parametrize("dtype,hd,pairing,S", [
+    (torch.float32, 64, 1, 700),    # 256-byte K rows
+    (torch.float32, 32, 0, 300),    # 128-byte K rows
+    (torch.float16, 64, 0, 1000),   # 128-byte K rows, 16-bit
+    (torch.bfloat16, 256, 1, 512),  # 512-byte K rows, 16-bit
+    (torch.float16, 32, 1, 2048),   # 64-byte K rows
+])
+def test_row_widths_against_operator_sequence(dtype, hd, pairing, S):
+    """Every K-row width the fused step takes (64 to 512 bytes: the four
+    streaming-row instantiations), both pairings, against the operator
+    sequence on the same buffers."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(hd * 7 + S)
+    B, H, F, V = 3, 4, 256, 500
+    D = H * hd
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(dtype)
+
+    base = dict(q_lens=torch.ones(B, dtype=torch.uint32, device=dev),
+                input_ids=torch.tensor([3, 499, 250], dtype=torch.uint32, device=dev),
+                embed_table=rnd(V, D, scale=0.02), norm_weight=(torch.rand(D, generator=g, device=dev) + 0.5).to(dtype),
+                qkv=rnd(B, 3 * D), is_done=torch.tensor([0, 1, 0], dtype=torch.uint8, device=dev), gate_up=rnd(B, 2 * F))
+    kv0 = torch.tensor([S // 2, 5, S - 1], dtype=torch.uint32, device=dev)
+    k0, v0 = rnd(B, H, S, hd), rnd(B, H, S, hd)
+
+    def fresh():
+        return dict(kv_lens=kv0.clone(), max_lens=torch.zeros(2, dtype=torch.uint32, device=dev),
+                    x=torch.empty(B, D, dtype=dtype, device=dev), normed=torch.empty(B, D, dtype=dtype, device=dev),
+                    q=torch.zeros(B, H, 1, hd, dtype=dtype, device=dev), k_cache=k0.clone(), v_cache=v0.clone(),
+                    qk=torch.full((B, H, 1, S), 7.0, dtype=dtype, device=dev),
+                    ffn_out=torch.empty(B, F, dtype=dtype, device=dev))
+
+    f = fresh()
+    assert ops.decode_step_supported(**base, **f, pairing=pairing)
+    ops.decode_step(**base, **f, workspace=ops.decode_step_workspace(dev), pairing=pairing)
+    u = fresh()
+    ops.launch_update_q_kv_lens(base["q_lens"], u["kv_lens"], u["max_lens"][0:1], u["max_lens"][1:2])
+    ops.launch_embedding(base["input_ids"], base["embed_table"], u["x"])
+    ops.launch_fused_add_residual_rmsnorm(base["norm_weight"], u["x"], u["normed"], False)
+    rope = ops.launch_fused_reshape_rope_kvcache_llama2_decode if pairing else ops.launch_fused_reshape_rope_kvcache_decode
+    rope(base["qkv"], base["is_done"], u["kv_lens"], u["q"], u["k_cache"], u["v_cache"])
+    ops.decode_attention_scores(u["q"], u["k_cache"], u["kv_lens"], u["max_lens"][1:2], u["qk"])
+    ops.launch_swiglu(base["gate_up"], u["ffn_out"])
+    torch.cuda.synchronize()
+    for n in ("kv_lens", "max_lens", "x", "q", "k_cache", "v_cache", "qk", "ffn_out"):
+        assert bits_equal(host(f[n]), host(u[n])), n
+    assert max_rel_err(host(f["normed"]), host(u["normed"])) <= (1e-5 if dtype == torch.float32 else 1e-2)
