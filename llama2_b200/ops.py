@@ -381,5 +381,6 @@ def decode_step_no_alloc(*, q_lens, kv_lens, max_lens, input_ids, embed_table, n
 def decode_step_supported(**kw) -> bool:
     """Whether decode_step takes these tensors (shape and alignment support)."""
     kw.pop("workspace", None)
+    kw.setdefault("use_table", True)
     args = _decode_step_args(**kw)
     return capi.lib().l2k_decode_step_supported(ctypes.byref(args)) == 0
