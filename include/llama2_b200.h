@@ -234,6 +234,21 @@ int l2k_swiglu(const void *input, void *output, int64_t num_tokens, int64_t inte
                l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Transpose + unpad of the attention output (a byte-exact copy):
+ *   unpad_qkv[t, h * hd + d] = qkv[b, h, i, d]
+ * for t < num_input_tokens, with b * q_cache_len + i = unpad_to_pad_idx[t].
+ * qkv: (batch, Hq, q_cache_len, hd); unpad_to_pad_idx: (batch * q_cache_len)
+ * (e.g. from l2k_build_padding_index_maps); unpad_qkv: (num_input_tokens,
+ * Hq * hd). A slot >= batch * q_cache_len gives a zero row (the reference
+ * reads out of bounds there).
+ * Replaces launch_fused_transpose_unpad (include/kernel/fused_transpose_unpad.h:6-11,
+ * src/kernel/fused_transpose_unpad.cu:51-73).
+ * ------------------------------------------------------------------------ */
+int l2k_fused_transpose_unpad(int64_t num_input_tokens, const void *qkv, const uint32_t *unpad_to_pad_idx,
+                              void *unpad_qkv, int64_t batch, int64_t q_head_num, int64_t q_cache_len,
+                              int64_t head_dim, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Fused decode attention scores: QK^T + 1/sqrt(head_dim) scale + causal
  * length mask + softmax in one pass over the K cache, for one query token
  * per sequence. qk: (B, Hq, 1, kv_cache_len). With kv_len = kv_lens[b] and

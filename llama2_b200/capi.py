@@ -61,6 +61,7 @@ SIGNATURES = {
     "l2k_qk_scores": [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, cint, vp],
     "l2k_compute_masked_attention_score": [i64, u32, u32, vp, vp, vp, i64, i64, i64, i64, cint, vp],
     "l2k_swiglu": [vp, vp, i64, i64, cint, vp],
+    "l2k_fused_transpose_unpad": [i64, vp, vp, vp, i64, i64, i64, i64, cint, vp],
     "l2k_decode_attention_scores": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],
     "l2k_prefill_attention_scores": [vp, vp, vp, vp, u32, u32, vp, i64, i64, i64, i64, i64, i64, cint, vp],
     "l2k_decode_step_workspace_bytes": ([], i64),

@@ -28,6 +28,7 @@
 #include "kernel/fused_pad_reshape_transpose_rope_kvcache_llama2.h"
 #include "kernel/fused_reshape_rope_kvcache_decode.h"
 #include "kernel/fused_reshape_rope_kvcache_llama2_decode.h"
+#include "kernel/fused_transpose_unpad.h"
 #include "kernel/linear.h"
 #include "kernel/swiglu.h"
 #include "kernel/update_q_kv_lens.h"
@@ -309,6 +310,19 @@ void launch_swiglu(const Tensor<T> &input, Tensor<T> &output)
 }
 
 template <typename T>
+void launch_fused_transpose_unpad(const unsigned int num_input_tokens, const Tensor<T> &qkv,
+                                  const Tensor<unsigned int> &unpad_to_pad_idx, Tensor<T> &unpad_qkv)
+{
+    const unsigned int b = qkv.shape()[0], h = qkv.shape()[1], qc = qkv.shape()[2], hd = qkv.shape()[3];
+    require(unpad_qkv.shape()[1] == h * hd, "Incorrect embed dim");
+    require(unpad_qkv.shape()[0] >= num_input_tokens && unpad_to_pad_idx.numel() >= num_input_tokens,
+            "Incorrect number of input tokens");
+    check(l2k_fused_transpose_unpad(num_input_tokens, qkv.data(), unpad_to_pad_idx.data(), unpad_qkv.data(), b, h, qc,
+                                    hd, dtype_of<T>(), nullptr),
+          "launch_fused_transpose_unpad");
+}
+
+template <typename T>
 void launch_decode_attention_scores(const Tensor<T> &q, const Tensor<T> &k, const Tensor<unsigned int> &kv_lens,
                                     const Tensor<unsigned int> &max_kv_len, Tensor<T> &qk)
 {
@@ -403,6 +417,8 @@ void launch_decode_step(const Tensor<unsigned int> &q_lens, Tensor<unsigned int>
         const unsigned int, const unsigned int, const unsigned int, const Tensor<unsigned int> &,                   \
         const Tensor<unsigned char> &, Tensor<T> &);                                                                \
     template void launch_swiglu<T>(const Tensor<T> &, Tensor<T> &);                                                 \
+    template void launch_fused_transpose_unpad<T>(const unsigned int, const Tensor<T> &,                            \
+                                                  const Tensor<unsigned int> &, Tensor<T> &);                       \
     template void launch_decode_attention_scores<T>(const Tensor<T> &, const Tensor<T> &,                           \
                                                     const Tensor<unsigned int> &, const Tensor<unsigned int> &,     \
                                                     Tensor<T> &);                                                   \

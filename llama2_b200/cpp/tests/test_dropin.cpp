@@ -23,6 +23,7 @@
 #include "kernel/fused_pad_reshape_transpose_rope_kvcache_llama2.h"
 #include "kernel/fused_reshape_rope_kvcache_decode.h"
 #include "kernel/fused_reshape_rope_kvcache_llama2_decode.h"
+#include "kernel/fused_transpose_unpad.h"
 #include "kernel/linear.h"
 #include "kernel/swiglu.h"
 #include "kernel/update_q_kv_lens.h"
@@ -48,6 +49,7 @@ void orc_masked_attention_score(float *, const uint8_t *, const uint32_t *, int6
 void orc_swiglu(const float *, int64_t, int64_t, float *);
 void orc_embedding(const uint32_t *, int64_t, const void *, int64_t, int64_t, void *);
 void orc_update_q_kv_lens(const uint32_t *, uint32_t *, int64_t, uint32_t *, uint32_t *);
+void orc_transpose_unpad(const void *, const uint32_t *, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, void *);
 }
 
 // ---------------------------------------------------------------------------
@@ -384,6 +386,43 @@ TEST(SwiGLUTest, LargeBatchRandomValues)
     upload(in_d, in);
     launch_swiglu(in_d, out_d);
     EXPECT_TRUE(max_rel(download(out_d), e) <= 1e-5f);
+}
+
+// The reference's BasicTwoSequences and HalfBasic cases
+// (test/kernel/test_fused_transpose_unpad.cu:180-190, 233-241): the padded
+// (B, H, Qc, hd) attention output back to (tokens, H * hd), byte-exact.
+TEST(FusedTransposeUnpadTest, BasicTwoSequencesAndHalf)
+{
+    const unsigned int b = 3, h = 4, qc = 16, hd = 16;
+    const std::vector<unsigned int> lens = {2, 5, 3};
+    std::vector<unsigned int> idx(b * qc, 0u);
+    unsigned int t = 0;
+    for (unsigned int s = 0; s < b; ++s)
+        for (unsigned int i = 0; i < lens[s]; ++i)
+            idx[t++] = s * qc + i;
+    Tensor<unsigned int> idx_d({b, qc}, GPU);
+    upload(idx_d, idx);
+    const std::vector<float> x = pattern(size_t(b) * h * qc * hd, 53, 0.1f, 1.0f);
+    {
+        Tensor<float> qkv({b, h, qc, hd}, GPU), out({t, h * hd}, GPU);
+        upload(qkv, x);
+        launch_fused_transpose_unpad(t, qkv, idx_d, out);
+        std::vector<float> e(size_t(t) * h * hd);
+        orc_transpose_unpad(x.data(), idx.data(), t, b, h, qc, hd, sizeof(float), e.data());
+        EXPECT_TRUE(download(out) == e);
+    }
+    {
+        std::vector<half> xh(x.size());
+        for (size_t i = 0; i < x.size(); ++i)
+            xh[i] = __float2half(x[i]);
+        Tensor<half> qkv({b, h, qc, hd}, GPU), out({t, h * hd}, GPU);
+        upload(qkv, xh);
+        launch_fused_transpose_unpad(t, qkv, idx_d, out);
+        std::vector<half> e(size_t(t) * h * hd);
+        orc_transpose_unpad(xh.data(), idx.data(), t, b, h, qc, hd, sizeof(half), e.data());
+        const std::vector<half> got = download(out);
+        EXPECT_TRUE(std::memcmp(got.data(), e.data(), e.size() * sizeof(half)) == 0);
+    }
 }
 
 TEST(DecodeAttentionScoresTest, Fp32)

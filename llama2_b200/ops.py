@@ -290,6 +290,19 @@ def launch_swiglu(input, output):
     capi.call("l2k_swiglu", input.data_ptr(), output.data_ptr(), n, f, _code(output), _stream())
 
 
+def launch_fused_transpose_unpad(num_input_tokens, qkv, unpad_to_pad_idx, unpad_qkv):
+    """include/kernel/fused_transpose_unpad.h:6-11 (qkv (B, H, Qc, hd) -> unpad_qkv (T, H * hd))."""
+    _dev(qkv, unpad_to_pad_idx, unpad_qkv)
+    _same(qkv, unpad_qkv, "launch_fused_transpose_unpad")
+    _u32(unpad_to_pad_idx, "unpad_to_pad_idx")
+    b, h, qc, hd = qkv.shape
+    _require(unpad_qkv.dim() == 2 and unpad_qkv.shape[1] == h * hd, "Incorrect embed dim")
+    _require(unpad_qkv.shape[0] >= num_input_tokens, "unpad_qkv has too few rows")
+    _require(unpad_to_pad_idx.numel() >= num_input_tokens, "unpad_to_pad_idx too small")
+    capi.call("l2k_fused_transpose_unpad", int(num_input_tokens), qkv.data_ptr(), unpad_to_pad_idx.data_ptr(),
+              unpad_qkv.data_ptr(), b, h, qc, hd, _code(qkv), _stream())
+
+
 def decode_attention_scores(q, k, kv_lens, max_kv_len, qk):
     """Fused QK^T + scale + length mask + softmax for one query token per sequence.
 

@@ -213,3 +213,24 @@ class port:
         out = np.empty((t, two_f // 2), dtype=np.float32)
         port_lib().orc_swiglu(_ptr(inp), _i64(t), _i64(two_f // 2), _ptr(out))
         return out
+
+    @staticmethod
+    def transpose_unpad(qkv, unpad_to_pad, n_tokens):
+        """qkv (B, H, Qc, hd) of any dtype -> (n_tokens, H * hd)."""
+        qkv = np.ascontiguousarray(qkv)
+        unpad_to_pad = u32(unpad_to_pad)
+        b, h, qc, hd = qkv.shape
+        out = np.empty((n_tokens, h * hd), dtype=qkv.dtype)
+        if n_tokens:
+            port_lib().orc_transpose_unpad(_ptr(qkv), _ptr(unpad_to_pad), _i64(n_tokens), _i64(b), _i64(h),
+                                           _i64(qc), _i64(hd), _i64(qkv.dtype.itemsize), _ptr(out))
+        return out
+
+    @staticmethod
+    def attention_qkv(qk, v, m, n, qkv):
+        """In place on qkv (B, Hq, Qc, hd) float32: rows < m, keys < n."""
+        qk, v = f32(qk), f32(v)
+        b, hq, qc, s = qk.shape
+        hkv, hd = v.shape[1], v.shape[3]
+        port_lib().orc_attention_qkv(_ptr(qk), _ptr(v), _i64(b), _i64(hq), _i64(hkv), _i64(qc), _i64(s), _i64(hd),
+                                     _i64(m), _i64(n), _ptr(qkv))

@@ -415,3 +415,69 @@ void orc_swiglu(const float *in, int64_t n_tokens, int64_t inter, float *out)
             out[t * inter + i] = x * sigmoid_x * y;
         }
 }
+
+/* ------------------------------------------------------------------------
+ * Transpose + unpad of the attention output (byte copy, any element size).
+ * Follows the expected-result loop of run_fused_transpose_unpad_test,
+ * test/kernel/test_fused_transpose_unpad.cu:148-167, with the token's padded
+ * slot taken from unpad_to_pad (the reference kernel's addressing,
+ * src/kernel/fused_transpose_unpad.cu:30-38):
+ *   p = unpad_to_pad[t], b = p / Qc, i = p % Qc,
+ *   out[t, h * hd + d] = qkv[b, h, i, d].
+ * A slot p >= batch * Qc (which the reference would read out of bounds)
+ * gives a zero row here, as the CUDA operator does.
+ * ------------------------------------------------------------------------ */
+void orc_transpose_unpad(const void *qkv, const uint32_t *unpad_to_pad, int64_t n_tokens, int64_t batch,
+                         int64_t heads, int64_t q_cache_len, int64_t head_dim, int64_t elem_size, void *out)
+{
+    const int64_t row = head_dim * elem_size;
+    const char *src = (const char *)qkv;
+    char *dst = (char *)out;
+    for (int64_t t = 0; t < n_tokens; ++t)
+    {
+        const int64_t p = unpad_to_pad[t];
+        for (int64_t h = 0; h < heads; ++h)
+        {
+            char *d = dst + (t * heads + h) * row;
+            if (p >= batch * q_cache_len)
+            {
+                memset(d, 0, (size_t)row);
+                continue;
+            }
+            const int64_t b = p / q_cache_len, i = p % q_cache_len;
+            memcpy(d, src + ((b * heads + h) * q_cache_len + i) * row, (size_t)row);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------
+ * P.V at the reference's launch_linear call site (trans_A = trans_B =
+ * false), per (b, q head) with grouped KV heads:
+ *   qkv[b, h, i, d] = sum_{j < n} qk[b, h, i, j] * v[b, h / (Hq/Hkv), j, d]
+ * for rows i < m; other rows untouched. Summation in j order in fp32, as
+ * compute_expected_linear does (test/kernel/test_linear.cu:78-108).
+ * qk: (B, Hq, Qc, S); v: (B, Hkv, S, hd); qkv: (B, Hq, Qc, hd).
+ * ------------------------------------------------------------------------ */
+void orc_attention_qkv(const float *qk, const float *v, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                       int64_t q_cache_len, int64_t kv_cache_len, int64_t head_dim, int64_t m, int64_t n,
+                       float *qkv)
+{
+    const int64_t group = q_heads / kv_heads;
+    for (int64_t b = 0; b < batch; ++b)
+        for (int64_t h = 0; h < q_heads; ++h)
+        {
+            const float *vh = v + (b * kv_heads + h / group) * kv_cache_len * head_dim;
+            for (int64_t i = 0; i < m; ++i)
+            {
+                const float *p = qk + ((b * q_heads + h) * q_cache_len + i) * kv_cache_len;
+                float *o = qkv + ((b * q_heads + h) * q_cache_len + i) * head_dim;
+                for (int64_t d = 0; d < head_dim; ++d)
+                {
+                    float acc = 0.f;
+                    for (int64_t j = 0; j < n; ++j)
+                        acc += p[j] * vh[j * head_dim + d];
+                    o[d] = acc;
+                }
+            }
+        }
+}

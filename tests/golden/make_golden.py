@@ -409,6 +409,66 @@ def gen_swiglu(lib):
     w.save()
 
 
+def gen_unpad(lib):
+    """test_fused_transpose_unpad.cu: the index map from the reference helper
+    compute_unpad_to_pad_idx (:78-93), the input pattern of the runner
+    (:115-117, i % 53 * 0.1 - 1, rounded through half for the half case), and
+    the expected rows of the runner's inline loop (:148-167), restated here
+    because that loop is not a callable helper."""
+    w = Writer("unpad")
+    cases = [("BasicTwoSequences", 3, 4, 16, 16, [2, 5, 3], "f32", 180),
+             ("SingleSequence", 1, 2, 8, 16, [6], "f32", 192),
+             ("IncrementalDecoding", 4, 2, 8, 16, [1, 1, 1, 1], "f32", 204),
+             ("LargerHeadDim", 2, 2, 32, 64, [7, 9], "f32", 217),
+             ("HalfBasic", 2, 2, 8, 16, [3, 4], "f16", 233)]
+    for name, b, h, qc, hd, q_lens, dtype, line in cases:
+        q_lens = np.array(q_lens, U32)
+        t = int(q_lens.sum())
+        idx = np.zeros(b * qc, U32)
+        lib.ref_unpad_to_pad_idx(P(q_lens), ctypes.c_uint(b), ctypes.c_uint(qc), P(idx))
+        qkv = pattern(b * h * qc * hd, 53, 0.1, 1.0)
+        if dtype == "f16":
+            qkv = qkv.astype(np.float16).astype(F32)
+        qkv = qkv.reshape(b, h, qc, hd)
+        out = np.zeros((t, h * hd), F32)
+        off = 0
+        for s, n in enumerate(q_lens):
+            for i in range(int(n)):
+                out[off + i] = qkv[s, :, i, :].reshape(-1)
+            off += int(n)
+        w.case(f"unpad.{name}", {"line": f"test_fused_transpose_unpad.cu:{line}", "dtype": dtype,
+                                 "num_input_tokens": t},
+               q_lens=q_lens, unpad_to_pad=idx.reshape(b, qc), qkv=qkv, out=out)
+    w.save()
+
+
+def gen_attention_qkv(lib):
+    """P.V at the launch_linear call site (trans_A = trans_B = false): per
+    (b, q head) the reference helper compute_expected_linear
+    (test_linear.cu:78-108) on the slice qk[b, h, :m, :n] x v[b, h / g, :n, :].
+    The shapes are the decode and prefill call sites with grouped heads."""
+    w = Writer("attention_qkv")
+    rng = np.random.default_rng(7)
+    cases = [("decode_mha", 2, 3, 3, 1, 40, 16, 1, 33),
+             ("decode_gqa", 2, 4, 2, 1, 64, 32, 1, 64),
+             ("prefill_gqa", 1, 4, 1, 8, 24, 16, 5, 20),
+             ("prefill_full", 2, 2, 2, 6, 12, 8, 6, 12)]
+    for name, b, hq, hkv, qc, s, hd, m, n in cases:
+        qk = rng.random((b, hq, qc, s), dtype=F32)
+        v = rng.standard_normal((b, hkv, s, hd), dtype=F32)
+        out = np.full((b, hq, qc, hd), -7.0, F32)
+        g = hq // hkv
+        for bi in range(b):
+            for h in range(hq):
+                a_s = np.ascontiguousarray(qk[bi, h, :m, :n])
+                b_s = np.ascontiguousarray(v[bi, h // g, :n, :])
+                c = np.zeros((m, hd), F32)
+                lib.ref_linear(P(a_s), P(b_s), 0, 0, ctypes.c_uint(m), ctypes.c_uint(hd), ctypes.c_uint(n), P(c))
+                out[bi, h, :m] = c
+        w.case(name, {"line": "test_linear.cu:78-108", "m": m, "n": n}, qk=qk, v=v, qkv=out)
+    w.save()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-root", default="/root/reference")
@@ -418,7 +478,7 @@ def main():
     if lib is None:
         sys.exit("reference helpers are not built; the reference sources are needed")
     for fn in (gen_embedding, gen_rmsnorm, gen_rope_decode, gen_rope_prefill, gen_integer, gen_linear, gen_score,
-               gen_swiglu):
+               gen_swiglu, gen_unpad, gen_attention_qkv):
         fn(lib)
 
 

@@ -56,6 +56,9 @@ def test_status_strings():
     ("l2k_decode_attention_scores", (None, None, None, None, None, 1, 3, 2, 16, 8, 0, None), 1),
     ("l2k_prefill_attention_scores", (None, None, None, None, 9, 4, None, 1, 2, 2, 8, 8, 16, 0, None), 1),
     ("l2k_compute_masked_attention_score", (16, 4, 4, None, None, None, 1, 1, 4, 4, 9, None), 1),
+    ("l2k_fused_transpose_unpad", (3, None, None, None, 2, 4, 8, 16, 0, None), 1),   # null pointers
+    ("l2k_fused_transpose_unpad", (17, None, None, None, 2, 4, 8, 16, 0, None), 1),  # more tokens than slots
+    ("l2k_fused_transpose_unpad", (1, None, None, None, 2, 4, 8, 16, 5, None), 1),   # dtype
 ])
 def test_bad_arguments_are_rejected(call, args, status):
     with pytest.raises(capi.L2KError) as e:
@@ -69,6 +72,7 @@ def test_empty_inputs_are_noops():
     capi.call("l2k_embedding", None, 0, None, 10, 8, None, 0, None)
     capi.call("l2k_swiglu", None, None, 0, 16, 2, None)
     capi.call("l2k_fused_add_residual_rmsnorm", None, None, None, 0, 64, 1, 1, None)
+    capi.call("l2k_fused_transpose_unpad", 0, None, None, None, 2, 4, 8, 16, 1, None)
 
 
 @pytest.mark.parametrize("hd", [2, 4, 48, 64, 128])

@@ -134,3 +134,19 @@ def test_masked_attention_score(case):
 def test_swiglu(case):
     _, a = golden_io.load("swiglu")[case]
     assert _bits_equal(port.swiglu(a["input"]), a["out"])
+
+
+@pytest.mark.parametrize("case", golden_io.case_ids("unpad"))
+def test_transpose_unpad(case):
+    p, a = golden_io.load("unpad")[case]
+    qkv = a["qkv"].astype(np.float16) if p["dtype"] == "f16" else a["qkv"]
+    got = port.transpose_unpad(qkv, a["unpad_to_pad"].reshape(-1), p["num_input_tokens"])
+    assert _bits_equal(got.astype(F32), a["out"])
+
+
+@pytest.mark.parametrize("case", golden_io.case_ids("attention_qkv"))
+def test_attention_qkv(case):
+    p, a = golden_io.load("attention_qkv")[case]
+    got = np.full_like(a["qkv"], -7.0)
+    port.attention_qkv(a["qk"], a["v"], p["m"], p["n"], got)
+    assert _bits_equal(got, a["qkv"])
