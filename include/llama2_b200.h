@@ -213,6 +213,21 @@ int l2k_qk_scores(const void *q, const void *k, void *qk, int64_t batch, int64_t
                   l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * P.V at the reference's launch_linear call site (trans_A = trans_B =
+ * false), per (b, q head) with grouped KV heads, without pointer arrays:
+ *   qkv[b, h, i, d] = sum_{j < n} qk[b, h, i, j] * v[b, h / (Hq/Hkv), j, d],
+ * i < m (fp32 accumulation). qk: (B, Hq, q_cache_len, kv_cache_len);
+ * v: (B, Hkv, kv_cache_len, hd); qkv: (B, Hq, q_cache_len, hd). Other rows
+ * are left as is. This is the batched launch_linear of the reference's
+ * qk x v product (src/kernel/linear.cu:96-128 with the qk, v and qkv
+ * arrays of include/kernel/build_q_k_v_qk_qkv_array.h:6-22), M = m,
+ * N = head_dim, K = n.
+ * ------------------------------------------------------------------------ */
+int l2k_attention_qkv(const void *qk, const void *v, void *qkv, int64_t batch, int64_t q_head_num,
+                      int64_t kv_head_num, int64_t q_cache_len, int64_t kv_cache_len, int64_t head_dim, int64_t m,
+                      int64_t n, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Masked attention score, in place on qk (B, H, q_cache_len, kv_cache_len):
  * for rows q < q_lens[b] and keys k < max_kv_len,
  *   qk = mask[b, q, k] ? exp(qk / sqrt(head_dim) - m) / (sum + 1e-6) : 0
@@ -264,6 +279,25 @@ int l2k_fused_transpose_unpad(int64_t num_input_tokens, const void *qkv, const u
 int l2k_decode_attention_scores(const void *q, const void *k, const uint32_t *kv_lens, const uint32_t *max_kv_len,
                                 void *qk, int64_t batch, int64_t q_head_num, int64_t kv_head_num,
                                 int64_t kv_cache_len, int64_t head_dim, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused decode attention: the probabilities of l2k_decode_attention_scores
+ * (written to qk exactly as that operator writes them) and the attention
+ * output P.V, in one pass over the K and V caches:
+ *   qkv[b, h, 0, d] = sum_{j < kv_len} p[b, h, j] * v[b, h / (Hq/Hkv), j, d]
+ * (fp32 probabilities and accumulation). v: (B, Hkv, kv_cache_len, hd);
+ * qkv: (B, Hq, 1, hd), which is also the unpadded (B, Hq * hd) layout of one
+ * token per sequence. The composition it replaces: the QK^T call site,
+ * the masked softmax, and the qk x v launch_linear call
+ * (src/kernel/linear.cu:96-128) over the keys j < max_kv_len, whose
+ * probabilities past kv_len are 0.
+ * Head sizes whose K rows are not 64, 128, 256 or 512 bytes (or unaligned
+ * operands) run the score operator and then l2k_attention_qkv's kernel.
+ * ------------------------------------------------------------------------ */
+int l2k_decode_attention(const void *q, const void *k, const void *v, const uint32_t *kv_lens,
+                         const uint32_t *max_kv_len, void *qk, void *qkv, int64_t batch, int64_t q_head_num,
+                         int64_t kv_head_num, int64_t kv_cache_len, int64_t head_dim, int dtype,
+                         l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Fused prefill attention scores: the same composition for q_len query rows

@@ -59,10 +59,12 @@ SIGNATURES = {
                                      vp],
     "l2k_linear": [cint, cint, i64, i64, i64, vp, i64, vp, i64, vp, i64, i64, vp, vp, vp, cint, vp],
     "l2k_qk_scores": [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, cint, vp],
+    "l2k_attention_qkv": [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, cint, vp],
     "l2k_compute_masked_attention_score": [i64, u32, u32, vp, vp, vp, i64, i64, i64, i64, cint, vp],
     "l2k_swiglu": [vp, vp, i64, i64, cint, vp],
     "l2k_fused_transpose_unpad": [i64, vp, vp, vp, i64, i64, i64, i64, cint, vp],
     "l2k_decode_attention_scores": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],
+    "l2k_decode_attention": [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],
     "l2k_prefill_attention_scores": [vp, vp, vp, vp, u32, u32, vp, i64, i64, i64, i64, i64, i64, cint, vp],
     "l2k_decode_step_workspace_bytes": ([], i64),
     "l2k_decode_step_supported": [ctypes.POINTER(DecodeStepArgs)],

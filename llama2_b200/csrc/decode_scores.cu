@@ -76,6 +76,19 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
                                     &g_scores_error);
 }
 
+// Attention rows: the score row and its P.V output in one streamed pass
+// over the row's K and V blocks (score_row_stream with PV).
+template <typename T, int LPR>
+__global__ void __launch_bounds__(kStreamThreads) attention_rows_stream_kernel(const DecodeArgs a)
+{
+    extern __shared__ __align__(128) uint8_t stream_smem[];
+    __shared__ StreamShared sh;
+    cg::cluster_group cluster = cg::this_cluster();
+    const StepRowArgs none{};
+    score_row_stream<T, LPR, false, true>(a, none, (int64_t)blockIdx.x / cluster.num_blocks(), cluster, stream_smem,
+                                          sh, &g_scores_error);
+}
+
 // Any head_dim / alignment: one thread per key, q staged in shared memory.
 template <typename T>
 __global__ void __launch_bounds__(kThreads) decode_scores_generic_kernel(const DecodeArgs a)
@@ -146,14 +159,53 @@ cudaError_t launch_clustered(K kernel, int C, int64_t rows, size_t smem, cudaStr
     return cudaLaunchKernelEx(&cfg, kernel, a);
 }
 
+// Whether score rows of this shape run the streaming kernel (K rows of 64,
+// 128, 256 or 512 bytes, 16-byte aligned operands; with P.V also V and qkv).
+template <typename T>
+bool stream_rows_ok(const DecodeArgs &a, bool pv)
+{
+    const int64_t row_bytes = a.hd * (int64_t)sizeof(T);
+    const int lpr = (int)(row_bytes / 16);
+    const bool vec = row_bytes % 16 == 0 && is_aligned(a.q, 16) && is_aligned(a.k, 16) &&
+                     (!pv || (is_aligned(a.v, 16) && is_aligned(a.qkv, 16)));
+    return vec && (lpr == 4 || lpr == 8 || lpr == 16 || lpr == 32);
+}
+
+template <typename T>
+int launch_attention_rows(const DecodeArgs &a, int64_t batch, cudaStream_t stream)
+{
+    const int64_t rows = batch * a.Hq * a.Qc;
+    const int64_t row_bytes = a.hd * (int64_t)sizeof(T);
+    const int lpr = (int)(row_bytes / 16);
+    const int64_t kb = kBlockBytes / row_bytes;
+    const int64_t blocks_per_row = ceil_div(a.S, kb);
+    int C = 1;
+    while (C < 8 && rows * C < 3LL * num_sms() && C * 2 <= blocks_per_row)
+        C *= 2;
+    const size_t smem = stream_smem_bytes(a.S, row_bytes, C) + pv_smem_bytes(a.hd);
+    L2K_REQUIRE_SHAPE(smem <= (size_t)kNS * kBlockBytes + 128 * 1024, "attention rows: kv_cache_len %lld too long",
+                      (long long)a.S);
+    cudaError_t e;
+    if (lpr == 32)
+        e = launch_clustered(attention_rows_stream_kernel<T, 32>, C, rows, smem, stream, a, kStreamThreads);
+    else if (lpr == 16)
+        e = launch_clustered(attention_rows_stream_kernel<T, 16>, C, rows, smem, stream, a, kStreamThreads);
+    else if (lpr == 8)
+        e = launch_clustered(attention_rows_stream_kernel<T, 8>, C, rows, smem, stream, a, kStreamThreads);
+    else
+        e = launch_clustered(attention_rows_stream_kernel<T, 4>, C, rows, smem, stream, a, kStreamThreads);
+    if (e != cudaSuccess)
+        return set_error(L2K_ERR_CUDA, "attention rows: %s", cudaGetErrorString(e));
+    return check_launch("attention rows");
+}
+
 template <typename T>
 int launch_score_rows(DecodeArgs a, int64_t batch, cudaStream_t stream)
 {
     const int64_t rows = batch * a.Hq * a.Qc;
     const int64_t row_bytes = a.hd * (int64_t)sizeof(T);
-    const bool vec = row_bytes % 16 == 0 && is_aligned(a.q, 16) && is_aligned(a.k, 16);
     const int lpr = (int)(row_bytes / 16);
-    const bool stream_ok = vec && (lpr == 4 || lpr == 8 || lpr == 16 || lpr == 32);
+    const bool stream_ok = stream_rows_ok<T>(a, false);
     a.bulk_out = (a.S * (int64_t)sizeof(T)) % 16 == 0 && is_aligned(a.qk, 16);
     cudaError_t e;
     if (stream_ok)
@@ -223,7 +275,48 @@ int prefill_score_rows(const void *q, const void *k, const uint32_t *q_lens, con
     return L2K_OK;
 }
 
+int attention_qkv_cuda_cores(const void *qk, const void *v, void *qkv, int64_t batch, int64_t Hq, int64_t Hkv,
+                             int64_t qc, int64_t S, int64_t hd, int64_t m, int64_t n, const uint32_t *n_dev,
+                             int dtype, cudaStream_t stream);
+
 } // namespace l2k
+
+extern "C" int l2k_decode_attention(const void *q, const void *k, const void *v, const uint32_t *kv_lens,
+                                    const uint32_t *max_kv_len, void *qk, void *qkv, int64_t batch,
+                                    int64_t q_head_num, int64_t kv_head_num, int64_t kv_cache_len, int64_t head_dim,
+                                    int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    L2K_REQUIRE(dtype_ok(dtype), "l2k_decode_attention: unsupported dtype %d", dtype);
+    L2K_REQUIRE(batch >= 0 && q_head_num >= 0 && kv_head_num >= 0 && kv_cache_len >= 0 && head_dim > 0,
+                "l2k_decode_attention: bad size");
+    if (batch == 0 || q_head_num == 0)
+        return L2K_OK;
+    L2K_REQUIRE(kv_head_num > 0 && q_head_num % kv_head_num == 0,
+                "l2k_decode_attention: q_head_num must be a multiple of kv_head_num");
+    L2K_REQUIRE(q && k && v && kv_lens && max_kv_len && qk && qkv, "l2k_decode_attention: null pointer");
+    L2K_REQUIRE(kv_cache_len > 0, "l2k_decode_attention: kv_cache_len must be positive");
+    L2K_REQUIRE_SHAPE(head_dim <= 4096, "l2k_decode_attention: head_dim > 4096");
+    L2K_REQUIRE_SHAPE(batch * q_head_num * 16 < (int64_t(1) << 31), "l2k_decode_attention: grid too large");
+    DecodeArgs a{q, k, nullptr, kv_lens, max_kv_len, 0u, qk, q_head_num, q_head_num / kv_head_num, kv_head_num, 1,
+                 kv_cache_len, head_dim, 0, 1.f / sqrtf((float)head_dim)};
+    a.v = v;
+    a.qkv = qkv;
+    bool streamed = false;
+    L2K_DISPATCH(dtype, { streamed = stream_rows_ok<T>(a, true); });
+    if (streamed)
+    {
+        L2K_DISPATCH(dtype, { return launch_attention_rows<T>(a, batch, stream); });
+    }
+    // Other head sizes / alignments: the score rows, then P.V over the keys
+    // j < *max_kv_len on the CUDA cores (the reference's call-site order).
+    int st = L2K_OK;
+    L2K_DISPATCH(dtype, { st = launch_score_rows<T>(a, batch, stream); });
+    if (st != L2K_OK)
+        return st;
+    return attention_qkv_cuda_cores(qk, v, qkv, batch, q_head_num, kv_head_num, 1, kv_cache_len, head_dim, 1,
+                                    kv_cache_len, max_kv_len, dtype, stream);
+}
 
 extern "C" int l2k_decode_attention_scores(const void *q, const void *k, const uint32_t *kv_lens,
                                            const uint32_t *max_kv_len, void *qk, int64_t batch, int64_t q_head_num,

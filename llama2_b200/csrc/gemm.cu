@@ -3,7 +3,8 @@
 // and the fp32 QK^T path. 64x64 output tile per CTA, 16-deep K slices staged
 // in shared memory, 4x4 outputs per thread. Three batch addressings:
 // plain (one GEMM), pointer arrays (the reference's batched form), and the
-// QK^T call site computed from (seq, head) with grouped KV heads.
+// attention call sites computed from (seq, head) with grouped KV heads:
+// QK^T (trans_B) and P.V.
 #include "common.cuh"
 
 #include <algorithm>
@@ -19,7 +20,7 @@ enum BatchMode
 {
     PLAIN = 0,
     PTR_ARRAYS = 1,
-    QK_HEADS = 2
+    QK_HEADS = 2 // (seq, head) slices; also the P.V call site
 };
 
 struct GemmArgs
@@ -39,6 +40,7 @@ struct GemmArgs
     // QK_HEADS
     int64_t Hq, group, Hkv, qc, S;
     const uint32_t *row_lens; // optional: rows i >= row_lens[seq] are skipped
+    const uint32_t *k_dev;    // optional: the contraction length is min(k, *k_dev)
 };
 
 template <typename T, int MODE>
@@ -77,15 +79,16 @@ __global__ void __launch_bounds__(256) gemm_kernel(const GemmArgs g)
         }
         if (i0 >= m)
             continue;
+        const int64_t kl = g.k_dev ? min(g.k, (int64_t)*g.k_dev) : g.k;
         float acc[4][4] = {};
-        for (int64_t k0 = 0; k0 < g.k; k0 += BK)
+        for (int64_t k0 = 0; k0 < kl; k0 += BK)
         {
             for (int e = threadIdx.x; e < BM * BK; e += blockDim.x)
             {
                 const int r = e / BK, kk = e % BK;
                 const int64_t gi = i0 + r, gk = k0 + kk;
                 float v = 0.f;
-                if (gi < m && gk < g.k)
+                if (gi < m && gk < kl)
                     v = to_f(g.trans_a ? A[gk * g.lda + gi] : A[gi * g.lda + gk]);
                 As[kk][r] = v;
             }
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(256) gemm_kernel(const GemmArgs g)
                 const int cidx = e / BK, kk = e % BK;
                 const int64_t gj = j0 + cidx, gk = k0 + kk;
                 float v = 0.f;
-                if (gj < g.n && gk < g.k)
+                if (gj < g.n && gk < kl)
                     v = to_f(g.trans_b ? B[gj * g.ldb + gk] : B[gk * g.ldb + gj]);
                 Bs[kk][cidx] = v;
             }
@@ -168,6 +171,35 @@ int qk_scores_cuda_cores(const void *q, const void *k, void *qk, int64_t batch, 
     return L2K_OK;
 }
 
+// P.V per (seq, head) on the CUDA cores: qkv[b,h,i,:] = sum_{j<n} qk[b,h,i,j] v[b,h/g,j,:]
+// for i < m (n further capped by *n_dev when given).
+int attention_qkv_cuda_cores(const void *qk, const void *v, void *qkv, int64_t batch, int64_t Hq, int64_t Hkv,
+                             int64_t qc, int64_t S, int64_t hd, int64_t m, int64_t n, const uint32_t *n_dev,
+                             int dtype, cudaStream_t stream)
+{
+    GemmArgs g{};
+    g.trans_a = 0;
+    g.trans_b = 0;
+    g.m = m;
+    g.n = hd;
+    g.k = n;
+    g.a = qk;
+    g.lda = S;
+    g.b = v;
+    g.ldb = hd;
+    g.c = qkv;
+    g.ldc = hd;
+    g.batch = batch * Hq;
+    g.Hq = Hq;
+    g.group = Hq / Hkv;
+    g.Hkv = Hkv;
+    g.qc = qc;
+    g.S = S;
+    g.k_dev = n_dev;
+    L2K_DISPATCH(dtype, { return launch_gemm<T, QK_HEADS>(g, stream); });
+    return L2K_OK;
+}
+
 } // namespace l2k
 
 extern "C" int l2k_linear(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda,
@@ -228,4 +260,23 @@ extern "C" int l2k_qk_scores(const void *q, const void *k, void *qk, int64_t bat
     L2K_REQUIRE(q && k && qk, "l2k_qk_scores: null pointer");
     return qk_scores_cuda_cores(q, k, qk, batch, q_head_num, kv_head_num, q_cache_len, kv_cache_len, head_dim, m, n,
                                 nullptr, dtype, stream);
+}
+
+extern "C" int l2k_attention_qkv(const void *qk, const void *v, void *qkv, int64_t batch, int64_t q_head_num,
+                                 int64_t kv_head_num, int64_t q_cache_len, int64_t kv_cache_len, int64_t head_dim,
+                                 int64_t m, int64_t n, int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    L2K_REQUIRE(dtype_ok(dtype), "l2k_attention_qkv: unsupported dtype %d", dtype);
+    L2K_REQUIRE(batch >= 0 && q_head_num >= 0 && kv_head_num >= 0 && head_dim >= 0 && m >= 0 && n >= 0,
+                "l2k_attention_qkv: negative size");
+    L2K_REQUIRE(m <= q_cache_len && n <= kv_cache_len, "l2k_attention_qkv: m/n exceed the cache dims");
+    if (batch == 0 || q_head_num == 0 || m == 0 || head_dim == 0)
+        return L2K_OK;
+    L2K_REQUIRE(kv_head_num > 0 && q_head_num % kv_head_num == 0,
+                "l2k_attention_qkv: q_head_num must be a multiple of kv_head_num");
+    L2K_REQUIRE(qk && v && qkv, "l2k_attention_qkv: null pointer");
+    L2K_REQUIRE_SHAPE(ceil_div(m, BM) <= 65535, "l2k_attention_qkv: m too large");
+    return attention_qkv_cuda_cores(qk, v, qkv, batch, q_head_num, kv_head_num, q_cache_len, kv_cache_len, head_dim,
+                                    m, n, nullptr, dtype, stream);
 }

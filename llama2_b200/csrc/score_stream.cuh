@@ -68,6 +68,9 @@ struct DecodeArgs
     int64_t chunk;
     float scale;
     int bulk_out; // score rows start 16-byte aligned: stored with cp.async.bulk
+    // PV rows only: the V cache and the attention output P.V
+    const void *v;        // (B, Hkv, S, hd)
+    void *qkv;            // (B, Hq, Qc, hd)
 };
 
 // Extra inputs of a score row inside the fused decode step. kv_lens and
@@ -171,18 +174,22 @@ struct StreamShared
     float2 wstat[kCW];  // per consumer warp: (max, sum of exp) of its logits
     float2 cstat[8];    // per cluster rank: (max, sum of exp), pushed by every rank
     uint64_t xbar;      // completes when the C - 1 peers' pairs have landed in cstat
+    uint64_t pvbar;     // PV, rank 0: completes when the C - 1 peers' partial P.V rows have landed
     uint32_t wkv[kCW];  // STEP: per consumer warp, max of the updated lengths
     float scratch[32];  // (block reductions of the step kernel's other roles)
     int abort_flag;
 };
 
-// Dynamic shared memory of one streaming score row: the ring and the logits.
+// Dynamic shared memory of one streaming score row: the ring and the logits,
+// and for PV rows the per-warp partial P.V rows and rank 0's receive slots
+// of the cluster's partial rows (kCW + 8 rows of head_dim floats).
 inline size_t stream_smem_bytes(int64_t S, int64_t row_bytes, int C)
 {
     const int64_t kb = kBlockBytes / row_bytes;
     const int64_t logit_bytes = ceil_div(ceil_div(S, kb), C) * kb * (int64_t)sizeof(float);
     return (size_t)kNS * kBlockBytes + (size_t)logit_bytes;
 }
+inline size_t pv_smem_bytes(int64_t head_dim) { return (size_t)(kCW + 8) * (size_t)head_dim * sizeof(float); }
 
 // (max, sum of exp) pairs: the pair of the union of both sets.
 __device__ __forceinline__ float2 stat_merge(float2 a, float2 b)
@@ -204,6 +211,22 @@ __device__ __forceinline__ void named_sync_consumers()
 {
     asm volatile("bar.sync 1, %0;" ::"n"(kCW * 32) : "memory");
 }
+// Barrier of the consumer warps that also ORs a per-thread flag: every
+// consumer thread gets the same answer, so a decision to leave (on an abort
+// flag that another thread may be setting meanwhile) is taken by all of them
+// or by none, and no consumer is left waiting at a later named barrier.
+__device__ __forceinline__ bool consumers_any(bool v)
+{
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\t"
+                 "setp.ne.u32 p, %1, 0;\n\t"
+                 "bar.red.or.pred q, 1, %2, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r)
+                 : "r"((uint32_t)v), "n"(kCW * 32)
+                 : "memory");
+    return r != 0;
+}
 __device__ __forceinline__ void cluster_arrive_relaxed()
 {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
@@ -221,6 +244,18 @@ __device__ __forceinline__ void push_stat(float2 *local_slot, uint64_t *local_ba
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(bar) : "r"(smem_addr(local_bar)), "r"(rank));
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(slot),
                  "f"(v.x), "f"(v.y), "r"(bar)
+                 : "memory");
+}
+// Pushes 4 floats into rank `rank`'s copy of *local_slot (16-byte aligned)
+// and signals 16 bytes on that rank's copy of *local_bar.
+__device__ __forceinline__ void push_f4(float4 *local_slot, uint64_t *local_bar, int rank, float4 v)
+{
+    uint32_t slot, bar;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(slot) : "r"(smem_addr(local_slot)), "r"(rank));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(bar) : "r"(smem_addr(local_bar)), "r"(rank));
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     slot),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
                  : "memory");
 }
 __device__ __forceinline__ void bulk_store(void *gdst, const void *ssrc, uint32_t bytes)
@@ -303,6 +338,153 @@ __device__ __forceinline__ void prefetch_first_blocks(const DecodeArgs &a, int64
     }
 }
 
+// The P.V part of a PV row, run by the consumer warps after the row's
+// (max, sum of exp) is known: probabilities in place of this CTA's logits,
+// their store (keys in [n_keys, M) as 0), the fold of p_j * V_j over this
+// CTA's V blocks (ring sequences n_mine + i, i < n_mine), and the reduction
+// lanes -> warps -> cluster ranks, the ranks' rows summed by rank 0 in rank
+// order and written to qkv[row].
+template <typename T, int LPR>
+__device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, const RowInfo &ri,
+                                       const int64_t n_keys, const int n_mine, const int c, const int C,
+                                       const float2 row_stat, uint8_t *smem, StreamShared &sh, int *err)
+{
+    constexpr int N = Vec16<T>::N;
+    constexpr int ROW_BYTES = LPR * 16;
+    constexpr int KB = kBlockBytes / ROW_BYTES;
+    constexpr int HALF = KB / 2;
+    constexpr int RPL = 32 / LPR;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float *logits = reinterpret_cast<float *>(smem + kNS * kBlockBytes);
+    const int64_t n_logits = ((a.S + KB - 1) / KB + C - 1) / C * KB;
+    float *pv_w = logits + n_logits;   // kCW partial rows of this CTA's warps
+    float *pv_r = pv_w + kCW * a.hd;   // rank 0: slot r receives rank r's partial row
+    const bool gather = C > 1 && c == 0;
+    if (gather && tid == 0)
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(&sh.pvbar)),
+                     "r"((uint32_t)((C - 1) * a.hd * (int64_t)sizeof(float)))
+                     : "memory");
+    auto leave = [&]() {
+        // Rank 0 lets peer rows still on their way land before it leaves.
+        if (gather)
+            bar_wait(smem_addr(&sh.pvbar), 0);
+    };
+    if (consumers_any(sh.abort_flag != 0))
+        return leave();
+
+    const float Mx = row_stat.x;
+    const float inv = __fdiv_rn(1.f, __fadd_rn(row_stat.y, kSoftmaxEps));
+    for (int e = tid; e < n_mine * KB; e += kCW * 32)
+    {
+        const int64_t j = (c + (int64_t)C * (e / KB)) * KB + e % KB;
+        logits[e] = j < n_keys ? __fmul_rn(expf(__fsub_rn(logits[e], Mx)), inv) : 0.f;
+    }
+    named_sync_consumers();
+    {
+        T *out_row = static_cast<T *>(a.qk) + row * a.S;
+        const int64_t n_wblk = (ri.M + KB - 1) / KB; // blocks with keys < M
+        const int n_wmine = n_wblk > c ? (int)((n_wblk - c + C - 1) / C) : 0;
+        for (int e = tid; e < n_wmine * KB; e += kCW * 32)
+        {
+            const int ib = e / KB;
+            const int64_t j = (c + (int64_t)C * ib) * KB + e % KB;
+            if (j < ri.M)
+                out_row[j] = from_f<T>(ib < n_mine ? logits[e] : 0.f);
+        }
+    }
+
+    float acc[N];
+#pragma unroll
+    for (int e = 0; e < N; ++e)
+        acc[e] = 0.f;
+    {
+        const int st = warp % kNS, hf = warp / kNS, sub = lane % LPR;
+        const uint8_t *stage = smem + st * kBlockBytes + hf * HALF * ROW_BYTES + sub * 16;
+        for (int i = ((st - n_mine) % kNS + kNS) % kNS; i < n_mine; i += kNS)
+        {
+            const int n = n_mine + i; // ring sequence: n % kNS == st
+            if (!bar_wait(smem_addr(&sh.full[st]), (n / kNS) & 1))
+            {
+                atomicCAS(err, 0, 0x204);
+                sh.abort_flag = 1;
+                break;
+            }
+            const int64_t valid = n_keys - (c + (int64_t)C * i) * KB - hf * HALF; // rows of this half with keys
+            const float *pr = logits + i * KB + hf * HALF;
+            auto fold = [&](int r) {
+                const float p = pr[r];
+                const Vec16<T> vv = as_vec<T>(*reinterpret_cast<const uint4 *>(stage + r * ROW_BYTES));
+#pragma unroll
+                for (int e = 0; e < N; ++e)
+                    acc[e] = fmaf(p, to_f(vv.v[e]), acc[e]);
+            };
+            if (valid >= HALF)
+            {
+#pragma unroll 4
+                for (int r = lane / LPR; r < HALF; r += RPL)
+                    fold(r);
+            }
+            else
+            {
+                for (int r = lane / LPR; r < valid; r += RPL)
+                    fold(r);
+            }
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&sh.empty[st])) : "memory");
+        }
+    }
+#pragma unroll
+    for (int off = LPR; off < 32; off <<= 1)
+#pragma unroll
+        for (int e = 0; e < N; ++e)
+            acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], off);
+    if (lane < LPR)
+    {
+#pragma unroll
+        for (int e = 0; e < N; e += 4)
+            *reinterpret_cast<float4 *>(pv_w + warp * a.hd + lane * N + e) =
+                make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
+    }
+    if (consumers_any(sh.abort_flag != 0)) // (also the barrier after the partial rows)
+        return leave();
+
+    const int nq = (int)(a.hd / 4);
+    if (tid < nq)
+    {
+        float4 sum = reinterpret_cast<const float4 *>(pv_w)[tid];
+#pragma unroll
+        for (int w = 1; w < kCW; ++w)
+        {
+            const float4 x = reinterpret_cast<const float4 *>(pv_w + w * a.hd)[tid];
+            sum = make_float4(sum.x + x.x, sum.y + x.y, sum.z + x.z, sum.w + x.w);
+        }
+        if (C > 1 && c != 0)
+        {
+            push_f4(reinterpret_cast<float4 *>(pv_r + c * a.hd) + tid, &sh.pvbar, 0, sum);
+            return;
+        }
+        if (gather)
+        {
+            if (!bar_wait(smem_addr(&sh.pvbar), 0))
+            {
+                atomicCAS(err, 0, 0x205);
+                return;
+            }
+            for (int r = 1; r < C; ++r)
+            {
+                const float4 x = reinterpret_cast<const float4 *>(pv_r + r * a.hd)[tid];
+                sum = make_float4(sum.x + x.x, sum.y + x.y, sum.z + x.z, sum.w + x.w);
+            }
+        }
+        T *o = static_cast<T *>(a.qkv) + row * a.hd + 4 * tid;
+        o[0] = from_f<T>(sum.x);
+        o[1] = from_f<T>(sum.y);
+        o[2] = from_f<T>(sum.z);
+        o[3] = from_f<T>(sum.w);
+    }
+}
+
 // One score row on this CTA's share of its keys (see the file comment).
 // head_dim * sizeof(T) = LPR * 16 bytes, LPR in {4, 8, 16, 32}. Every CTA of
 // the cluster calls it for the same row. `err` receives the first timeout
@@ -316,11 +498,22 @@ __device__ __forceinline__ void prefetch_first_blocks(const DecodeArgs &a, int64
 // statistics need one barrier; cluster peers push their statistics into
 // each other's shared memory before a single cluster barrier; probabilities
 // are staged in the (now idle) ring and written with cp.async.bulk stores.
-template <typename T, int LPR, bool STEP>
+//
+// PV rows (attention output, flash-decode style) also stream the V rows of
+// the same blocks: once its K blocks are issued the producer lane continues
+// with the V blocks into the same ring (the first kNS while the consumers
+// still finish the keys), and after the cluster's statistics are known the
+// consumers turn their logits into probabilities in place, store them, and
+// fold p_j * V_j over their V blocks from shared memory (each lane a 16-byte
+// slice of head_dim). Lanes, warps and then the cluster's CTAs are summed in
+// a fixed order (peers push their partial rows into rank 0's shared memory
+// with st.async), so the output does not depend on timing.
+template <typename T, int LPR, bool STEP, bool PV = false>
 __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const StepRowArgs &sa, const int64_t row,
                                                  cg::cluster_group &cluster, uint8_t *smem, StreamShared &sh,
                                                  int *err)
 {
+    static_assert(!(STEP && PV), "the decode step has no P.V output");
     constexpr int N = Vec16<T>::N;
     constexpr int ROW_BYTES = LPR * 16;
     constexpr int KB = kBlockBytes / ROW_BYTES; // K rows per block
@@ -415,18 +608,40 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
     const int n_mine = n_blk > c ? (int)((n_blk - c + C - 1) / C) : 0;
     const char *kbase = static_cast<const char *>(a.k) + (ri.b * a.Hkv + kvh) * a.S * (int64_t)ROW_BYTES;
 
+    // Ring sequence number i: K block i for i < n_mine, V block i - n_mine
+    // after (PV rows); sequence i lands in stage i % kNS.
     auto issue = [&](int i) {
         const int st = i % kNS;
+        const bool is_v = PV && i >= n_mine;
         // Whole blocks (up to the cache end): rows past kv_len are computed and
         // masked, which keeps the consumers' inner loop free of bounds checks.
-        const int64_t g = c + (int64_t)C * i;
+        const int64_t g = c + (int64_t)C * (is_v ? i - n_mine : i);
         const uint32_t bytes = (uint32_t)(min((int64_t)KB, a.S - g * KB) * ROW_BYTES);
         const uint32_t bar = smem_addr(&sh.full[st]);
+        const char *base = kbase;
+        if constexpr (PV)
+            if (is_v)
+                base = static_cast<const char *>(a.v) + (ri.b * a.Hkv + kvh) * a.S * (int64_t)ROW_BYTES;
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                          smem_addr(smem + st * kBlockBytes)),
-                     "l"(kbase + g * KB * ROW_BYTES), "r"(bytes), "r"(bar)
+                     "l"(base + g * KB * ROW_BYTES), "r"(bytes), "r"(bar)
                      : "memory");
+    };
+    // Producer lane: issues sequences up to `end`, each after its stage's
+    // previous contents were consumed (bounded waits; stops on abort).
+    auto issue_until = [&](int &n_iss, int end) {
+        for (; n_iss < end && !sh.abort_flag; ++n_iss)
+        {
+            const int st = n_iss % kNS;
+            if (n_iss >= kNS && !bar_wait(smem_addr(&sh.empty[st]), ((n_iss / kNS) - 1) & 1))
+            {
+                atomicCAS(err, 0, 0x201);
+                sh.abort_flag = 1;
+                break;
+            }
+            issue(n_iss);
+        }
     };
 
     int n_issued = 0; // producer lane only
@@ -443,6 +658,8 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                              : "memory");
             }
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&sh.xbar)) : "memory");
+            if constexpr (PV)
+                asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&sh.pvbar)) : "memory");
             sh.abort_flag = 0;
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
             for (; n_issued < n_mine && n_issued < kNS; ++n_issued)
@@ -541,6 +758,8 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                 }
                 issue(n_issued);
             }
+            if constexpr (PV) // the first V blocks, into stages the keys free
+                issue_until(n_issued, n_mine + min(n_mine, kNS));
         }
         if (C > 1)
         {
@@ -667,6 +886,18 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
     {
         if (STEP)
             step_ticket(sa, lane, sa.batch <= 32, pq, pkv);
+        if constexpr (PV)
+        {
+            if (lane == 0)
+            {
+                // The remaining V blocks, as the consumers free stages; then every
+                // copy this CTA issued has landed before it can leave (on the
+                // normal path the consumers have waited for each of them too).
+                issue_until(n_issued, 2 * n_mine);
+                for (int i = max(0, n_issued - kNS); i < n_issued; ++i)
+                    bar_wait(smem_addr(&sh.full[i % kNS]), (i / kNS) & 1);
+            }
+        }
         return;
     }
     float2 row_stat = cta;
@@ -696,7 +927,12 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
         for (int r = 1; r < C; ++r)
             row_stat = stat_merge(row_stat, sh.cstat[r]);
     }
-    if (sh.abort_flag)
+    if constexpr (PV)
+    {
+        pv_row<T, LPR>(a, row, ri, n_keys, n_mine, c, C, row_stat, smem, sh, err);
+        return;
+    }
+    if (consumers_any(sh.abort_flag != 0))
         return;
 
     // Probabilities p = exp(x - M) / (L + eps); keys in [n_keys, M) are

@@ -270,6 +270,19 @@ def launch_qk_scores(q, k, qk, M, N):
               _stream())
 
 
+def launch_attention_qkv(qk, v, qkv, M, N):
+    """P.V at the launch_linear call site (qk x v), per (seq, head) with grouped KV heads."""
+    _dev(qk, v, qkv)
+    _same(qk, v, "launch_attention_qkv")
+    _same(qk, qkv, "launch_attention_qkv")
+    b, hq, qc, s = qk.shape
+    hkv, hd = v.shape[1], v.shape[3]
+    _require(tuple(v.shape) == (b, hkv, s, hd), "Incorrect v size")
+    _require(tuple(qkv.shape) == (b, hq, qc, hd), "Incorrect qkv size")
+    capi.call("l2k_attention_qkv", qk.data_ptr(), v.data_ptr(), qkv.data_ptr(), b, hq, hkv, qc, s, hd, M, N,
+              _code(qk), _stream())
+
+
 def launch_compute_masked_attention_score(head_dim, max_q_len, max_kv_len, q_lens, mask, qk):
     """include/kernel/compute_masked_attention_score.h:6-12"""
     _dev(q_lens, mask, qk)
@@ -316,6 +329,21 @@ def decode_attention_scores(q, k, kv_lens, max_kv_len, qk):
     _require(one == 1 and tuple(qk.shape) == (b, hq, 1, s), "Incorrect q / qk size")
     capi.call("l2k_decode_attention_scores", q.data_ptr(), k.data_ptr(), kv_lens.data_ptr(), max_kv_len.data_ptr(),
               qk.data_ptr(), b, hq, hkv, s, hd, _code(q), _stream())
+
+
+def decode_attention(q, k, v, kv_lens, max_kv_len, qk, qkv):
+    """Fused decode attention: the decode_attention_scores probabilities (into qk)
+    and the attention output P.V (into qkv (B, Hq, 1, hd)) in one pass."""
+    _dev(q, k, v, kv_lens, max_kv_len, qk, qkv)
+    for t in (k, v, qk, qkv):
+        _same(q, t, "decode_attention")
+    b, hq, one, hd = q.shape
+    hkv, s = k.shape[1], k.shape[2]
+    _require(one == 1 and tuple(qk.shape) == (b, hq, 1, s), "Incorrect q / qk size")
+    _require(tuple(v.shape) == tuple(k.shape), "Incorrect v size")
+    _require(tuple(qkv.shape) == (b, hq, 1, hd), "Incorrect qkv size")
+    capi.call("l2k_decode_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), kv_lens.data_ptr(),
+              max_kv_len.data_ptr(), qk.data_ptr(), qkv.data_ptr(), b, hq, hkv, s, hd, _code(q), _stream())
 
 
 def prefill_attention_scores(q, k, q_lens, kv_lens, max_q_len, max_kv_len, qk):

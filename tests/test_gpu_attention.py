@@ -12,9 +12,10 @@ import pytest
 import torch
 
 from llama2_b200 import ops
+from oracle import chain as ochain
 from oracle import port
 from tests import golden_io
-from tests.gpu_util import TORCH, dev, host
+from tests.gpu_util import TORCH, dev, host, max_rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -24,10 +25,6 @@ F32 = np.float32
 @pytest.fixture(autouse=True)
 def _lib(cuda_lib):
     yield
-
-
-def _np_dtype(dt):
-    return {"f32": np.float32, "f16": np.float16}.get(dt)
 
 
 # ---------------------------------------------------------------------------
@@ -105,7 +102,7 @@ def test_unpad_unaligned_base_takes_the_narrow_path():
 
 def test_unpad_full_prefill_size_round_trip():
     # 8 x 2048 tokens at 7B dims in bf16 (268 MB each way): every output row
-    # is the padded row it names, checked as a checksum of row checksums.
+    # is the padded row its slot names (a torch gather of the same rows).
     b, h, qc, hd = 8, 32, 2048, 128
     qkv = torch.randn(b, h, qc, hd, device="cuda", dtype=torch.bfloat16)
     lens = [2048, 1500, 2048, 7, 2048, 1024, 2048, 333]
@@ -115,3 +112,115 @@ def test_unpad_full_prefill_size_round_trip():
     s = torch.from_numpy(slots[:t].astype(np.int64)).cuda()
     want = qkv.permute(0, 2, 1, 3).reshape(b * qc, h * hd).index_select(0, s)
     assert torch.equal(out, want)
+
+
+# ---------------------------------------------------------------------------
+# P.V and the fused decode attention
+# ---------------------------------------------------------------------------
+REL = {"f32": 1e-5, "bf16": 1e-2, "f16": 1e-2}
+
+
+def _row_rel_err(got, want):
+    """max |got - want| / max |want| per output row (the last axis)."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    scale = np.maximum(np.abs(want).max(axis=-1, keepdims=True), 1e-30)
+    return float((np.abs(got - want) / scale).max()) if want.size else 0.0
+
+
+@pytest.mark.parametrize("case", golden_io.case_ids("attention_qkv"))
+def test_attention_qkv_golden(case):
+    p, a = golden_io.load("attention_qkv")[case]
+    qk, v = dev(a["qk"]), dev(a["v"])
+    out = torch.full(a["qkv"].shape, -7.0, device="cuda")
+    ops.launch_attention_qkv(qk, v, out, p["m"], p["n"])
+    got = host(out)
+    assert _row_rel_err(got, a["qkv"]) <= 1e-5
+    assert np.all(got[:, :, p["m"]:] == -7.0), "rows >= m are left as is"
+
+
+def _attention_oracle(q, k, v, kv_lens, max_kv):
+    """Probabilities (keys < max_kv) and P.V of the chain oracle's helpers."""
+    b, hq, _, hd = q.shape
+    s = k.shape[2]
+    ones = np.ones(b, np.uint32)
+    qk = np.zeros((b, hq, 1, s), np.float32)
+    port.qk_scores(q, k, 1, max_kv, qk)
+    mask = ochain.intended_mask(ones, kv_lens, 1, max_kv, 1, s)
+    port.masked_attention_score(qk, mask, ones, max_kv, hd)
+    out = np.zeros((b, hq, 1, hd), np.float32)
+    port.attention_qkv(qk, v, 1, max_kv, out)
+    return qk, out
+
+
+def _run_decode_attention(dt, b, hq, hkv, s, hd, kv_lens, seed=0):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    td = TORCH[dt]
+    q = torch.randn(b, hq, 1, hd, generator=g, device="cuda").to(td)
+    k = torch.randn(b, hkv, s, hd, generator=g, device="cuda").to(td)
+    v = torch.randn(b, hkv, s, hd, generator=g, device="cuda").to(td)
+    kv = torch.tensor(kv_lens, dtype=torch.uint32, device="cuda")
+    mx = torch.tensor([max(kv_lens)], dtype=torch.uint32, device="cuda")
+    qk = torch.full((b, hq, 1, s), 7.0, dtype=td, device="cuda")
+    qkv = torch.full((b, hq, 1, hd), 7.0, dtype=td, device="cuda")
+    ops.decode_attention(q, k, v, kv, mx, qk, qkv)
+    torch.cuda.synchronize()
+    return q, k, v, kv, mx, qk, qkv
+
+
+@pytest.mark.parametrize("dt,b,hq,hkv,s,hd,kv_lens", [
+    ("f32", 3, 4, 4, 1000, 128, [700, 3, 1000]),       # 512-byte K/V rows, a row at the cache end
+    ("bf16", 2, 8, 2, 4096, 128, [4096, 1]),           # 256-byte rows, GQA, one key
+    ("f16", 3, 4, 2, 777, 64, [777, 400, 33]),         # 128-byte rows, a ragged last block
+    ("f32", 2, 2, 1, 300, 16, [300, 17]),              # 64-byte rows
+    ("f32", 2, 6, 6, 256, 48, [200, 256]),             # 192-byte rows: score operator + P.V kernel
+    ("bf16", 3, 4, 4, 512, 128, [0, 512, 5]),          # a sequence with no keys: a zero row
+])
+def test_decode_attention_matches_oracle(dt, b, hq, hkv, s, hd, kv_lens):
+    q, k, v, kv, mx, qk, qkv = _run_decode_attention(dt, b, hq, hkv, s, hd, kv_lens)
+    m = max(kv_lens)
+    want_qk, want_out = _attention_oracle(host(q), host(k), host(v), np.array(kv_lens, np.uint32), m)
+    got_qk = host(qk)
+    tol = REL[dt]
+    assert max_rel_err(got_qk[..., :m], want_qk[..., :m]) <= tol
+    assert np.all(got_qk[..., m:] == 7.0), "keys >= max_kv_len are left as is"
+    got = host(qkv)
+    assert _row_rel_err(got, want_out) <= tol
+    for bi, n in enumerate(kv_lens):
+        if n == 0:
+            assert not got[bi].any() and not got_qk[bi, ..., :m].any()
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_decode_attention_is_scores_plus_attention_qkv(dt):
+    """The fused operator's probabilities are bit-identical to the score
+    operator's; its output equals P.V of those probabilities through the
+    launch_linear call-site operator (within the fp32 summation-order bar)."""
+    b, hq, hkv, s, hd = 4, 8, 8, 2048, 128
+    kv_lens = [2048, 1500, 2, 999]
+    q, k, v, kv, mx, qk, qkv = _run_decode_attention(dt, b, hq, hkv, s, hd, kv_lens, seed=3)
+    qk2 = torch.full_like(qk, 7.0)
+    ops.decode_attention_scores(q, k, kv, mx, qk2)
+    out2 = torch.empty_like(qkv)
+    ops.launch_attention_qkv(qk2, v, out2, 1, max(kv_lens))
+    torch.cuda.synchronize()
+    assert torch.equal(qk, qk2)
+    # 16-bit: the fused output uses the fp32 probabilities, the call site the stored ones
+    assert _row_rel_err(host(qkv), host(out2)) <= (1e-5 if dt == "f32" else 1e-2)
+
+
+def test_decode_attention_7b_dims_against_oracle():
+    """7B dims (32 heads x 128, 4096-key cache) at four sequences, bf16."""
+    kv_lens = [4096, 2048, 1, 3333]
+    q, k, v, kv, mx, qk, qkv = _run_decode_attention("bf16", 4, 32, 32, 4096, 128, kv_lens, seed=11)
+    want_qk, want_out = _attention_oracle(host(q), host(k), host(v), np.array(kv_lens, np.uint32), 4096)
+    assert max_rel_err(host(qk), want_qk) <= 1e-2
+    assert _row_rel_err(host(qkv), want_out) <= 1e-2
+
+
+def test_decode_attention_repeatable():
+    """Fixed-order reductions: two runs give identical bits."""
+    r1 = _run_decode_attention("f32", 8, 32, 32, 4096, 128, [4096] * 8, seed=5)
+    r2 = _run_decode_attention("f32", 8, 32, 32, 4096, 128, [4096] * 8, seed=5)
+    assert torch.equal(r1[-1], r2[-1]) and torch.equal(r1[-2], r2[-2])
