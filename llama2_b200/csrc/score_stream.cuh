@@ -144,6 +144,45 @@ __device__ __forceinline__ float multi_reduce(float (&v)[R], int lane, int &idx)
     return s;
 }
 
+// Dot product of 16 bytes of a K row with this lane's slice of q, as the
+// chain sacc = fma(k_e, q_e, sacc), e = 0..N-1, from sacc = 0. For 16-bit
+// elements each step is the sm_100 mixed-precision fma (16-bit a and b,
+// fp32 c and d): it rounds a*b+c once, exactly as fmaf does on the widened
+// (exact) operands, and saves the two widening instructions per element.
+template <typename T>
+__device__ __forceinline__ float dot16(uint4 k, uint4 q, const float *qf)
+{
+    const Vec16<T> kv = as_vec<T>(k);
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < Vec16<T>::N; ++e)
+        s = fmaf(to_f(kv.v[e]), qf[e], s);
+    return s;
+}
+#define L2K_DOT16_MIXED(TYPE, PTXTYPE)                                                                       \
+    template <>                                                                                              \
+    __device__ __forceinline__ float dot16<TYPE>(uint4 k, uint4 q, const float *)                           \
+    {                                                                                                        \
+        float s;                                                                                             \
+        asm("{\n\t.reg .b16 k0, k1, k2, k3, k4, k5, k6, k7, q0, q1, q2, q3, q4, q5, q6, q7;\n\t"             \
+            "mov.b32 {k0, k1}, %1;\n\tmov.b32 {k2, k3}, %2;\n\tmov.b32 {k4, k5}, %3;\n\tmov.b32 {k6, k7}, %4;\n\t" \
+            "mov.b32 {q0, q1}, %5;\n\tmov.b32 {q2, q3}, %6;\n\tmov.b32 {q4, q5}, %7;\n\tmov.b32 {q6, q7}, %8;\n\t" \
+            "fma.rn.f32." PTXTYPE " %0, k0, q0, 0f00000000;\n\t"                                             \
+            "fma.rn.f32." PTXTYPE " %0, k1, q1, %0;\n\t"                                                     \
+            "fma.rn.f32." PTXTYPE " %0, k2, q2, %0;\n\t"                                                     \
+            "fma.rn.f32." PTXTYPE " %0, k3, q3, %0;\n\t"                                                     \
+            "fma.rn.f32." PTXTYPE " %0, k4, q4, %0;\n\t"                                                     \
+            "fma.rn.f32." PTXTYPE " %0, k5, q5, %0;\n\t"                                                     \
+            "fma.rn.f32." PTXTYPE " %0, k6, q6, %0;\n\t"                                                     \
+            "fma.rn.f32." PTXTYPE " %0, k7, q7, %0;\n\t}"                                                    \
+            : "=f"(s)                                                                                        \
+            : "r"(k.x), "r"(k.y), "r"(k.z), "r"(k.w), "r"(q.x), "r"(q.y), "r"(q.z), "r"(q.w));              \
+        return s;                                                                                            \
+    }
+L2K_DOT16_MIXED(__nv_bfloat16, "bf16")
+L2K_DOT16_MIXED(__half, "f16")
+#undef L2K_DOT16_MIXED
+
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 // Bounded wait on an mbarrier phase: false after ~2 s.
@@ -646,6 +685,7 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
 
     int n_issued = 0; // producer lane only
     float qf[N];
+    uint4 qraw;                              // the same slice as stored (16-bit types: the mixed fma's operand)
     uint4 knew = make_uint4(0u, 0u, 0u, 0u); // STEP and fresh: this lane's slice of the rotated new K row
     if (warp == kCW)
     {
@@ -728,6 +768,7 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
 #pragma unroll
         for (int e = 0; e < N; ++e)
             qf[e] = to_f(qo.v[e]);
+        qraw = as_u4(qo);
         knew = as_u4(ko);
         if (c == 0 && warp == 0 && lane < LPR)
             stg(static_cast<T *>(sa.q_out) + row * a.hd + i0, as_u4(qo));
@@ -735,7 +776,8 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
     else
     {
         const T *qrow = static_cast<const T *>(a.q) + row * a.hd;
-        const Vec16<T> qv = as_vec<T>(STEP ? ldg_coherent(qrow + i0) : ldg_keep(qrow + i0));
+        qraw = STEP ? ldg_coherent(qrow + i0) : ldg_keep(qrow + i0);
+        const Vec16<T> qv = as_vec<T>(qraw);
 #pragma unroll
         for (int e = 0; e < N; ++e)
             qf[e] = to_f(qv.v[e]);
@@ -815,13 +857,8 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
 #pragma unroll
                 for (int j = 0; j < R; ++j)
                 {
-                    const Vec16<T> kv =
-                        as_vec<T>(*reinterpret_cast<const uint4 *>(stage + (base + j * RPL) * ROW_BYTES));
-                    float sacc = 0.f;
-#pragma unroll
-                    for (int e = 0; e < N; ++e)
-                        sacc = fmaf(to_f(kv.v[e]), qf[e], sacc);
-                    part[j] = sacc;
+                    part[j] = dot16<T>(*reinterpret_cast<const uint4 *>(stage + (base + j * RPL) * ROW_BYTES), qraw,
+                                       qf);
                 }
                 int idx;
                 const float dot = multi_reduce<R, LPR>(part, lane, idx);
