@@ -19,6 +19,20 @@ void launch_prefill_attention_scores(const Tensor<T> &q, const Tensor<T> &k, con
                                      const Tensor<unsigned int> &kv_lens, const unsigned int max_q_len,
                                      const unsigned int max_kv_len, Tensor<T> &qk);
 
+// The scores of launch_decode_attention_scores (into qk) and the attention
+// output qkv (batch, Hq, 1, hd) = P.V over keys 0..kv_lens[b]-1, in one pass
+// over the K and V caches.
+template <typename T>
+void launch_decode_attention(const Tensor<T> &q, const Tensor<T> &k, const Tensor<T> &v,
+                             const Tensor<unsigned int> &kv_lens, const Tensor<unsigned int> &max_kv_len, Tensor<T> &qk,
+                             Tensor<T> &qkv);
+
+// P.V at the qk x v launch_linear call site without pointer arrays:
+// qkv[b, h, i, :] = sum_{j < N} qk[b, h, i, j] * v[b, h / (Hq/Hkv), j, :], i < M.
+template <typename T>
+void launch_attention_qkv(const Tensor<T> &qk, const Tensor<T> &v, Tensor<T> &qkv, const unsigned int M,
+                          const unsigned int N);
+
 // The whole decode chain of one layer step in one launch (no counterpart in
 // the reference): kv_lens += q_lens and max_lens = (max q_len, max kv_len);
 // x = embed_table[input_ids]; normed = RMSNorm(x) with norm_weight; RoPE of

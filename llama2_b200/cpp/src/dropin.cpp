@@ -333,6 +333,28 @@ void launch_decode_attention_scores(const Tensor<T> &q, const Tensor<T> &k, cons
 }
 
 template <typename T>
+void launch_decode_attention(const Tensor<T> &q, const Tensor<T> &k, const Tensor<T> &v,
+                             const Tensor<unsigned int> &kv_lens, const Tensor<unsigned int> &max_kv_len, Tensor<T> &qk,
+                             Tensor<T> &qkv)
+{
+    require(max_kv_len.devtype() == GPU, "max_kv_len must be a device tensor");
+    require(v.shape() == k.shape(), "Incorrect v size");
+    check(l2k_decode_attention(q.data(), k.data(), v.data(), kv_lens.data(), max_kv_len.data(), qk.data(), qkv.data(),
+                               q.shape()[0], q.shape()[1], k.shape()[1], k.shape()[2], q.shape()[3], dtype_of<T>(),
+                               nullptr),
+          "launch_decode_attention");
+}
+
+template <typename T>
+void launch_attention_qkv(const Tensor<T> &qk, const Tensor<T> &v, Tensor<T> &qkv, const unsigned int M,
+                          const unsigned int N)
+{
+    check(l2k_attention_qkv(qk.data(), v.data(), qkv.data(), qk.shape()[0], qk.shape()[1], v.shape()[1], qk.shape()[2],
+                            qk.shape()[3], v.shape()[3], M, N, dtype_of<T>(), nullptr),
+          "launch_attention_qkv");
+}
+
+template <typename T>
 void launch_prefill_attention_scores(const Tensor<T> &q, const Tensor<T> &k, const Tensor<unsigned int> &q_lens,
                                      const Tensor<unsigned int> &kv_lens, const unsigned int max_q_len,
                                      const unsigned int max_kv_len, Tensor<T> &qk)
@@ -422,6 +444,11 @@ void launch_decode_step(const Tensor<unsigned int> &q_lens, Tensor<unsigned int>
     template void launch_decode_attention_scores<T>(const Tensor<T> &, const Tensor<T> &,                           \
                                                     const Tensor<unsigned int> &, const Tensor<unsigned int> &,     \
                                                     Tensor<T> &);                                                   \
+    template void launch_decode_attention<T>(const Tensor<T> &, const Tensor<T> &, const Tensor<T> &,               \
+                                             const Tensor<unsigned int> &, const Tensor<unsigned int> &, Tensor<T> &, \
+                                             Tensor<T> &);                                                          \
+    template void launch_attention_qkv<T>(const Tensor<T> &, const Tensor<T> &, Tensor<T> &, const unsigned int,    \
+                                          const unsigned int);                                                      \
     template void launch_prefill_attention_scores<T>(const Tensor<T> &, const Tensor<T> &,                          \
                                                      const Tensor<unsigned int> &, const Tensor<unsigned int> &,    \
                                                      const unsigned int, const unsigned int, Tensor<T> &);          \

@@ -50,6 +50,8 @@ void orc_swiglu(const float *, int64_t, int64_t, float *);
 void orc_embedding(const uint32_t *, int64_t, const void *, int64_t, int64_t, void *);
 void orc_update_q_kv_lens(const uint32_t *, uint32_t *, int64_t, uint32_t *, uint32_t *);
 void orc_transpose_unpad(const void *, const uint32_t *, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, void *);
+void orc_attention_qkv(const float *, const float *, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
+                       int64_t, float *);
 }
 
 // ---------------------------------------------------------------------------
@@ -450,6 +452,49 @@ TEST(DecodeAttentionScoresTest, Fp32)
     orc_build_intended_mask(ones.data(), kv.data(), b, 1, 1000, 1, s, mask.data());
     orc_masked_attention_score(e.data(), mask.data(), ones.data(), b, h, 1, s, 1000, hd);
     EXPECT_TRUE(max_rel(download(qk_d), e) <= 1e-5f);
+}
+
+// Decode attention: the scores and P.V through the fused operator, against
+// the oracle composition (scores, then the P.V of the launch_linear site).
+TEST(DecodeAttentionTest, Fp32ScoresAndOutput)
+{
+    const unsigned int b = 2, h = 4, hd = 128, s = 700;
+    std::vector<unsigned int> kv = {700, 33};
+    std::mt19937 gen(9);
+    std::normal_distribution<float> nd(0.f, 1.f);
+    std::vector<float> q(b * h * hd), k(b * h * s * hd), v(b * h * s * hd);
+    for (auto *vec : {&q, &k, &v})
+        for (auto &x : *vec)
+            x = nd(gen);
+    Tensor<float> q_d({b, h, 1, hd}, GPU), k_d({b, h, s, hd}, GPU), v_d({b, h, s, hd}, GPU), qk_d({b, h, 1, s}, GPU),
+        o_d({b, h, 1, hd}, GPU);
+    Tensor<unsigned int> kv_d({b}, GPU), mkv({1}, GPU);
+    upload(q_d, q);
+    upload(k_d, k);
+    upload(v_d, v);
+    upload(kv_d, kv);
+    upload(mkv, std::vector<unsigned int>{700});
+    launch_decode_attention(q_d, k_d, v_d, kv_d, mkv, qk_d, o_d);
+    std::vector<float> e(b * h * s, 0.f), eo(b * h * hd, 0.f);
+    orc_qk_scores(q.data(), k.data(), b, h, h, 1, s, hd, 1, 700, e.data());
+    std::vector<uint8_t> mask(b * s, 0);
+    std::vector<unsigned int> ones(b, 1);
+    orc_build_intended_mask(ones.data(), kv.data(), b, 1, 700, 1, s, mask.data());
+    orc_masked_attention_score(e.data(), mask.data(), ones.data(), b, h, 1, s, 700, hd);
+    orc_attention_qkv(e.data(), v.data(), b, h, h, 1, s, hd, 1, 700, eo.data());
+    EXPECT_TRUE(max_rel(download(qk_d), e) <= 1e-5f);
+    // P.V elements may cancel towards 0: relative to each output row's largest magnitude
+    const std::vector<float> got = download(o_d);
+    for (unsigned int r = 0; r < b * h; ++r)
+    {
+        float mx = 0.f, err = 0.f;
+        for (unsigned int d = 0; d < hd; ++d)
+        {
+            mx = std::fmax(mx, std::fabs(eo[r * hd + d]));
+            err = std::fmax(err, std::fabs(got[r * hd + d] - eo[r * hd + d]));
+        }
+        EXPECT_TRUE(err <= 1e-5f * mx);
+    }
 }
 
 TEST(DecodeStepTest, WholeChainOneLaunch)

@@ -200,6 +200,11 @@ int attention_qkv_cuda_cores(const void *qk, const void *v, void *qkv, int64_t b
     return L2K_OK;
 }
 
+bool attention_qkv_tc_supported(int dtype, int64_t head_dim, int64_t S, int64_t n, const void *qk, const void *v,
+                                const void *qkv, int64_t grid); // attention_qkv_tc.cu
+int attention_qkv_tc(const void *qk, const void *v, void *qkv, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc,
+                     int64_t S, int64_t m, int64_t n, int dtype, cudaStream_t stream);
+
 } // namespace l2k
 
 extern "C" int l2k_linear(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda,
@@ -276,6 +281,10 @@ extern "C" int l2k_attention_qkv(const void *qk, const void *v, void *qkv, int64
     L2K_REQUIRE(kv_head_num > 0 && q_head_num % kv_head_num == 0,
                 "l2k_attention_qkv: q_head_num must be a multiple of kv_head_num");
     L2K_REQUIRE(qk && v && qkv, "l2k_attention_qkv: null pointer");
+    // 16-bit, head_dim 128: tcgen05 (P tiles by TMA, fp32 accumulator in tensor memory)
+    if (attention_qkv_tc_supported(dtype, head_dim, kv_cache_len, n, qk, v, qkv, ceil_div(m, 128) * batch * q_head_num))
+        return attention_qkv_tc(qk, v, qkv, batch, q_head_num, kv_head_num, q_cache_len, kv_cache_len, m, n, dtype,
+                                stream);
     L2K_REQUIRE_SHAPE(ceil_div(m, BM) <= 65535, "l2k_attention_qkv: m too large");
     return attention_qkv_cuda_cores(qk, v, qkv, batch, q_head_num, kv_head_num, q_cache_len, kv_cache_len, head_dim,
                                     m, n, nullptr, dtype, stream);

@@ -224,3 +224,49 @@ def test_decode_attention_repeatable():
     r1 = _run_decode_attention("f32", 8, 32, 32, 4096, 128, [4096] * 8, seed=5)
     r2 = _run_decode_attention("f32", 8, 32, 32, 4096, 128, [4096] * 8, seed=5)
     assert torch.equal(r1[-1], r2[-1]) and torch.equal(r1[-2], r2[-2])
+
+
+# ---------------------------------------------------------------------------
+# P.V on the tensor cores (16-bit, head_dim 128)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dt,b,hq,hkv,qc,s,m,n", [
+    ("bf16", 2, 4, 2, 256, 512, 256, 300),   # GQA, n not a multiple of the 64-key block
+    ("f16", 1, 2, 2, 300, 256, 200, 64),     # a partial 128-row tile, one key block
+    ("bf16", 3, 2, 1, 1, 1024, 1, 777),      # the decode call site (one row per head)
+    ("f16", 2, 2, 2, 128, 64, 128, 1),       # one key
+])
+def test_attention_qkv_tensor_cores_against_oracle(dt, b, hq, hkv, qc, s, m, n):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(n + qc)
+    td = TORCH[dt]
+    qk = torch.rand(b, hq, qc, s, generator=g, device="cuda").to(td)
+    v = torch.randn(b, hkv, s, 128, generator=g, device="cuda").to(td)
+    # entries the product must not read: keys >= n of qk and V rows >= n
+    qk[..., n:] = float("nan")
+    v[:, :, n:] = float("nan")
+    out = torch.full((b, hq, qc, 128), 7.0, dtype=td, device="cuda")
+    ops.launch_attention_qkv(qk, v, out, m, n)
+    torch.cuda.synchronize()
+    want = np.full((b, hq, qc, 128), 7.0, np.float32)
+    port.attention_qkv(host(qk), host(v), m, n, want)
+    got = host(out)
+    assert np.isfinite(got).all()
+    assert _row_rel_err(got[:, :, :m], want[:, :, :m]) <= 1e-2
+    assert np.all(got[:, :, m:] == 7.0), "rows >= m are left as is"
+
+
+def test_attention_qkv_tensor_cores_prefill_size_one_hot():
+    """7B prefill shape (8 x 32 heads, 2048 x 2048 probabilities, bf16): with
+    one-hot probability rows the product is exactly the selected V rows, so
+    the whole output is checked bit for bit at full size."""
+    b, h, qc, s = 8, 32, 2048, 2048
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    v = torch.randn(b, h, s, 128, generator=g, device="cuda", dtype=torch.bfloat16)
+    sel = torch.randint(0, s, (b, h, qc), generator=g, device="cuda")
+    qk = torch.zeros(b, h, qc, s, device="cuda", dtype=torch.bfloat16)
+    qk.scatter_(3, sel.unsqueeze(-1), 1.0)
+    out = torch.empty(b, h, qc, 128, device="cuda", dtype=torch.bfloat16)
+    ops.launch_attention_qkv(qk, v, out, qc, s)
+    want = torch.gather(v, 2, sel.unsqueeze(-1).expand(b, h, qc, 128))
+    assert torch.equal(out, want)
