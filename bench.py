@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the workload's per-GPU batch (small cases for profiling)")
+    ap.add_argument("--attention", action="store_true",
+                    help="the chain also produces the attention output: P.V (fused into the decode scores; at the "
+                         "launch_linear call site for prefill) and the transpose + unpad")
     ap.add_argument("--unfused", action="store_true",
                     help="run a decode step as the operator sequence instead of the one-launch fused step")
     return ap.parse_args()
@@ -130,10 +133,10 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baselines (oracle / reference helpers) — only the CPU legs touch oracle/
 # ---------------------------------------------------------------------------
-def cpu_chain_rate(w, inputs, seconds, impl):
+def cpu_chain_rate(w, inputs, seconds, impl, attention_output=False):
     """tokens/s of the CPU chain on a bounded sample: whole steps until `seconds`."""
     from oracle import cpu_chain
-    runner = cpu_chain.CpuChain(w, inputs, impl=impl)
+    runner = cpu_chain.CpuChain(w, inputs, impl=impl, attention_output=attention_output)
     steps, t0 = 0, time.perf_counter()
     while True:
         runner.step()
@@ -161,7 +164,7 @@ def run_ours(args, rank, world, local_rank):
     if args.batch:
         w = with_batch(w, args.batch)
     inputs = host_inputs(w, seed=0, rank=rank, kv_cache=host_cache_ok(w))
-    chain = Chain(w, inputs, device=dev, fused=not args.unfused)
+    chain = Chain(w, inputs, device=dev, fused=not args.unfused, attention_output=args.attention)
 
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     flush = torch.empty(max(2 * l2, 256 << 20) // 4, dtype=torch.float32, device=dev)
@@ -233,10 +236,14 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = sum(a.elapsed_time(b) for a, b in ev2)
 
     kv_after = inputs["kv_lens"].astype(np.int64) + inputs["q_lens"].astype(np.int64)
-    chain_bytes = algorithmic_bytes(w, kv_after)
-    # The timed kernel: the fused step (the whole chain) or the fused scores.
+    chain_bytes = algorithmic_bytes(w, kv_after, args.attention)
+    # The timed kernel: the fused step (the whole chain), the fused decode
+    # attention, or the fused scores.
     if chain.fused:
         kernel_name, kernel_key, kernel_bytes = "fused decode step", "decode_step", chain_bytes
+    elif w.decode and args.attention:
+        kernel_name, kernel_key = "fused decode attention", "attention_rows_stream"
+        kernel_bytes = scores_bytes(w, kv_after, attention_output=True)
     else:
         kernel_name = "fused decode scores" if w.decode else "fused prefill scores"
         kernel_key = "score_rows_stream" if w.decode else "prefill_scores_tc"
@@ -264,7 +271,8 @@ def run_ours(args, rank, world, local_rank):
             "data": "synthetic (seeded; N(0,1) activations and KV cache, N(0,0.02) embeddings)",
             "config": {"workload": w.name, "dim": w.dim, "heads": w.heads, "head_dim": w.head_dim,
                        "hidden": w.hidden, "kv_cache_len": w.kv_cache_len, "batch_per_gpu": w.batch,
-                       "prefill_len": w.prefill_len, "parallelism": f"sequence-batch shards x{world}",
+                       "prefill_len": w.prefill_len, "attention_output": bool(args.attention),
+                       "parallelism": f"sequence-batch shards x{world}",
                        "l2": "flushed between timed steps"},
             "chain_hbm": {"algorithmic_bytes_per_step": chain_bytes,
                           "achieved_gbs": chain_bytes / (total_ms / args.steps * 1e-3) / 1e9,
@@ -281,7 +289,8 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks.summary(),
         }
         if not args.no_cpu_baseline and world == 1:
-            result["cpu_baseline"] = cpu_chain_rate(w, inputs, args.cpu_sample_seconds, impl="port")
+            result["cpu_baseline"] = cpu_chain_rate(w, inputs, args.cpu_sample_seconds, impl="port",
+                                                    attention_output=args.attention)
     return result
 
 
@@ -307,7 +316,7 @@ def capture_with_kernel_events(chain, kev):
     dominant kernel (the fused decode step, or the fused scores)."""
     from llama2_b200 import ops
 
-    names = ("decode_step", "decode_attention_scores", "prefill_attention_scores")
+    names = ("decode_step", "decode_attention_scores", "decode_attention", "prefill_attention_scores")
     orig = {n: getattr(ops, n) for n in names}
 
     def wrap(fn):
@@ -326,13 +335,15 @@ def capture_with_kernel_events(chain, kev):
             setattr(ops, n, orig[n])
 
 
-def scores_bytes(w, kv_after):
-    """Algorithmic bytes of one fused-scores launch: q, K rows 0..pos, score rows."""
+def scores_bytes(w, kv_after, attention_output=False):
+    """Algorithmic bytes of one fused-scores launch: q, K rows 0..pos, score rows
+    (and for the fused decode attention also V rows 0..pos and the output)."""
     s = 2 if w.dtype in ("bf16", "f16") else 4
     kv = np.asarray(kv_after, np.int64)
     max_kv = int(kv.max())
     if w.decode:
-        return int(w.batch * w.dim * s + kv.sum() * w.dim * s + w.batch * w.heads * max_kv * s)
+        pv = (kv.sum() * w.dim * s + w.batch * w.dim * s) if attention_output else 0
+        return int(w.batch * w.dim * s + kv.sum() * w.dim * s + w.batch * w.heads * max_kv * s + pv)
     q = w.prefill_len
     return int(w.tokens * w.dim * s + kv.sum() * w.dim * s + w.batch * w.heads * q * max_kv * s)
 
@@ -357,7 +368,7 @@ def run_reference(args):
     w = WORKLOADS[args.workload]
     inputs = host_inputs(w, seed=0, kv_cache=host_cache_ok(w))
     impl = "ref" if cpu_chain.ref_available() else "port"
-    runner = cpu_chain.CpuChain(w, inputs, impl=impl, threads=os.cpu_count())
+    runner = cpu_chain.CpuChain(w, inputs, impl=impl, threads=os.cpu_count(), attention_output=args.attention)
     sample = runner.sample_batch()
     # Prefill: the scores of every 16th query row are computed and their time is
     # scaled by 16 (a full 2048-row step of the CPU helpers takes many seconds).
@@ -377,7 +388,7 @@ def run_reference(args):
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": {"f32": "fp32", "bf16": "bf16", "f16": "fp16"}[w.dtype],
         "data": "synthetic (seeded)",
-        "config": {"workload": w.name, "batch_per_step_sample": len(sample)},
+        "config": {"workload": w.name, "batch_per_step_sample": len(sample), "attention_output": bool(args.attention)},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": runner.threads, "kind": runner.kind,
                          "sample": f"{len(sample)} of {w.batch} sequence(s) per step, {args.steps} steps" +
                                    (f"; scores of every {stride}th query row, their time x{stride}" if stride > 1

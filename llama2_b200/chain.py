@@ -8,6 +8,12 @@ This composes the operators in the order the reference's tests exercise them
   prefill: update lens -> padding maps -> embedding -> RMSNorm
            -> prefill RoPE + KV append -> fused prefill scores -> SwiGLU
 
+With ``attention_output=True`` the chain also produces the attention output
+(tokens, D): decode runs the fused decode attention (scores and P.V in one
+pass over the K and V caches) in place of the scores; prefill follows the
+scores with P.V at the launch_linear call site (tensor cores for 16-bit) and
+the transpose + unpad.
+
 The q/k/v and gate/up activations are inputs (the projection GEMMs are not
 on this path). A decode step runs as ONE launch (ops.decode_step, the fused
 decode-step kernel) whenever its shapes are supported, else as the operator
@@ -51,8 +57,10 @@ class Packed:
 
 
 class Chain:
-    def __init__(self, w: Workload, inputs: dict, device="cuda", use_table: bool = True, fused: bool = True):
+    def __init__(self, w: Workload, inputs: dict, device="cuda", use_table: bool = True, fused: bool = True,
+                 attention_output: bool = False):
         self.w = w
+        self.attention_output = attention_output
         self.device = torch.device(device)
         dt = _TORCH[w.dtype]
         self.dtype = dt
@@ -88,11 +96,16 @@ class Chain:
         self.kv_lens_initial = self.kv_lens.clone()
         # results, packed (the small ones in one device-to-host copy per step,
         # the score rows last), and intermediates
-        self.out_specs = [("max_lens", (2,), torch.uint32), ("normed", (t, d), dt), ("ffn_out", (t, f), dt),
-                          ("qk", (b, h, qc, s), dt)]
+        self.out_specs = [("max_lens", (2,), torch.uint32), ("normed", (t, d), dt), ("ffn_out", (t, f), dt)]
+        if attention_output:
+            self.out_specs.append(("attn_out", (t, d), dt))
+        self.out_specs.append(("qk", (b, h, qc, s), dt))
         self.outputs = Packed(self.out_specs, self.device)
         self.max_lens, self.normed = self.outputs["max_lens"], self.outputs["normed"]
         self.ffn_out, self.qk = self.outputs["ffn_out"], self.outputs["qk"]
+        self.attn_out = self.outputs["attn_out"] if attention_output else None
+        if attention_output and not w.decode:
+            self.qkv_pad = torch.empty(b, h, qc, hd, dtype=dt, device=self.device)  # P.V before the unpad
         self.x = torch.empty(t, d, dtype=dt, device=self.device)
         self.q = torch.zeros(b, h, qc, hd, dtype=dt, device=self.device)
         if not w.decode:
@@ -107,7 +120,7 @@ class Chain:
         # Decode runs as one fused launch (ops.decode_step) whenever the shapes
         # allow it; otherwise, and for prefill, as the sequence of operators.
         self.fused = False
-        if w.decode and fused:
+        if w.decode and fused and not attention_output:
             self.workspace = ops.decode_step_workspace(self.device)
             self.fused = ops.decode_step_supported(**self._step_tensors())
         self.graph = None
@@ -153,7 +166,11 @@ class Chain:
             rope = (ops.launch_fused_reshape_rope_kvcache_llama2_decode if w.pairing
                     else ops.launch_fused_reshape_rope_kvcache_decode)
             rope(self.qkv, self.is_done, self.kv_lens, self.q, self.k_cache, self.v_cache, use_table=self.use_table)
-            ops.decode_attention_scores(self.q, self.k_cache, self.kv_lens, self.max_lens[1:2], self.qk)
+            if self.attention_output:
+                ops.decode_attention(self.q, self.k_cache, self.v_cache, self.kv_lens, self.max_lens[1:2], self.qk,
+                                     self.attn_out.view(w.batch, w.heads, 1, w.head_dim))
+            else:
+                ops.decode_attention_scores(self.q, self.k_cache, self.kv_lens, self.max_lens[1:2], self.qk)
         else:
             rope = (ops.launch_fused_pad_reshape_transpose_rope_kvcache_llama2 if w.pairing
                     else ops.launch_fused_pad_reshape_transpose_rope_kvcache)
@@ -161,6 +178,9 @@ class Chain:
                  use_table=self.use_table)
             ops.prefill_attention_scores(self.q, self.k_cache, self.q_lens, self.kv_lens, self.max_q, self.max_kv,
                                          self.qk)
+            if self.attention_output:
+                ops.launch_attention_qkv(self.qk, self.v_cache, self.qkv_pad, self.max_q, self.max_kv)
+                ops.launch_fused_transpose_unpad(w.tokens, self.qkv_pad, self.unpad_to_pad.view(-1), self.attn_out)
         if branches:
             for s in branches:
                 main.wait_stream(s)
@@ -173,8 +193,8 @@ class Chain:
             return 1
         if self.w.decode:
             return 6
-        # lens, maps, embedding, norm, rope, scores (+ masked softmax for fp32), swiglu
-        return 8 if self.w.dtype == "f32" else 7
+        # lens, maps, embedding, norm, rope, scores (+ masked softmax for fp32), swiglu (+ P.V, unpad)
+        return (8 if self.w.dtype == "f32" else 7) + (2 if self.attention_output else 0)
 
     def reset_lengths(self):
         """Restore the pre-step kv_lens (so a step can be repeated)."""

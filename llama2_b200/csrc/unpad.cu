@@ -4,8 +4,9 @@
 // HBM-bound gather copy. Each CTA walks output tokens (stride gridDim.x),
 // reads the token's padded slot once, and its threads copy the H head rows
 // (each hd * sizeof(T) bytes, Qc rows apart in the source) into the
-// contiguous output row in 16-byte units: read-once loads that skip L1,
-// plain stores. Rows whose byte size or base alignment is not a multiple of
+// contiguous output row in 16-byte units, four per thread with all four
+// loads in flight before the stores: read-once loads that skip L1, plain
+// stores. Rows whose byte size or base alignment is not a multiple of
 // 16 take the 2-byte path. A slot >= batch * Qc gives a zero row.
 //
 // Reference: src/kernel/fused_transpose_unpad.cu:11-73 (a grid capped at
@@ -19,6 +20,8 @@ namespace l2k
 {
 namespace
 {
+
+constexpr int kUnroll = 4; // 16-byte units in flight per thread
 
 template <typename Unit>
 __global__ void __launch_bounds__(256) transpose_unpad_kernel(const uint32_t *__restrict__ slots, int64_t n_tokens,
@@ -36,13 +39,35 @@ __global__ void __launch_bounds__(256) transpose_unpad_kernel(const uint32_t *__
         {
             const int64_t b = p / q_cache_len, i = p - b * q_cache_len;
             const Unit *base = src + (b * heads * q_cache_len + i) * units_per_head; // (b, head 0, i)
-            for (int64_t u = threadIdx.x; u < units_per_row; u += blockDim.x)
+            // kUnroll units per thread, every load issued before the stores
+            for (int64_t u0 = threadIdx.x; u0 < units_per_row; u0 += kUnroll * blockDim.x)
             {
-                const int64_t h = u / units_per_head, c = u - h * units_per_head;
-                if constexpr (sizeof(Unit) == 16)
-                    stg(out + u, ldg_stream(base + h * head_stride + c));
-                else
-                    out[u] = __ldg(base + h * head_stride + c);
+                Unit v[kUnroll];
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k)
+                {
+                    const int64_t u = u0 + k * blockDim.x;
+                    if (u < units_per_row)
+                    {
+                        const int64_t h = u / units_per_head, c = u - h * units_per_head;
+                        if constexpr (sizeof(Unit) == 16)
+                            v[k] = ldg_stream(base + h * head_stride + c);
+                        else
+                            v[k] = __ldg(base + h * head_stride + c);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < kUnroll; ++k)
+                {
+                    const int64_t u = u0 + k * blockDim.x;
+                    if (u < units_per_row)
+                    {
+                        if constexpr (sizeof(Unit) == 16)
+                            stg(out + u, v[k]);
+                        else
+                            out[u] = v[k];
+                    }
+                }
             }
         }
         else
@@ -58,7 +83,7 @@ void launch(const uint32_t *slots, int64_t n_tokens, int64_t n_slots, int64_t qc
             const void *src, void *dst, cudaStream_t stream)
 {
     const int64_t units = heads * uph;
-    const int block = (int)std::min<int64_t>(256, std::max<int64_t>(32, ceil_div(units, 32) * 32));
+    const int block = (int)std::min<int64_t>(256, std::max<int64_t>(32, ceil_div(ceil_div(units, kUnroll), 32) * 32));
     const int grid = (int)std::min<int64_t>(n_tokens, (int64_t)num_sms() * 16);
     transpose_unpad_kernel<Unit><<<grid, block, 0, stream>>>(slots, n_tokens, n_slots, qc, heads, uph,
                                                              static_cast<const Unit *>(src), static_cast<Unit *>(dst));

@@ -102,12 +102,16 @@ def host_cache_ok(w: Workload, limit_elems: int = 1 << 28) -> bool:
     return w.batch * w.heads * w.kv_cache_len * w.head_dim <= limit_elems
 
 
-def algorithmic_bytes(w: Workload, kv_lens_after: np.ndarray) -> int:
+def algorithmic_bytes(w: Workload, kv_lens_after: np.ndarray, attention_output: bool = False) -> int:
     """Mandatory HBM bytes of one chain step (reads + writes, no intermediates):
     embedding 2*D*s per token, RMSNorm 2*D*s per token + D*s weight,
     RoPE/KV 6*D*s per token (read q, k, v; write q, k row, v row), scores
     D*s (q) + K rows 0..pos (D*s per key) + H*s per score written (all keys
-    < max_kv of each row are written), SwiGLU 3*F*s per token."""
+    < max_kv of each row are written), SwiGLU 3*F*s per token.
+    attention_output adds, for decode, the V rows 0..pos (D*s per key) and
+    the output (D*s per sequence); for prefill, the P.V call site (read the
+    score matrix and V rows < max_kv, write max_q padded rows of D*s) and the
+    unpad (read and write D*s per token)."""
     s = 2 if w.dtype in ("bf16", "f16") else 4
     d, f, h = w.dim, w.hidden, w.heads
     t = w.tokens
@@ -119,9 +123,17 @@ def algorithmic_bytes(w: Workload, kv_lens_after: np.ndarray) -> int:
         total += w.batch * d * s                  # q read by the scores
         total += int(kv.sum()) * d * s            # K rows 0..pos of every head
         total += w.batch * h * max_kv * s         # score rows written
+        if attention_output:
+            total += int(kv.sum()) * d * s        # V rows 0..pos
+            total += w.batch * d * s              # attention output
     else:
         q = w.prefill_len
         total += t * d * s                        # q read
         total += w.batch * max_kv * d * s         # K read
         total += w.batch * h * q * max_kv * s     # score matrix written (zeros included)
+        if attention_output:
+            total += w.batch * h * q * max_kv * s  # score matrix read by P.V
+            total += w.batch * max_kv * d * s      # V read
+            total += w.batch * q * d * s           # padded P.V rows written
+            total += 2 * t * d * s                 # unpad: read and write
     return int(total)

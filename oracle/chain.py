@@ -30,8 +30,10 @@ def intended_mask(q_lens, kv_lens, max_q, max_kv, q_cache_len, kv_cache_len):
     return m
 
 
-def decode_step(w, inp: dict, qk_init=None) -> dict:
-    """One decode chain step on host copies. Returns every output tensor."""
+def decode_step(w, inp: dict, qk_init=None, attention_output: bool = False) -> dict:
+    """One decode chain step on host copies. Returns every output tensor; with
+    attention_output also "attn_out" (B, D): P.V of the fp32 probabilities
+    (the fused decode attention keeps them in fp32), rounded once."""
     r = rounder(w.dtype)
     b, h, hd, s = w.batch, w.heads, w.head_dim, w.kv_cache_len
     table = r(inp["embed_table"])
@@ -51,14 +53,23 @@ def decode_step(w, inp: dict, qk_init=None) -> dict:
     port.qk_scores(q, k, 1, mkv, qk)
     mask = intended_mask(inp["q_lens"], kv, 1, mkv, 1, s)
     port.masked_attention_score(qk, mask, inp["q_lens"], mkv, hd)
+    out = {}
+    if attention_output:
+        attn = np.zeros((b, h, 1, hd), np.float32)
+        port.attention_qkv(qk, v, 1, mkv, attn)
+        out["attn_out"] = r(attn.reshape(b, h * hd))
     qk = r(qk)
     ffn = r(port.swiglu(gate_up))
-    return {"x": x, "normed": normed, "q": q, "k": k, "v": v, "qk": qk, "ffn_out": ffn, "kv_lens": kv,
-            "max_q": mq, "max_kv": mkv}
+    out.update({"x": x, "normed": normed, "q": q, "k": k, "v": v, "qk": qk, "ffn_out": ffn, "kv_lens": kv,
+                "max_q": mq, "max_kv": mkv})
+    return out
 
 
-def prefill_step(w, inp: dict) -> dict:
-    """One prefill chain pass on host copies."""
+def prefill_step(w, inp: dict, attention_output: bool = False) -> dict:
+    """One prefill chain pass on host copies; with attention_output also
+    "attn_out" (tokens, D): P.V of the stored (rounded) probabilities over keys
+    < max_kv for rows < max_q (the launch_linear call site), rounded, then
+    transposed and unpadded."""
     r = rounder(w.dtype)
     b, h, hd, s, qc = w.batch, w.heads, w.head_dim, w.kv_cache_len, w.prefill_len
     table = r(inp["embed_table"])
@@ -80,9 +91,15 @@ def prefill_step(w, inp: dict) -> dict:
     mask = intended_mask(inp["q_lens"], kv, mq, mkv, qc, s)
     port.masked_attention_score(qk, mask, inp["q_lens"], mkv, hd)
     qk = r(qk)
+    out = {}
+    if attention_output:
+        attn = np.zeros((b, h, qc, hd), np.float32)
+        port.attention_qkv(qk, v, mq, mkv, attn)
+        out["attn_out"] = port.transpose_unpad(r(attn), unpad, int(np.asarray(inp["q_lens"], np.int64).sum()))
     ffn = r(port.swiglu(gate_up))
-    return {"x": x, "normed": normed, "q": q, "k": k, "v": v, "qk": qk, "ffn_out": ffn, "kv_lens": kv,
-            "max_q": mq, "max_kv": mkv, "unpad_to_pad": unpad, "seq_offsets": offs}
+    out.update({"x": x, "normed": normed, "q": q, "k": k, "v": v, "qk": qk, "ffn_out": ffn, "kv_lens": kv,
+                "max_q": mq, "max_kv": mkv, "unpad_to_pad": unpad, "seq_offsets": offs})
+    return out
 
 
 def score_row(q_row, k_rows, keep_upto, head_dim):

@@ -29,8 +29,10 @@ def ref_available() -> bool:
 
 
 class CpuChain:
-    def __init__(self, w, inputs: dict, impl: str = "port", threads: int = 1, seed: int = 0):
+    def __init__(self, w, inputs: dict, impl: str = "port", threads: int = 1, seed: int = 0,
+                 attention_output: bool = False):
         self.w = w
+        self.attention_output = attention_output
         self.impl = impl
         self.kind = "reference" if impl == "ref" else "port"
         self.threads = max(1, int(threads or 1))
@@ -118,6 +120,7 @@ class CpuChain:
         # RoPE + KV append, then scores per (sequence, head)
         q = np.zeros((nb, h, qlen, hd), np.float32)
         qk = np.zeros((nb, h, qlen, s), np.float32)
+        attn = np.zeros((nb, h, qlen, hd), np.float32) if self.attention_output else None
 
         def head_work(item):
             si, hh = item
@@ -172,6 +175,18 @@ class CpuChain:
                                                    ctypes.c_int64(1), ctypes.c_int64(max_kv), ctypes.c_int64(max_kv),
                                                    ctypes.c_int64(hd))
                     qk[si, hh, ti, :max_kv] = logits
+                if attn is not None:
+                    # P.V of this row: the launch_linear helper on (1 x max_kv) x (max_kv x hd)
+                    prow = np.ascontiguousarray(qk[si, hh, ti, :max_kv])
+                    vslice = np.ascontiguousarray(self.v[si, hh, :max_kv])
+                    orow = np.zeros(hd, np.float32)
+                    if self.impl == "ref":
+                        lib.ref_linear(P(prow), P(vslice), ctypes.c_int(0), ctypes.c_int(0), u(1), u(hd), u(max_kv),
+                                       P(orow))
+                    else:
+                        lib.orc_linear(P(prow), P(vslice), ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int64(1),
+                                       ctypes.c_int64(hd), ctypes.c_int64(max_kv), P(orow))
+                    attn[si, hh, ti] = orow
 
         self._rope_only = True
         self._map(head_work, [(si, hh) for si in range(nb) for hh in range(h)])
@@ -194,6 +209,9 @@ class CpuChain:
         self._map(swiglu, blocks)
         t_end = _time.perf_counter()
         self.last = {"normed": normed, "q": q, "qk": qk, "ffn_out": ffn, "kv_lens": kv}
+        if attn is not None:
+            # transpose + unpad: token rows (sequence-major) of H * hd
+            self.last["attn_out"] = np.ascontiguousarray(attn.transpose(0, 2, 1, 3)).reshape(nb * qlen, h * hd)
         self.last_times = {"other": (t_scores - t_start) + (t_end - t_scores_end),
                            "scores": t_scores_end - t_scores}
         return nb * qlen

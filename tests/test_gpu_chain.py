@@ -141,3 +141,43 @@ def test_end_to_end_step_reads_back_results(name, batch):
     assert max_rel_err(host(hout["qk"])[..., :m], ref["qk"][..., :m]) <= REL[w.dtype]
     h2d, d2h = ch.e2e_bytes()
     assert h2d == hin.buf.numel() and d2h < hout.buf.numel()
+
+
+# ---------------------------------------------------------------------------
+# The chain with the attention output (P.V and the transpose + unpad)
+# ---------------------------------------------------------------------------
+def _row_rel_err(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    scale = np.maximum(np.abs(want).max(axis=-1, keepdims=True), 1e-30)
+    return float((np.abs(got - want) / scale).max())
+
+
+@pytest.mark.parametrize("name,batch", [("7b-b1", 1), ("7b-b64", 3), ("7b-b64-bf16", 4), ("tiny", 1)])
+def test_decode_chain_with_attention_output(name, batch):
+    w = with_batch(WORKLOADS[name], batch)
+    inp = host_inputs(w, seed=2)
+    ch = Chain(w, inp, attention_output=True)
+    assert not ch.fused  # the one-launch step has no P.V output
+    ch.capture()
+    ch.replay()
+    torch.cuda.synchronize()
+    ref = ochain.decode_step(w, inp, attention_output=True)
+    tol = REL[w.dtype]
+    assert max_rel_err(host(ch.qk), ref["qk"]) <= tol
+    assert bits_equal(host(ch.v_cache), ref["v"])
+    assert _row_rel_err(host(ch.attn_out), ref["attn_out"]) <= tol
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_prefill_chain_with_attention_output(dtype):
+    w = dataclasses.replace(WORKLOADS["7b-prefill"], batch=2, prefill_len=192, kv_cache_len=256, dtype=dtype)
+    inp = host_inputs(w, seed=4)
+    ch = Chain(w, inp, attention_output=True)
+    assert ch.kernels_per_step() == (10 if dtype == "f32" else 9)
+    ch.step()
+    torch.cuda.synchronize()
+    ref = ochain.prefill_step(w, inp, attention_output=True)
+    tol = REL[w.dtype]
+    assert max_rel_err(host(ch.qk), ref["qk"]) <= tol
+    assert _row_rel_err(host(ch.attn_out), ref["attn_out"]) <= tol
