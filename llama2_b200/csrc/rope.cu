@@ -3,9 +3,10 @@
 //
 // Work item = VP rotation pairs of one q or k head, or 2*VP elements of one
 // v head. gridDim.x covers the items of a token, gridDim.y strides over
-// tokens, so a single decode token already spreads over several SMs. With
-// VP = 16 / (2 sizeof(T)) every item is one 16-byte load + store (interleaved)
-// or two 8-byte ones (half pairs) — no warp shuffles, any even head_dim.
+// tokens, so a single decode token already spreads over several SMs. VP is
+// chosen so that every access is 16 bytes: one load + store of 2 VP
+// elements (interleaved pairs) or one in each half of the head (half pairs),
+// with the cos/sin pairs read two per 16-byte load — no warp shuffles.
 //
 // Angles come from the host-built cos/sin table (rope_table.cpp) when the
 // reference's length-scaling factor is exactly 1 (sequence length <= 4096),
@@ -165,7 +166,15 @@ __global__ void __launch_bounds__(256) rope_kvcache_kernel(const RopeArgs a)
             // v: copy 2*VP elements into cache row pos.
             const int64_t h = head - a.hq - a.hkv;
             T *dst = static_cast<T *>(a.v) + ((seq * a.hkv + h) * a.S + pos) * a.hd;
-            if constexpr (VP > 1)
+            if constexpr (2 * VP * sizeof(T) == 32)
+            {
+                const uint4 *s4 = reinterpret_cast<const uint4 *>(src + 2 * i0);
+                uint4 *d4 = reinterpret_cast<uint4 *>(dst + 2 * i0);
+                const uint4 lo = s4[0], hi = s4[1];
+                d4[0] = lo;
+                d4[1] = hi;
+            }
+            else if constexpr (VP > 1)
             {
                 using R = typename RawT<2 * VP * sizeof(T)>::type;
                 *reinterpret_cast<R *>(dst + 2 * i0) = *reinterpret_cast<const R *>(src + 2 * i0);
@@ -198,12 +207,28 @@ __global__ void __launch_bounds__(256) rope_kvcache_kernel(const RopeArgs a)
         if (a.table && kv_len <= 4096u && (int64_t)pos < a.table_pos)
         {
             const float2 *row = a.table + (int64_t)pos * half + i0;
-#pragma unroll
-            for (int e = 0; e < VP; ++e)
+            if constexpr (VP % 2 == 0)
             {
-                const float2 cs = __ldg(row + e);
-                c[e] = cs.x;
-                s[e] = cs.y;
+                // two pairs per 16-byte load (the launcher checked the table's alignment)
+#pragma unroll
+                for (int e = 0; e < VP; e += 2)
+                {
+                    const float4 cs = __ldg(reinterpret_cast<const float4 *>(row + e));
+                    c[e] = cs.x;
+                    s[e] = cs.y;
+                    c[e + 1] = cs.z;
+                    s[e + 1] = cs.w;
+                }
+            }
+            else
+            {
+#pragma unroll
+                for (int e = 0; e < VP; ++e)
+                {
+                    const float2 cs = __ldg(row + e);
+                    c[e] = cs.x;
+                    s[e] = cs.y;
+                }
             }
         }
         else
@@ -258,7 +283,9 @@ int launch_rope_vp(const RopeArgs &a, cudaStream_t stream)
 template <typename T, int PAIRING, bool PREFILL>
 int launch_rope(const RopeArgs &a, cudaStream_t stream)
 {
-    constexpr int VPMAX = 16 / (2 * sizeof(T));
+    // 16-byte accesses: interleaved pairs 2 VP contiguous elements, half pairs
+    // VP contiguous elements in each half.
+    constexpr int VPMAX = PAIRING == L2K_ROPE_INTERLEAVED ? 16 / (2 * sizeof(T)) : 16 / sizeof(T);
     const int64_t half = a.hd / 2;
     const bool vec = half % VPMAX == 0 && (a.hd * (int64_t)sizeof(T)) % 16 == 0 && is_aligned(a.input, 16) &&
                      is_aligned(a.q, 16) && is_aligned(a.k, 16) && is_aligned(a.v, 16) &&
