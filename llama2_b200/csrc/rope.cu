@@ -3,7 +3,10 @@
 //
 // Work item = VP rotation pairs of one q or k head, or 2*VP elements of one
 // v head. gridDim.x covers the items of a token, gridDim.y strides over
-// tokens, so a single decode token already spreads over several SMs. VP is
+// tokens (runs of 8 consecutive tokens for prefill, whose q and cache rows
+// of one head are then written back to back: 256-byte rows of one head lie
+// 512 KB apart otherwise), so a single decode token already spreads over
+// several SMs. VP is
 // chosen so that every access is 16 bytes: one load + store of 2 VP
 // elements (interleaved pairs) or one in each half of the head (half pairs),
 // with the cos/sin pairs read two per 16-byte load — no warp shuffles.
@@ -32,6 +35,10 @@ namespace l2k
 {
 namespace
 {
+
+// Prefill: consecutive tokens per CTA row (decode keeps one token per row
+// for parallelism: its few tokens are latency-bound).
+constexpr int kTokRun = 8;
 
 struct RopeArgs
 {
@@ -135,7 +142,12 @@ __global__ void __launch_bounds__(256) rope_kvcache_kernel(const RopeArgs a)
     const int64_t i0 = (int64_t)(it - head * pc) * VP;
     const int64_t total_heads = a.hq + 2 * a.hkv;
 
-    for (int64_t tok = blockIdx.y; tok < a.n_tokens; tok += gridDim.y)
+    // Each CTA row takes RUN consecutive tokens (then strides by the grid), so
+    // a thread writes the consecutive cache / q rows of its head back to back.
+    constexpr int RUN = PREFILL ? kTokRun : 1;
+    for (int64_t tok0 = (int64_t)blockIdx.y * RUN; tok0 < a.n_tokens; tok0 += (int64_t)gridDim.y * RUN)
+#pragma unroll 1
+    for (int64_t tok = tok0; tok < tok0 + RUN && tok < a.n_tokens; ++tok)
     {
         int64_t seq, t;
         uint32_t kv_len, pos;
@@ -275,7 +287,7 @@ int launch_rope_vp(const RopeArgs &a, cudaStream_t stream)
     const int64_t items = (a.hq + 2 * a.hkv) * pc;
     const int block = (int)std::min<int64_t>(256, std::max<int64_t>(32, ceil_div(items, 32) * 32));
     const int64_t gx = ceil_div(items, block);
-    const int64_t gy = std::min<int64_t>(a.n_tokens, 65535);
+    const int64_t gy = std::min<int64_t>(ceil_div(a.n_tokens, PREFILL ? kTokRun : 1), 65535);
     rope_kvcache_kernel<T, PAIRING, VP, PREFILL><<<dim3((unsigned)gx, (unsigned)gy), block, 0, stream>>>(a);
     return check_launch(PREFILL ? "l2k prefill rope" : "l2k decode rope");
 }
