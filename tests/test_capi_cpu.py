@@ -59,6 +59,12 @@ def test_status_strings():
     ("l2k_fused_transpose_unpad", (3, None, None, None, 2, 4, 8, 16, 0, None), 1),   # null pointers
     ("l2k_fused_transpose_unpad", (17, None, None, None, 2, 4, 8, 16, 0, None), 1),  # more tokens than slots
     ("l2k_fused_transpose_unpad", (1, None, None, None, 2, 4, 8, 16, 5, None), 1),   # dtype
+    ("l2k_attention_qkv", (None, None, None, 2, 4, 2, 8, 16, 128, 4, 8, 2, None), 1),  # null pointers
+    ("l2k_attention_qkv", (None, None, None, 2, 4, 2, 8, 16, 128, 9, 8, 2, None), 1),  # m > q_cache_len
+    ("l2k_attention_qkv", (None, None, None, 2, 4, 3, 8, 16, 128, 4, 8, 2, None), 1),  # Hq % Hkv
+    ("l2k_decode_attention", (None, None, None, None, None, None, None, 2, 4, 2, 64, 128, 0, None), 1),
+    ("l2k_decode_attention", (None, None, None, None, None, None, None, 2, 4, 3, 64, 128, 0, None), 1),
+    ("l2k_decode_attention", (None, None, None, None, None, None, None, 2, 4, 2, 64, 0, 0, None), 1),
 ])
 def test_bad_arguments_are_rejected(call, args, status):
     with pytest.raises(capi.L2KError) as e:
@@ -73,6 +79,8 @@ def test_empty_inputs_are_noops():
     capi.call("l2k_swiglu", None, None, 0, 16, 2, None)
     capi.call("l2k_fused_add_residual_rmsnorm", None, None, None, 0, 64, 1, 1, None)
     capi.call("l2k_fused_transpose_unpad", 0, None, None, None, 2, 4, 8, 16, 1, None)
+    capi.call("l2k_attention_qkv", None, None, None, 0, 4, 2, 8, 16, 128, 4, 8, 2, None)
+    capi.call("l2k_decode_attention", None, None, None, None, None, None, None, 0, 4, 2, 64, 128, 2, None)
 
 
 @pytest.mark.parametrize("hd", [2, 4, 48, 64, 128])
