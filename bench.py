@@ -11,13 +11,14 @@ on its own GPU (sharding by sequence batch; no collective on the data path),
 so scaling is weak; time is the max over ranks of the summed per-step device
 time (CUDA events), and value = tokens of all ranks / that time.
 
-Between timed steps the sequence lengths are restored and, unless the step
-itself moves more than 4 x L2 of HBM traffic (then its inputs are larger
-than L2 and nothing of one step survives in L2 for the next), the L2 cache
-is flushed by writing a 2 x L2-sized buffer — outside the timed windows,
-though the flush's dirty lines are still being written back when the next
-step starts. `--l2-flush always` flushes before every step regardless;
-`config.l2` says which was done.
+Between timed steps the sequence lengths are restored and the L2 cache is
+flushed: a 2 x L2-sized buffer is written, then another one read, so that
+L2 holds none of the step's data and the written lines have gone back to
+HBM before the next step starts — all outside the timed windows.
+`--l2-flush write` flushes by the write alone (its dirty lines are then
+written back while the next step runs, which costs short HBM-bound steps
+up to 5 %), `--l2-flush auto` skips the flush when a step moves more than
+4 x L2; `config.l2` says which was done.
 
 --impl reference times the reference's own CPU implementation of the path
 (its CPU test helpers compiled from its sources, oracle/_ref; the C
@@ -58,8 +59,11 @@ def parse():
     ap.add_argument("--attention", action="store_true",
                     help="the chain also produces the attention output: P.V (fused into the decode scores; at the "
                          "launch_linear call site for prefill) and the transpose + unpad")
-    ap.add_argument("--l2-flush", default="auto", choices=["auto", "always"],
-                    help="auto: flush L2 between steps only when a step moves less than 4 x L2")
+    ap.add_argument("--l2-flush", default="always", choices=["always", "write", "auto"],
+                    help="always: before every step, a 2 x L2 write then a 2 x L2 read (the written lines "
+                         "go back to HBM before the step); write: the write alone (its dirty lines are "
+                         "written back while the next step runs); auto: as always, but no flush when a "
+                         "step moves more than 4 x L2")
     ap.add_argument("--unfused", action="store_true",
                     help="run a decode step as the operator sequence instead of the one-launch fused step")
     return ap.parse_args()
@@ -176,12 +180,19 @@ def run_ours(args, rank, world, local_rank):
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     kv_after = inputs["kv_lens"].astype(np.int64) + inputs["q_lens"].astype(np.int64)
     chain_bytes = algorithmic_bytes(w, kv_after, args.attention)
-    flush_each = args.l2_flush == "always" or chain_bytes < 4 * l2
+    flush_each = args.l2_flush != "auto" or chain_bytes < 4 * l2
     flush_buf = torch.empty(max(2 * l2, 256 << 20) // 4, dtype=torch.float32, device=dev)
+    drain_buf = torch.ones(max(2 * l2, 256 << 20) // 4, dtype=torch.float32, device=dev) \
+        if args.l2_flush != "write" else None
 
     def flush():
+        """Evict L2: write a 2 x L2 buffer, then (unless --l2-flush write) read
+        another one, so that the written lines are evicted (written back to
+        HBM) here, outside the timed window, instead of during the next step."""
         if flush_each:
             flush_buf.zero_()
+            if drain_buf is not None:
+                drain_buf.sum()
 
     def barrier():
         if world > 1:
@@ -285,7 +296,8 @@ def run_ours(args, rank, world, local_rank):
                        "hidden": w.hidden, "kv_cache_len": w.kv_cache_len, "batch_per_gpu": w.batch,
                        "prefill_len": w.prefill_len, "attention_output": bool(args.attention),
                        "parallelism": f"sequence-batch shards x{world}",
-                       "l2": ("flushed between timed steps (2 x L2 written)" if flush_each else
+                       "l2": (("flushed between timed steps (2 x L2 written" +
+                               (")" if drain_buf is None else ", then 2 x L2 read to evict it)")) if flush_each else
                               f"not flushed: inputs larger than L2 ({chain_bytes / 1e9:.2f} GB per step, "
                               f"> 4 x L2)")},
             "chain_hbm": {"algorithmic_bytes_per_step": chain_bytes,
