@@ -264,6 +264,8 @@ def run_ours(args, rank, world, local_rank):
     # attention, or the fused scores.
     if chain.fused:
         kernel_name, kernel_key, kernel_bytes = "fused decode step", "decode_step", chain_bytes
+        if args.attention:
+            kernel_name, kernel_key = "fused decode step with P.V", "decode_step_attention"
     elif w.decode and args.attention:
         kernel_name, kernel_key = "fused decode attention", "attention_rows_stream"
         kernel_bytes = scores_bytes(w, kv_after, attention_output=True)
@@ -342,7 +344,8 @@ def capture_with_kernel_events(chain, kev):
     dominant kernel (the fused decode step, or the fused scores)."""
     from llama2_b200 import ops
 
-    names = ("decode_step", "decode_attention_scores", "decode_attention", "prefill_attention_scores")
+    names = ("decode_step", "decode_step_attention", "decode_attention_scores", "decode_attention",
+             "prefill_attention_scores")
     orig = {n: getattr(ops, n) for n in names}
 
     def wrap(fn):

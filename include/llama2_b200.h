@@ -386,6 +386,19 @@ int l2k_decode_step_supported(const l2k_decode_step_args *args);
 int l2k_decode_step(const l2k_decode_step_args *args, uint32_t *workspace, l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * The fused decode step with the attention output: everything
+ * l2k_decode_step computes, and in the same launch
+ *   attn_out[b, h, 0, :] = sum_{j <= pos} qk[b, h, 0, j] * v_cache[b, h / (Hq/Hkv), j, :]
+ * over the appended cache (fp32 probabilities and accumulation), i.e. the
+ * results of l2k_decode_attention in place of l2k_decode_attention_scores.
+ * attn_out: (batch, Hq, 1, head_dim), 16-byte aligned — also the unpadded
+ * (batch, Hq * head_dim) layout. Same shape coverage as l2k_decode_step
+ * (l2k_decode_step_supported).
+ * ------------------------------------------------------------------------ */
+int l2k_decode_step_attention(const l2k_decode_step_args *args, void *attn_out, uint32_t *workspace,
+                              l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * l2k_decode_step without a workspace argument, for callers that cannot
  * provide device memory (for example a binding whose host side only passes
  * the tensors it already has and owns no device allocator). The workspace is

@@ -9,10 +9,11 @@ This composes the operators in the order the reference's tests exercise them
            -> prefill RoPE + KV append -> fused prefill scores -> SwiGLU
 
 With ``attention_output=True`` the chain also produces the attention output
-(tokens, D): decode runs the fused decode attention (scores and P.V in one
-pass over the K and V caches) in place of the scores; prefill follows the
-scores with P.V at the launch_linear call site (tensor cores for 16-bit) and
-the transpose + unpad.
+(tokens, D): the one-launch decode step computes it in the same pass
+(l2k_decode_step_attention; the operator sequence runs the fused decode
+attention in place of the scores); prefill follows the scores with P.V at
+the launch_linear call site (tensor cores for 16-bit) and the transpose +
+unpad.
 
 The q/k/v and gate/up activations are inputs (the projection GEMMs are not
 on this path). A decode step runs as ONE launch (ops.decode_step, the fused
@@ -120,7 +121,7 @@ class Chain:
         # Decode runs as one fused launch (ops.decode_step) whenever the shapes
         # allow it; otherwise, and for prefill, as the sequence of operators.
         self.fused = False
-        if w.decode and fused and not attention_output:
+        if w.decode and fused:
             self.workspace = ops.decode_step_workspace(self.device)
             self.fused = ops.decode_step_supported(**self._step_tensors())
         self.graph = None
@@ -145,7 +146,11 @@ class Chain:
         longest of them instead of their sum."""
         w = self.w
         if self.fused:
-            ops.decode_step(**self._step_tensors(), workspace=self.workspace)
+            if self.attention_output:
+                ops.decode_step_attention(**self._step_tensors(), workspace=self.workspace,
+                                          attn_out=self.attn_out.view(w.batch, w.heads, 1, w.head_dim))
+            else:
+                ops.decode_step(**self._step_tensors(), workspace=self.workspace)
             return
         main = torch.cuda.current_stream(self.device)
         ops.launch_update_q_kv_lens(self.q_lens, self.kv_lens, self.max_lens[0:1], self.max_lens[1:2])

@@ -5,11 +5,13 @@
 //   q, k_cache[pos], v_cache[pos] = RoPE(qkv), pos = kv_len - 1 (fused RoPE + KV append)
 //   qk = softmax(q K^T / sqrt(hd), keys 0..pos)                 (QK^T + masked softmax)
 //   ffn_out = silu(gate) * up                                   (SwiGLU)
+//   [attn_out = qk V over keys 0..pos                           (l2k_decode_step_attention)]
 //
 // with exactly the results of those operators run one after another
 // (l2k_update_q_kv_lens, l2k_embedding, l2k_fused_add_residual_rmsnorm
 // without add, l2k_fused_reshape_rope_kvcache[_llama2]_decode,
-// l2k_decode_attention_scores, l2k_swiglu).
+// l2k_decode_attention_scores — l2k_decode_attention with the attention
+// output — , l2k_swiglu).
 //
 // At small batch every one of those kernels is latency-bound (a 7B batch-1
 // step moves ~9-35 MB, a few microseconds of HBM time, while each launch and
@@ -141,7 +143,9 @@ __device__ __forceinline__ void swiglu_range(const StepArgs &a, int64_t n)
     }
 }
 
-template <typename T, int LPR>
+// PV: the score rows also produce the attention output P.V (the V blocks
+// stream after the K blocks; this step's V row is patched in like the K row).
+template <typename T, int LPR, bool PV>
 __global__ void __launch_bounds__(kStreamThreads) decode_step_kernel(const StepArgs a)
 {
     extern __shared__ __align__(128) uint8_t step_smem[];
@@ -151,8 +155,8 @@ __global__ void __launch_bounds__(kStreamThreads) decode_step_kernel(const StepA
     {
         // (takes its ticket for the length update inside)
         cg::cluster_group cluster = cg::this_cluster();
-        score_row_stream<T, LPR, true>(a.d, a.r, bid / (int64_t)cluster.num_blocks(), cluster, step_smem, sh,
-                                       &g_step_error);
+        score_row_stream<T, LPR, true, PV>(a.d, a.r, bid / (int64_t)cluster.num_blocks(), cluster, step_smem, sh,
+                                           &g_step_error);
         return;
     }
     // Other roles read no lengths: their ticket comes first.
@@ -168,13 +172,14 @@ struct Plan
 {
     int lpr;
     int C;
+    bool pv;
     size_t smem;
     StepArgs k;
 };
 
 // Validates the arguments and lays out the grid; L2K_OK or a status.
 template <typename T>
-int plan_step(const l2k_decode_step_args &p, uint32_t *workspace, Plan &plan)
+int plan_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace, Plan &plan)
 {
     constexpr int N = Vec16<T>::N;
     const int64_t row_bytes = p.head_dim * (int64_t)sizeof(T);
@@ -201,9 +206,11 @@ int plan_step(const l2k_decode_step_args &p, uint32_t *workspace, Plan &plan)
     int C = 1;
     while (C < 8 && rows * C < 3LL * num_sms() && C * 2 <= blocks_per_row)
         C *= 2;
-    const size_t smem = stream_smem_bytes(p.kv_cache_len, row_bytes, C);
+    const size_t smem = stream_smem_bytes(p.kv_cache_len, row_bytes, C) + (attn_out ? pv_smem_bytes(p.head_dim) : 0);
     L2K_REQUIRE_SHAPE(smem <= (size_t)kNS * kBlockBytes + 128 * 1024, "l2k_decode_step: kv_cache_len %lld too long",
                       (long long)p.kv_cache_len);
+    L2K_REQUIRE_SHAPE(attn_out == nullptr || is_aligned(attn_out, 16),
+                      "l2k_decode_step_attention: attn_out must be 16-byte aligned");
 
     StepArgs &k = plan.k;
     k = StepArgs{};
@@ -211,6 +218,8 @@ int plan_step(const l2k_decode_step_args &p, uint32_t *workspace, Plan &plan)
                      p.q_head_num / p.kv_head_num, p.kv_head_num, 1, p.kv_cache_len, p.head_dim, 0,
                      1.f / sqrtf((float)p.head_dim),
                      (p.kv_cache_len * (int64_t)sizeof(T)) % 16 == 0 && is_aligned(p.qk, 16)};
+    k.d.v = p.v_cache;
+    k.d.qkv = attn_out; // (B, Hq, 1, hd); null without the attention output
     k.r = StepRowArgs{p.qkv, p.is_done, p.q_lens, p.kv_lens, p.max_lens, workspace, p.q, p.k_cache, p.v_cache,
                       reinterpret_cast<const float2 *>(p.rope_table), p.rope_table ? p.rope_table_positions : 0,
                       p.batch, (p.q_head_num + 2 * p.kv_head_num) * p.head_dim, p.pairing};
@@ -233,14 +242,15 @@ int plan_step(const l2k_decode_step_args &p, uint32_t *workspace, Plan &plan)
     L2K_REQUIRE_SHAPE(k.score_ctas + aux < (int64_t(1) << 31), "l2k_decode_step: grid too large");
     plan.lpr = lpr;
     plan.C = C;
+    plan.pv = attn_out != nullptr;
     plan.smem = smem;
     return L2K_OK;
 }
 
-template <typename T, int LPR>
+template <typename T, int LPR, bool PV>
 cudaError_t launch_step_kernel(const Plan &plan, cudaStream_t stream)
 {
-    auto kernel = decode_step_kernel<T, LPR>;
+    auto kernel = decode_step_kernel<T, LPR, PV>;
     if (plan.smem > 48 * 1024)
     {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
@@ -263,36 +273,37 @@ cudaError_t launch_step_kernel(const Plan &plan, cudaStream_t stream)
     return cudaLaunchKernelEx(&cfg, kernel, plan.k);
 }
 
-template <typename T>
-int run_step(const l2k_decode_step_args &p, uint32_t *workspace, cudaStream_t stream, bool launch)
+template <typename T, bool PV>
+cudaError_t launch_step_lpr(const Plan &plan, cudaStream_t stream)
 {
-    Plan plan;
-    if (int st = plan_step<T>(p, workspace, plan))
-        return st;
-    if (!launch)
-        return L2K_OK;
-    cudaError_t e;
     switch (plan.lpr)
     {
     case 32:
-        e = launch_step_kernel<T, 32>(plan, stream);
-        break;
+        return launch_step_kernel<T, 32, PV>(plan, stream);
     case 16:
-        e = launch_step_kernel<T, 16>(plan, stream);
-        break;
+        return launch_step_kernel<T, 16, PV>(plan, stream);
     case 8:
-        e = launch_step_kernel<T, 8>(plan, stream);
-        break;
+        return launch_step_kernel<T, 8, PV>(plan, stream);
     default:
-        e = launch_step_kernel<T, 4>(plan, stream);
-        break;
+        return launch_step_kernel<T, 4, PV>(plan, stream);
     }
+}
+
+template <typename T>
+int run_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace, cudaStream_t stream, bool launch)
+{
+    Plan plan;
+    if (int st = plan_step<T>(p, attn_out, workspace, plan))
+        return st;
+    if (!launch)
+        return L2K_OK;
+    const cudaError_t e = plan.pv ? launch_step_lpr<T, true>(plan, stream) : launch_step_lpr<T, false>(plan, stream);
     if (e != cudaSuccess)
         return set_error(L2K_ERR_CUDA, "l2k_decode_step: %s", cudaGetErrorString(e));
     return check_launch("l2k_decode_step");
 }
 
-int step_entry(const l2k_decode_step_args *pp, uint32_t *workspace, cudaStream_t stream, bool launch)
+int step_entry(const l2k_decode_step_args *pp, void *attn_out, uint32_t *workspace, cudaStream_t stream, bool launch)
 {
     L2K_REQUIRE(pp != nullptr, "l2k_decode_step: null args");
     const l2k_decode_step_args &p = *pp;
@@ -312,7 +323,7 @@ int step_entry(const l2k_decode_step_args *pp, uint32_t *workspace, cudaStream_t
                 "l2k_decode_step: null pointer");
     L2K_REQUIRE(p.hidden == 0 || (p.gate_up && p.ffn_out), "l2k_decode_step: null gate_up / ffn_out");
     L2K_REQUIRE(p.x != p.normed, "l2k_decode_step: x and normed must be distinct buffers");
-    L2K_DISPATCH(p.dtype, { return run_step<T>(p, workspace, stream, launch); });
+    L2K_DISPATCH(p.dtype, { return run_step<T>(p, attn_out, workspace, stream, launch); });
     return L2K_OK;
 }
 
@@ -339,12 +350,19 @@ extern "C" int64_t l2k_decode_step_workspace_bytes(void) { return 16; }
 extern "C" int l2k_decode_step_supported(const l2k_decode_step_args *args)
 {
     uint32_t dummy = 0; // never dereferenced: nothing is launched
-    return l2k::step_entry(args, &dummy, nullptr, false);
+    return l2k::step_entry(args, nullptr, &dummy, nullptr, false);
 }
 
 extern "C" int l2k_decode_step(const l2k_decode_step_args *args, uint32_t *workspace, l2k_stream_t stream)
 {
-    return l2k::step_entry(args, workspace, stream, true);
+    return l2k::step_entry(args, nullptr, workspace, stream, true);
+}
+
+extern "C" int l2k_decode_step_attention(const l2k_decode_step_args *args, void *attn_out, uint32_t *workspace,
+                                         l2k_stream_t stream)
+{
+    L2K_REQUIRE(attn_out != nullptr, "l2k_decode_step_attention: null attn_out");
+    return l2k::step_entry(args, attn_out, workspace, stream, true);
 }
 
 // ---------------------------------------------------------------------------
@@ -397,5 +415,5 @@ extern "C" int l2k_decode_step_no_alloc(const l2k_decode_step_args *args, l2k_st
         }
         scratch = g_scratch_ptr[dev];
     }
-    return step_entry(args, scratch, stream, true);
+    return step_entry(args, nullptr, scratch, stream, true);
 }

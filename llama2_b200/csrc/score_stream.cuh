@@ -383,10 +383,17 @@ __device__ __forceinline__ void prefetch_first_blocks(const DecodeArgs &a, int64
 // CTA's V blocks (ring sequences n_mine + i, i < n_mine), and the reduction
 // lanes -> warps -> cluster ranks, the ranks' rows summed by rank 0 in rank
 // order and written to qkv[row].
+//
+// In the fused decode step the V row at this step's position is still being
+// written to the cache (by the CTA that owns its block), so the warp that
+// folds that block replaces the row in shared memory with the new V row
+// (vnew_src, this lane's 16-byte slice read at the start) before folding;
+// patch_pos < 0 when there is nothing to patch.
 template <typename T, int LPR>
 __device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, const RowInfo &ri,
                                        const int64_t n_keys, const int n_mine, const int c, const int C,
-                                       const float2 row_stat, uint8_t *smem, StreamShared &sh, int *err)
+                                       const float2 row_stat, uint8_t *smem, StreamShared &sh, int *err,
+                                       const int64_t patch_pos = -1, const T *vnew_src = nullptr)
 {
     constexpr int N = Vec16<T>::N;
     constexpr int ROW_BYTES = LPR * 16;
@@ -408,6 +415,23 @@ __device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, c
         if (gather)
             bar_wait(smem_addr(&sh.pvbar), 0);
     };
+    // The warp (stage, half) that will fold the V block holding patch_pos
+    // reads its slice of the new V row now, ahead of need.
+    int patch_i = -1, patch_r = -1;
+    uint4 vnew = make_uint4(0u, 0u, 0u, 0u);
+    if (patch_pos >= 0)
+    {
+        const int64_t g = patch_pos / KB;
+        const int rib = (int)(patch_pos - g * KB);
+        if (g % C == c && (g - c) / C < n_mine && (int)((n_mine + (g - c) / C) % kNS) == warp % kNS &&
+            rib / HALF == warp / kNS)
+        {
+            patch_i = (int)((g - c) / C);
+            patch_r = rib - (warp / kNS) * HALF;
+            if (lane < LPR)
+                vnew = ldg_keep(vnew_src + lane * (16 / (int)sizeof(T)));
+        }
+    }
     if (consumers_any(sh.abort_flag != 0))
         return leave();
 
@@ -447,6 +471,16 @@ __device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, c
                 atomicCAS(err, 0, 0x204);
                 sh.abort_flag = 1;
                 break;
+            }
+            if (i == patch_i)
+            {
+                // this step's V row: stale in the cache copy, replaced by the new row
+                if (lane < LPR)
+                {
+                    *reinterpret_cast<uint4 *>(const_cast<uint8_t *>(stage) + patch_r * ROW_BYTES) = vnew;
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); // before the stage is refilled
+                }
+                __syncwarp();
             }
             const int64_t valid = n_keys - (c + (int64_t)C * i) * KB - hf * HALF; // rows of this half with keys
             const float *pr = logits + i * KB + hf * HALF;
@@ -538,8 +572,8 @@ __device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, c
 // each other's shared memory before a single cluster barrier; probabilities
 // are staged in the (now idle) ring and written with cp.async.bulk stores.
 //
-// PV rows (attention output, flash-decode style) also stream the V rows of
-// the same blocks: once its K blocks are issued the producer lane continues
+// PV rows (attention output, flash-decode style; also in the fused decode
+// step) also stream the V rows of the same blocks: once its K blocks are issued the producer lane continues
 // with the V blocks into the same ring (the first kNS while the consumers
 // still finish the keys), and after the cluster's statistics are known the
 // consumers turn their logits into probabilities in place, store them, and
@@ -552,7 +586,6 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                                                  cg::cluster_group &cluster, uint8_t *smem, StreamShared &sh,
                                                  int *err)
 {
-    static_assert(!(STEP && PV), "the decode step has no P.V output");
     constexpr int N = Vec16<T>::N;
     constexpr int ROW_BYTES = LPR * 16;
     constexpr int KB = kBlockBytes / ROW_BYTES; // K rows per block
@@ -966,7 +999,14 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
     }
     if constexpr (PV)
     {
-        pv_row<T, LPR>(a, row, ri, n_keys, n_mine, c, C, row_stat, smem, sh, err);
+        if constexpr (STEP)
+        {
+            const T *vsrc = static_cast<const T *>(sa.qkv) + ri.b * sa.qkv_stride + (a.Hq + a.Hkv + kvh) * a.hd;
+            pv_row<T, LPR>(a, row, ri, n_keys, n_mine, c, C, row_stat, smem, sh, err, fresh ? (int64_t)pos : -1,
+                           vsrc);
+        }
+        else
+            pv_row<T, LPR>(a, row, ri, n_keys, n_mine, c, C, row_stat, smem, sh, err);
         return;
     }
     if (consumers_any(sh.abort_flag != 0))

@@ -409,6 +409,19 @@ def decode_step(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weigh
     capi.call("l2k_decode_step", ctypes.byref(args), workspace.data_ptr(), _stream())
 
 
+def decode_step_attention(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv,
+                          is_done, q, k_cache, v_cache, qk, gate_up, ffn_out, attn_out, workspace, pairing,
+                          use_table=True):
+    """decode_step plus the attention output attn_out (B, Hq, 1, hd) = P.V over
+    the appended V cache, in the same launch (l2k_decode_step_attention)."""
+    args = _decode_step_args(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done,
+                             q, k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table)
+    _dev(workspace, attn_out)
+    _same(qk, attn_out, "decode_step_attention")
+    _require(attn_out.numel() == q.numel(), "attn_out must hold (batch, Hq, 1, head_dim)")
+    capi.call("l2k_decode_step_attention", ctypes.byref(args), attn_out.data_ptr(), workspace.data_ptr(), _stream())
+
+
 def decode_step_no_alloc(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv,
                          is_done, q, k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table=True):
     """decode_step with the library's own static scratch as workspace

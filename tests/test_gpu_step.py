@@ -211,3 +211,58 @@ def test_row_widths_against_operator_sequence(dtype, hd, pairing, S):
     for n in ("kv_lens", "max_lens", "x", "q", "k_cache", "v_cache", "qk", "ffn_out"):
         assert bits_equal(host(f[n]), host(u[n])), n
     assert max_rel_err(host(f["normed"]), host(u["normed"])) <= (1e-5 if dtype == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("dtype,hd,pairing,S,hq,hkv", [
+    (torch.float32, 128, 1, 4096, 8, 8),    # 512-byte rows (7B head)
+    (torch.bfloat16, 128, 1, 2048, 8, 2),   # 256-byte rows, GQA
+    (torch.float16, 64, 0, 1000, 4, 4),     # 128-byte rows, ragged last block
+    (torch.float32, 16, 1, 300, 4, 2),      # 64-byte rows
+])
+def test_step_attention_matches_operator_sequence(dtype, hd, pairing, S, hq, hkv):
+    """l2k_decode_step_attention against the operator sequence with the fused
+    decode attention in place of the scores: every output bit-identical (the
+    new V row is patched into its block exactly as the cache receives it),
+    RMSNorm within its tolerance."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(hd + S + hkv)
+    B, F, V = 3, 256, 500
+    D = hq * hd
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(dtype)
+
+    base = dict(q_lens=torch.ones(B, dtype=torch.uint32, device=dev),
+                input_ids=torch.tensor([3, 499, 250], dtype=torch.uint32, device=dev),
+                embed_table=rnd(V, D, scale=0.02), norm_weight=(torch.rand(D, generator=g, device=dev) + 0.5).to(dtype),
+                qkv=rnd(B, (hq + 2 * hkv) * hd), is_done=torch.tensor([0, 1, 0], dtype=torch.uint8, device=dev),
+                gate_up=rnd(B, 2 * F))
+    kv0 = torch.tensor([S // 2, 5, S - 1], dtype=torch.uint32, device=dev)
+    k0, v0 = rnd(B, hkv, S, hd), rnd(B, hkv, S, hd)
+
+    def fresh():
+        return dict(kv_lens=kv0.clone(), max_lens=torch.zeros(2, dtype=torch.uint32, device=dev),
+                    x=torch.empty(B, D, dtype=dtype, device=dev), normed=torch.empty(B, D, dtype=dtype, device=dev),
+                    q=torch.zeros(B, hq, 1, hd, dtype=dtype, device=dev), k_cache=k0.clone(), v_cache=v0.clone(),
+                    qk=torch.full((B, hq, 1, S), 7.0, dtype=dtype, device=dev),
+                    ffn_out=torch.empty(B, F, dtype=dtype, device=dev))
+
+    f = fresh()
+    out_f = torch.full((B, hq, 1, hd), 7.0, dtype=dtype, device=dev)
+    assert ops.decode_step_supported(**base, **f, pairing=pairing)
+    ops.decode_step_attention(**base, **f, attn_out=out_f, workspace=ops.decode_step_workspace(dev), pairing=pairing)
+    u = fresh()
+    out_u = torch.full((B, hq, 1, hd), 7.0, dtype=dtype, device=dev)
+    ops.launch_update_q_kv_lens(base["q_lens"], u["kv_lens"], u["max_lens"][0:1], u["max_lens"][1:2])
+    ops.launch_embedding(base["input_ids"], base["embed_table"], u["x"])
+    ops.launch_fused_add_residual_rmsnorm(base["norm_weight"], u["x"], u["normed"], False)
+    rope = ops.launch_fused_reshape_rope_kvcache_llama2_decode if pairing else ops.launch_fused_reshape_rope_kvcache_decode
+    rope(base["qkv"], base["is_done"], u["kv_lens"], u["q"], u["k_cache"], u["v_cache"])
+    ops.decode_attention(u["q"], u["k_cache"], u["v_cache"], u["kv_lens"], u["max_lens"][1:2], u["qk"], out_u)
+    ops.launch_swiglu(base["gate_up"], u["ffn_out"])
+    torch.cuda.synchronize()
+    for n in ("kv_lens", "max_lens", "x", "q", "k_cache", "v_cache", "qk", "ffn_out"):
+        assert bits_equal(host(f[n]), host(u[n])), n
+    assert bits_equal(host(out_f), host(out_u)), "attention output"
+    assert max_rel_err(host(f["normed"]), host(u["normed"])) <= (1e-5 if dtype == torch.float32 else 1e-2)
