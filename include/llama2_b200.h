@@ -397,6 +397,8 @@ int l2k_decode_step(const l2k_decode_step_args *args, uint32_t *workspace, l2k_s
  * ------------------------------------------------------------------------ */
 int l2k_decode_step_attention(const l2k_decode_step_args *args, void *attn_out, uint32_t *workspace,
                               l2k_stream_t stream);
+/* The same on the library's static scratch (see l2k_decode_step_no_alloc). */
+int l2k_decode_step_attention_no_alloc(const l2k_decode_step_args *args, void *attn_out, l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * l2k_decode_step without a workspace argument, for callers that cannot

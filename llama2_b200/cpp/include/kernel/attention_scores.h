@@ -49,3 +49,15 @@ void launch_decode_step(const Tensor<unsigned int> &q_lens, Tensor<unsigned int>
                         const Tensor<T> &qkv, const Tensor<unsigned char> &is_done, Tensor<T> &q, Tensor<T> &k_cache,
                         Tensor<T> &v_cache, Tensor<T> &qk, const Tensor<T> &gate_up, Tensor<T> &ffn_out,
                         bool llama2_pairs);
+
+// launch_decode_step with the attention output attn_out (batch, Hq, 1, hd) =
+// P.V over the appended V cache, in the same launch (static scratch, as
+// launch_decode_step).
+template <typename T>
+void launch_decode_step_attention(const Tensor<unsigned int> &q_lens, Tensor<unsigned int> &kv_lens,
+                                  Tensor<unsigned int> &max_lens, const Tensor<unsigned int> &input_ids,
+                                  const Tensor<T> &embed_table, const Tensor<T> &norm_weight, Tensor<T> &x,
+                                  Tensor<T> &normed, const Tensor<T> &qkv, const Tensor<unsigned char> &is_done,
+                                  Tensor<T> &q, Tensor<T> &k_cache, Tensor<T> &v_cache, Tensor<T> &qk,
+                                  const Tensor<T> &gate_up, Tensor<T> &ffn_out, Tensor<T> &attn_out,
+                                  bool llama2_pairs);

@@ -365,13 +365,15 @@ void launch_prefill_attention_scores(const Tensor<T> &q, const Tensor<T> &k, con
           "launch_prefill_attention_scores");
 }
 
+// The arguments of one fused decode step, read from the tensors as the
+// separate launch_* functions read theirs.
 template <typename T>
-void launch_decode_step(const Tensor<unsigned int> &q_lens, Tensor<unsigned int> &kv_lens,
-                        Tensor<unsigned int> &max_lens, const Tensor<unsigned int> &input_ids,
-                        const Tensor<T> &embed_table, const Tensor<T> &norm_weight, Tensor<T> &x, Tensor<T> &normed,
-                        const Tensor<T> &qkv, const Tensor<unsigned char> &is_done, Tensor<T> &q, Tensor<T> &k_cache,
-                        Tensor<T> &v_cache, Tensor<T> &qk, const Tensor<T> &gate_up, Tensor<T> &ffn_out,
-                        bool llama2_pairs)
+l2k_decode_step_args step_args(const Tensor<unsigned int> &q_lens, Tensor<unsigned int> &kv_lens,
+                               Tensor<unsigned int> &max_lens, const Tensor<unsigned int> &input_ids,
+                               const Tensor<T> &embed_table, const Tensor<T> &norm_weight, Tensor<T> &x,
+                               Tensor<T> &normed, const Tensor<T> &qkv, const Tensor<unsigned char> &is_done,
+                               Tensor<T> &q, Tensor<T> &k_cache, Tensor<T> &v_cache, Tensor<T> &qk,
+                               const Tensor<T> &gate_up, Tensor<T> &ffn_out, bool llama2_pairs)
 {
     const unsigned int b = input_ids.shape()[0];
     const unsigned int hq = q.shape()[1], hd = q.shape()[3], hkv = k_cache.shape()[1], s = k_cache.shape()[2];
@@ -407,7 +409,37 @@ void launch_decode_step(const Tensor<unsigned int> &q_lens, Tensor<unsigned int>
     a.hidden = ffn_out.shape()[1];
     a.pairing = llama2_pairs ? L2K_ROPE_HALF : L2K_ROPE_INTERLEAVED;
     a.dtype = dtype_of<T>();
+    return a;
+}
+
+template <typename T>
+void launch_decode_step(const Tensor<unsigned int> &q_lens, Tensor<unsigned int> &kv_lens,
+                        Tensor<unsigned int> &max_lens, const Tensor<unsigned int> &input_ids,
+                        const Tensor<T> &embed_table, const Tensor<T> &norm_weight, Tensor<T> &x, Tensor<T> &normed,
+                        const Tensor<T> &qkv, const Tensor<unsigned char> &is_done, Tensor<T> &q, Tensor<T> &k_cache,
+                        Tensor<T> &v_cache, Tensor<T> &qk, const Tensor<T> &gate_up, Tensor<T> &ffn_out,
+                        bool llama2_pairs)
+{
+    const l2k_decode_step_args a = step_args<T>(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x,
+                                                normed, qkv, is_done, q, k_cache, v_cache, qk, gate_up, ffn_out,
+                                                llama2_pairs);
     check(l2k_decode_step_no_alloc(&a, nullptr), "launch_decode_step");
+}
+
+template <typename T>
+void launch_decode_step_attention(const Tensor<unsigned int> &q_lens, Tensor<unsigned int> &kv_lens,
+                                  Tensor<unsigned int> &max_lens, const Tensor<unsigned int> &input_ids,
+                                  const Tensor<T> &embed_table, const Tensor<T> &norm_weight, Tensor<T> &x,
+                                  Tensor<T> &normed, const Tensor<T> &qkv, const Tensor<unsigned char> &is_done,
+                                  Tensor<T> &q, Tensor<T> &k_cache, Tensor<T> &v_cache, Tensor<T> &qk,
+                                  const Tensor<T> &gate_up, Tensor<T> &ffn_out, Tensor<T> &attn_out,
+                                  bool llama2_pairs)
+{
+    require(attn_out.numel() == q.numel(), "Incorrect attn_out size");
+    const l2k_decode_step_args a = step_args<T>(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x,
+                                                normed, qkv, is_done, q, k_cache, v_cache, qk, gate_up, ffn_out,
+                                                llama2_pairs);
+    check(l2k_decode_step_attention_no_alloc(&a, attn_out.data(), nullptr), "launch_decode_step_attention");
 }
 
 // Explicit instantiations: float, half and bfloat16, as the reference
@@ -452,6 +484,11 @@ void launch_decode_step(const Tensor<unsigned int> &q_lens, Tensor<unsigned int>
     template void launch_prefill_attention_scores<T>(const Tensor<T> &, const Tensor<T> &,                          \
                                                      const Tensor<unsigned int> &, const Tensor<unsigned int> &,    \
                                                      const unsigned int, const unsigned int, Tensor<T> &);          \
+    template void launch_decode_step_attention<T>(                                                                  \
+        const Tensor<unsigned int> &, Tensor<unsigned int> &, Tensor<unsigned int> &, const Tensor<unsigned int> &, \
+        const Tensor<T> &, const Tensor<T> &, Tensor<T> &, Tensor<T> &, const Tensor<T> &,                          \
+        const Tensor<unsigned char> &, Tensor<T> &, Tensor<T> &, Tensor<T> &, Tensor<T> &, const Tensor<T> &,       \
+        Tensor<T> &, Tensor<T> &, bool);                                                                            \
     template void launch_decode_step<T>(const Tensor<unsigned int> &, Tensor<unsigned int> &,                       \
                                         Tensor<unsigned int> &, const Tensor<unsigned int> &, const Tensor<T> &,    \
                                         const Tensor<T> &, Tensor<T> &, Tensor<T> &, const Tensor<T> &,             \

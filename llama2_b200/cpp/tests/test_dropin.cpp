@@ -560,6 +560,30 @@ TEST(DecodeStepTest, WholeChainOneLaunch)
     EXPECT_TRUE(download(v_d) == v_e);
     EXPECT_TRUE(max_rel(download(qk_d), qk_e) <= 1e-5f);
     EXPECT_TRUE(max_rel(download(ffn_d), ffn_e) <= 1e-5f);
+    // The same step with the attention output: a second run on fresh lengths
+    // and caches, whose P.V is checked against the oracle's P.V of the
+    // probabilities above over the appended V cache.
+    upload(kv_d, kv);
+    upload(k_d, kc);
+    upload(v_d, vc);
+    Tensor<float> o_d({b, h, 1, hd}, GPU);
+    launch_decode_step_attention(ql_d, kv_d, ml_d, ids_d, table_d, w_d, x_d, n_d, qkv_d, done_d, q_d, k_d, v_d, qk_d,
+                                 gu_d, ffn_d, o_d, true);
+    EXPECT_TRUE(download(v_d) == v_e);
+    EXPECT_TRUE(max_rel(download(qk_d), qk_e) <= 1e-5f);
+    std::vector<float> o_e((size_t)b * h * hd, 0.f);
+    orc_attention_qkv(qk_e.data(), v_e.data(), b, h, h, 1, s, hd, 1, mkv[0], o_e.data());
+    const std::vector<float> o = download(o_d);
+    for (unsigned int r = 0; r < b * h; ++r)
+    {
+        float mx = 0.f, err = 0.f;
+        for (unsigned int e = 0; e < hd; ++e)
+        {
+            mx = std::fmax(mx, std::fabs(o_e[r * hd + e]));
+            err = std::fmax(err, std::fabs(o[r * hd + e] - o_e[r * hd + e]));
+        }
+        EXPECT_TRUE(err <= 1e-5f * mx);
+    }
 }
 
 int main()

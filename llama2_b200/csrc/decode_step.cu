@@ -387,9 +387,13 @@ uint32_t *g_scratch_ptr[kMaxScratchDevices] = {};
 } // namespace
 } // namespace l2k
 
-extern "C" int l2k_decode_step_no_alloc(const l2k_decode_step_args *args, l2k_stream_t stream)
+namespace l2k
 {
-    using namespace l2k;
+namespace
+{
+// The static scratch of the current device (looked up on its first use).
+int static_scratch(uint32_t **out)
+{
     if (l2k_decode_step_workspace_bytes() > kStepScratchBytes)
         return set_error(L2K_ERR_UNSUPPORTED_SHAPE,
                          "l2k_decode_step_no_alloc: the step needs %lld bytes of scratch, the static scratch holds %d",
@@ -401,19 +405,36 @@ extern "C" int l2k_decode_step_no_alloc(const l2k_decode_step_args *args, l2k_st
     if (dev < 0 || dev >= kMaxScratchDevices)
         return set_error(L2K_ERR_UNSUPPORTED_SHAPE, "l2k_decode_step_no_alloc: device %d >= %d", dev,
                          kMaxScratchDevices);
-    uint32_t *scratch = nullptr;
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_ptr[dev])
     {
-        std::lock_guard<std::mutex> lock(g_scratch_mutex);
-        if (!g_scratch_ptr[dev])
-        {
-            void *p = nullptr;
-            e = cudaGetSymbolAddress(&p, g_step_scratch);
-            if (e != cudaSuccess)
-                return set_error(L2K_ERR_CUDA, "l2k_decode_step_no_alloc: cudaGetSymbolAddress: %s",
-                                 cudaGetErrorString(e));
-            g_scratch_ptr[dev] = static_cast<uint32_t *>(p);
-        }
-        scratch = g_scratch_ptr[dev];
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_step_scratch);
+        if (e != cudaSuccess)
+            return set_error(L2K_ERR_CUDA, "l2k_decode_step_no_alloc: cudaGetSymbolAddress: %s",
+                             cudaGetErrorString(e));
+        g_scratch_ptr[dev] = static_cast<uint32_t *>(p);
     }
-    return step_entry(args, nullptr, scratch, stream, true);
+    *out = g_scratch_ptr[dev];
+    return L2K_OK;
+}
+} // namespace
+} // namespace l2k
+
+extern "C" int l2k_decode_step_no_alloc(const l2k_decode_step_args *args, l2k_stream_t stream)
+{
+    uint32_t *scratch = nullptr;
+    if (int st = l2k::static_scratch(&scratch))
+        return st;
+    return l2k::step_entry(args, nullptr, scratch, stream, true);
+}
+
+extern "C" int l2k_decode_step_attention_no_alloc(const l2k_decode_step_args *args, void *attn_out,
+                                                  l2k_stream_t stream)
+{
+    L2K_REQUIRE(attn_out != nullptr, "l2k_decode_step_attention_no_alloc: null attn_out");
+    uint32_t *scratch = nullptr;
+    if (int st = l2k::static_scratch(&scratch))
+        return st;
+    return l2k::step_entry(args, attn_out, scratch, stream, true);
 }
