@@ -194,8 +194,10 @@ int l2k_build_q_k_v_qk_qkv_array(void *const bases[8], const int64_t slice_elems
  * entry of the device pointer arrays a_array, b_array, c_array (a, b, c
  * ignored). lda/ldb/ldc are the row strides of the stored matrices.
  * Replaces launch_linear (include/kernel/linear.h:9-24,
- * src/kernel/linear.cu:42-155), which calls cuBLAS; here it is a CUDA
- * kernel of this library. (The reference accumulates fp16 in fp16.)
+ * src/kernel/linear.cu:42-155), which calls cuBLAS; here it is a kernel of
+ * this library: plain 16-bit GEMMs with trans_a = 0 (16-byte aligned bases
+ * and row strides) run on the tcgen05 tensor cores, everything else on the
+ * CUDA cores. (The reference accumulates fp16 in fp16.)
  * ------------------------------------------------------------------------ */
 int l2k_linear(int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda,
                const void *b, int64_t ldb, void *c, int64_t ldc, int64_t batch_count, const void *const *a_array,

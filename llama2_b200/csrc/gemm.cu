@@ -1,6 +1,7 @@
 // Row-major GEMM on the CUDA cores with fp32 accumulation: the drop-in for
 // the reference's launch_linear (src/kernel/linear.cu:42-155, a cuBLAS call)
-// and the fp32 QK^T path. 64x64 output tile per CTA, 16-deep K slices staged
+// wherever the tensor-core kernel (gemm_tc.cu: plain 16-bit GEMMs with A
+// not transposed) does not take it, and the fp32 QK^T path. 64x64 output tile per CTA, 16-deep K slices staged
 // in shared memory, 4x4 outputs per thread. Three batch addressings:
 // plain (one GEMM), pointer arrays (the reference's batched form), and the
 // attention call sites computed from (seq, head) with grouped KV heads:
@@ -200,6 +201,10 @@ int attention_qkv_cuda_cores(const void *qk, const void *v, void *qkv, int64_t b
     return L2K_OK;
 }
 
+bool gemm_tc_supported(int dtype, int trans_a, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda,
+                       const void *b, int64_t ldb, const void *c); // gemm_tc.cu
+int gemm_tc(int trans_b, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda, const void *b, int64_t ldb,
+            void *c, int64_t ldc, int dtype, cudaStream_t stream);
 bool attention_qkv_tc_supported(int dtype, int64_t head_dim, int64_t S, int64_t n, const void *qk, const void *v,
                                 const void *qkv, int64_t grid); // attention_qkv_tc.cu
 int attention_qkv_tc(const void *qk, const void *v, void *qkv, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc,
@@ -237,6 +242,9 @@ extern "C" int l2k_linear(int trans_a, int trans_b, int64_t m, int64_t n, int64_
     if (batch_count == 0)
     {
         L2K_REQUIRE(a && b && c, "l2k_linear: null pointer");
+        // 16-bit with A not transposed: tcgen05 (A and B tiles by TMA, fp32 accumulator in tensor memory)
+        if (gemm_tc_supported(dtype, trans_a, m, n, k, a, lda, b, ldb, c))
+            return gemm_tc(trans_b, m, n, k, a, lda, b, ldb, c, ldc, dtype, stream);
         g.batch = 1;
         L2K_DISPATCH(dtype, { return launch_gemm<T, PLAIN>(g, stream); });
     }

@@ -489,6 +489,7 @@ int prefill_scores_tc(const void *q, const void *k, const uint32_t *q_lens, cons
 int read_scores_error(bool clear); // decode_scores.cu
 int read_step_error(bool clear);   // decode_step.cu
 int read_pv_error(bool clear);     // attention_qkv_tc.cu
+int read_gemm_error(bool clear);   // gemm_tc.cu
 
 } // namespace l2k
 
@@ -507,7 +508,8 @@ extern "C" int l2k_device_error(int clear)
     const int v2 = l2k::read_scores_error(clear != 0);
     const int v3 = l2k::read_step_error(clear != 0);
     const int v4 = l2k::read_pv_error(clear != 0);
-    if (v2 < 0 || v3 < 0 || v4 < 0)
+    const int v5 = l2k::read_gemm_error(clear != 0);
+    if (v2 < 0 || v3 < 0 || v4 < 0 || v5 < 0)
         return -1;
-    return v ? v : (v2 ? v2 : (v3 ? v3 : v4));
+    return v ? v : (v2 ? v2 : (v3 ? v3 : (v4 ? v4 : v5)));
 }
