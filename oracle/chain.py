@@ -113,3 +113,50 @@ def score_row(q_row, k_rows, keep_upto, head_dim):
     mask[0, 0, :keep_upto + 1] = 1
     port.masked_attention_score(qk, mask, np.ones(1, np.uint32), n, head_dim)
     return qk.reshape(-1)
+
+
+def decode_layer(wts: dict, x, pending, kv_lens, max_kv, is_done, k, v, pairing: int, dtype: str) -> dict:
+    """One decoder-layer decode step (llama2_b200.layer.DecoderLayer.decode)
+    composed from the restated helpers: add-residual RMSNorm
+    (test_fused_add_residual_rmsnorm.cu:21-52), compute_expected_linear
+    (test_linear.cu:78-108) for the projections, the decode RoPE + append,
+    QK^T + the intended mask + softmax, P.V of the fp32 probabilities, SwiGLU.
+    Every tensor the device stores in 16 bits is rounded there. k, v are
+    updated in place (float32). kv_lens are the updated lengths."""
+    r = rounder(dtype)
+    w = {n: r(np.asarray(a, np.float32)) for n, a in wts.items()}
+    x = r(x)
+    b, d = x.shape
+    h_n = k.shape[1]
+    hd = k.shape[3]
+    hq = d // hd
+    s = k.shape[2]
+    f = w["w_down"].shape[0]
+    if pending is None:
+        x1, h = port.fused_add_residual_rmsnorm(x, np.zeros_like(x), w["w_attn_norm"], False)
+    else:
+        x1, h = port.fused_add_residual_rmsnorm(x, r(pending), w["w_attn_norm"], True)
+    x1, h = r(x1), r(h)
+    n_qkv = w["w_qkv"].shape[1]
+    qkv = r(port.linear(h, w["w_qkv"], False, False, b, n_qkv, d))
+    q = np.zeros((b, hq, 1, hd), np.float32)
+    port.rope_kvcache_decode(pairing, qkv, is_done, kv_lens, q, k, v)
+    q = r(q)
+    k[...] = r(k)
+    v[...] = r(v)
+    qk = np.zeros((b, hq, 1, s), np.float32)
+    port.qk_scores(q, k, 1, max_kv, qk)
+    ones = np.ones(b, np.uint32)
+    mask = intended_mask(ones, kv_lens, 1, max_kv, 1, s)
+    port.masked_attention_score(qk, mask, ones, max_kv, hd)
+    attn = np.zeros((b, hq, 1, hd), np.float32)
+    port.attention_qkv(qk, v, 1, max_kv, attn)
+    attn = r(attn.reshape(b, d))
+    o = r(port.linear(attn, w["w_o"], False, False, b, d, d))
+    x2, h2 = port.fused_add_residual_rmsnorm(x1, o, w["w_ffn_norm"], True)
+    x2, h2 = r(x2), r(h2)
+    gu = r(port.linear(h2, w["w_gate_up"], False, False, b, 2 * f, d))
+    act = r(port.swiglu(gu))
+    down = r(port.linear(act, w["w_down"], False, False, b, d, f))
+    del h_n
+    return {"x": x2, "down": down, "qk": r(qk), "attn": attn, "h": h, "qkv": qkv}
