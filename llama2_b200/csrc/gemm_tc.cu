@@ -17,7 +17,10 @@
 // MMAs that read it complete; another issues four 128 x BN x 16 MMAs per
 // block. The tensor maps bound rows at M, columns at N and k at K, so partial
 // tiles read zeros. The four warps then read their 32 TMEM lanes (rows) and
-// store the rows' BN columns.
+// store the rows' BN columns. Products of one row tile (M <= 128: decode
+// batches, bound by reading B) split K over a thread-block cluster of up to
+// 8 CTAs that reduce their fp32 rows into rank 0 over distributed shared
+// memory.
 // Every mbarrier wait is bounded; on expiry the kernel records an error code
 // (l2k_device_error) and leaves after its copies and MMAs have drained.
 //
@@ -71,7 +74,21 @@ struct GemmTcArgs
     int n_kb;   // k blocks
     int n_nt;   // column tiles
     int wide;   // C rows are 16-byte aligned: 16-byte stores
+    int split;  // SPLIT: CTAs per cluster sharing one C tile, each a K range
 };
+
+// Pushes 4 floats into cluster rank 0's copy of *local_slot (16-byte
+// aligned) and signals 16 bytes on rank 0's copy of *local_bar.
+__device__ __forceinline__ void push_rank0(const float4 *local_slot, uint32_t local_bar, float4 v)
+{
+    uint32_t slot, bar;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(slot) : "r"(smem_u32(local_slot)));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(bar) : "r"(local_bar));
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     slot),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(bar)
+                 : "memory");
+}
 
 // MN-major operand, 128-byte swizzle: LBO = 8 KB between the two 64-column
 // halves, SBO = 1024 bytes between 8-row k groups.
@@ -94,7 +111,11 @@ __device__ __forceinline__ void gemm_fail(int code, volatile int *abort_flag)
     *abort_flag = 1;
 }
 
-template <typename T, bool B_MN, int BN, int STAGES>
+// SPLIT: a cluster of a.split CTAs shares one C tile, each CTA summing a
+// contiguous range of the k blocks; once every rank's MMAs are done (cluster
+// barrier) ranks 1.. push their fp32 rows into rank 0's idle ring with
+// st.async, and rank 0 adds them to its own in rank order and stores.
+template <typename T, bool B_MN, int BN, int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const GemmTcArgs a)
@@ -118,9 +139,15 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kOffMisc + 8);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int mt = (int)(blockIdx.x / a.n_nt), nt = (int)(blockIdx.x % a.n_nt);
+    const int split = SPLIT ? a.split : 1;
+    const int rank = SPLIT ? (int)(blockIdx.x % split) : 0;
+    const int tile = (int)(blockIdx.x / split);
+    const int mt = tile / a.n_nt, nt = tile % a.n_nt;
     const int row0 = mt * BM, col0 = nt * BN;
-    const int n_kb = a.n_kb;
+    // this CTA's k blocks: [kb0, kb0 + n_kb)
+    const int kb0 = (int)((int64_t)rank * a.n_kb / split);
+    const int n_kb = (int)((int64_t)(rank + 1) * a.n_kb / split) - kb0;
+    const uint32_t bar_red = bar_done + 8; // SPLIT, rank 0: the peers' rows have landed
 
     if (tid == 0)
     {
@@ -130,6 +157,8 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
             mbar_init(bar_freed + 8 * i, 1);
         }
         mbar_init(bar_done, 1);
+        if (SPLIT)
+            mbar_init(bar_red, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -159,15 +188,16 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
             const uint32_t dst = sbase + st * kStageBytes;
             const uint32_t bar = bar_full + 8 * st;
             mbar_expect_tx(bar, kStageBytes);
-            tma_load_3d(dst, &tm_a, kb * BK, row0, 0, bar);
+            const int kx = (kb0 + kb) * BK;
+            tma_load_3d(dst, &tm_a, kx, row0, 0, bar);
             if constexpr (B_MN)
             {
 #pragma unroll
                 for (int h = 0; h < BN / 64; ++h)
-                    tma_load_3d(dst + kABox + h * BK * 128, &tm_b, col0 + 64 * h, kb * BK, 0, bar);
+                    tma_load_3d(dst + kABox + h * BK * 128, &tm_b, col0 + 64 * h, kx, 0, bar);
             }
             else
-                tma_load_3d(dst + kABox, &tm_b, kb * BK, col0, 0, bar);
+                tma_load_3d(dst + kABox, &tm_b, kx, col0, 0, bar);
             issued = kb + 1;
         }
     }
@@ -204,13 +234,50 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
     T *out = static_cast<T *>(a.c) + row * a.ldc;
     const bool store = row < a.m;
     const bool wide = a.wide != 0;
+    const int lrow = 32 * warp + lane;          // row within the tile
+    float *red = reinterpret_cast<float *>(smem); // SPLIT, rank 0: [split - 1][m][BN] peer rows (in the idle ring)
+    const int m_tile = (int)min((int64_t)BM, a.m - row0);
     if (n_kb > 0)
     {
         if (!mbar_wait(bar_done, 0, abort_flag))
             gemm_fail(ERR_GEMM_WAIT_DONE, abort_flag);
         tc_fence_after();
         __syncwarp();
-        if (!*abort_flag)
+        if constexpr (SPLIT)
+        {
+            // every rank's MMAs are done: rank 0's ring may take the peers' rows
+            asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+            asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+            if (rank == 0 && tid == 0)
+                mbar_expect_tx(bar_red, (uint32_t)((split - 1) * m_tile * BN * (int)sizeof(float)));
+            if (rank != 0)
+            {
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32)
+                {
+                    uint32_t r[32];
+                    tmem_ld32_async(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, r);
+                    tmem_wait_ld();
+                    if (lrow < m_tile && !*abort_flag)
+                    {
+                        const float4 *dst =
+                            reinterpret_cast<const float4 *>(red + ((int64_t)(rank - 1) * m_tile + lrow) * BN + c0);
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            push_rank0(dst + v, bar_red,
+                                       make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                                   __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3])));
+                    }
+                }
+            }
+            else
+            {
+                // (also after a failure: the peers' rows land before this CTA leaves)
+                if (!mbar_wait(bar_red, 0, abort_flag))
+                    gemm_fail(ERR_GEMM_WAIT_DONE, abort_flag);
+            }
+        }
+        if (!*abort_flag && (!SPLIT || rank == 0))
         {
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32)
@@ -220,6 +287,16 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
                 tmem_wait_ld();
                 if (!store)
                     continue;
+                if constexpr (SPLIT)
+                {
+                    for (int p = 1; p < split; ++p)
+                    {
+                        const float *src = red + ((int64_t)(p - 1) * m_tile + lrow) * BN + c0;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            r[j] = __float_as_uint(__uint_as_float(r[j]) + src[j]);
+                    }
+                }
 #pragma unroll
                 for (int v = 0; v < 4; ++v)
                 {
@@ -270,9 +347,9 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
     }
 }
 
-template <typename T, bool B_MN, int BN, int STAGES>
+template <typename T, bool B_MN, int BN, int STAGES, bool SPLIT = false>
 int launch_gemm_tc(const void *A, int64_t lda, const void *B, int64_t ldb, void *C, int64_t ldc, int64_t m,
-                   int64_t n, int64_t k, cudaStream_t stream)
+                   int64_t n, int64_t k, cudaStream_t stream, int split = 1)
 {
     constexpr uint32_t kSmemBytes = Cfg<BN, STAGES>::kSmemBytes;
     const CUtensorMapDataType dt =
@@ -288,16 +365,35 @@ int launch_gemm_tc(const void *A, int64_t lda, const void *B, int64_t ldb, void 
     if (!ok)
         return set_error(L2K_ERR_CUDA, "l2k_linear: tensor map encoding failed");
     GemmTcArgs a{C, ldc, m, n, (int)ceil_div(k, BK), (int)ceil_div(n, BN),
-                 (ldc * 2) % 16 == 0 && is_aligned(C, 16) ? 1 : 0};
-    auto kernel = gemm_tc_kernel<T, B_MN, BN, STAGES>;
+                 (ldc * 2) % 16 == 0 && is_aligned(C, 16) ? 1 : 0, split};
+    auto kernel = gemm_tc_kernel<T, B_MN, BN, STAGES, SPLIT>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e == cudaSuccess) // two CTAs per SM need the whole shared-memory carveout
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess)
         return set_error(L2K_ERR_CUDA, "l2k_linear: %s", cudaGetErrorString(e));
-    const int64_t grid = ceil_div(m, BM) * a.n_nt;
-    kernel<<<(unsigned)grid, kThreads, kSmemBytes, stream>>>(ma, mb, a);
-    return check_launch("l2k_linear (tcgen05)");
+    const int64_t grid = ceil_div(m, BM) * a.n_nt * split;
+    if (!SPLIT)
+    {
+        kernel<<<(unsigned)grid, kThreads, kSmemBytes, stream>>>(ma, mb, a);
+        return check_launch("l2k_linear (tcgen05)");
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)split;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, a);
+    if (e != cudaSuccess)
+        return set_error(L2K_ERR_CUDA, "l2k_linear (split k): %s", cudaGetErrorString(e));
+    return check_launch("l2k_linear (tcgen05, split k)");
 }
 
 } // namespace
@@ -323,6 +419,17 @@ int launch_tiles(const void *a, int64_t lda, const void *b, int64_t ldb, void *c
 {
     if (m > BM)
         return launch_gemm_tc<T, B_MN, 256, 2>(a, lda, b, ldb, c, ldc, m, n, k, stream);
+    // One row tile: too few CTAs to stream B at full bandwidth unless K is
+    // split across a cluster (the peers' fp32 rows must fit rank 0's ring).
+    constexpr int kSplitStages = 3;
+    const int64_t tiles = ceil_div(n, 128), n_kb = ceil_div(k, BK);
+    const int64_t ring = (int64_t)kSplitStages * Cfg<128, kSplitStages>::kStageBytes;
+    int split = 1;
+    while (split < 8 && tiles * split * 2 <= 2LL * num_sms() && split * 2 <= n_kb &&
+           (int64_t)(split * 2 - 1) * m * 128 * 4 <= ring)
+        split *= 2;
+    if (split > 1)
+        return launch_gemm_tc<T, B_MN, 128, kSplitStages, true>(a, lda, b, ldb, c, ldc, m, n, k, stream, split);
     return launch_gemm_tc<T, B_MN, 128, 4>(a, lda, b, ldb, c, ldc, m, n, k, stream);
 }
 

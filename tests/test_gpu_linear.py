@@ -52,8 +52,10 @@ def _call(a, b, c, trans_b, m, n, k):
 @pytest.mark.parametrize("m,n,k,pad", [
     (128, 128, 64, 0),     # one tile, one k block
     (300, 200, 136, 8),    # partial tiles in every dimension, padded row strides
-    (1, 512, 4096, 0),     # a decode-shaped product (one row)
+    (1, 512, 4096, 0),     # a decode-shaped product (one row): k split over a cluster of 8
     (257, 384, 320, 16),
+    (64, 1024, 2048, 0),   # a batch-64 decode product: k split over a cluster of 2
+    (16, 384, 1000, 8),    # a ragged last k block with the split
 ])
 def test_linear_tensor_cores_against_oracle(dt, trans_b, m, n, k, pad):
     a, b = _operands(dt, m, n, k, trans_b, seed=m + n + k + trans_b, pad=pad)
