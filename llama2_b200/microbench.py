@@ -1,0 +1,165 @@
+"""Timings of single operators and of the decoder layer on one GPU.
+
+    python -m llama2_b200.microbench {gemm,attention,pv,unpad,rope,layer} [--iters N]
+
+Each prints one line per shape. Kernels are timed with CUDA events on the
+current stream; ``gemm`` times back-to-back launches (compute-bound, L2
+irrelevant) next to ``torch.matmul`` on the same operands (cuBLAS, for
+reference); the others flush L2 before every timed launch (write a 512 MB
+buffer, then read another, outside the timed window). Inputs are seeded
+random tensors of the 7B shapes.
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import capi, ops
+
+_FLUSH = {}
+
+
+def _flush():
+    if "w" not in _FLUSH:
+        _FLUSH["w"] = torch.empty(512 << 20 >> 2, device="cuda")
+        _FLUSH["r"] = torch.ones(512 << 20 >> 2, device="cuda")
+    _FLUSH["w"].zero_()
+    _FLUSH["r"].sum()
+
+
+def time_ms(fn, iters: int, flush: bool = True) -> float:
+    """Mean milliseconds of fn() over iters launches (after 3 untimed ones)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    if not flush:
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            fn()
+        z.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(z) / iters
+    total = 0.0
+    for _ in range(iters):
+        _flush()
+        a, z = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        z.record()
+        torch.cuda.synchronize()
+        total += a.elapsed_time(z)
+    return total / iters
+
+
+def bench_gemm(iters):
+    for (m, n, k) in [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 12288, 4096), (16384, 4096, 4096),
+                      (64, 12288, 4096), (1, 12288, 4096)]:
+        for trans_b in (0, 1):
+            a = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+            b = (torch.randn(n, k, device="cuda", dtype=torch.bfloat16) if trans_b
+                 else torch.randn(k, n, device="cuda", dtype=torch.bfloat16))
+            c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+            ours = lambda: capi.call("l2k_linear", 0, trans_b, m, n, k, a.data_ptr(), k, b.data_ptr(), b.stride(0),
+                                     c.data_ptr(), n, 0, None, None, None, capi.L2K_BF16,
+                                     torch.cuda.current_stream().cuda_stream)
+            ref = lambda: torch.matmul(a, b.t() if trans_b else b, out=c)
+            t1, t2 = time_ms(ours, iters, flush=False), time_ms(ref, iters, flush=False)
+            fl = 2.0 * m * n * k
+            print(f"gemm bf16 m={m} n={n} k={k} trans_b={trans_b}: {t1 * 1e3:.1f} us {fl / t1 / 1e9:.1f} TF/s | "
+                  f"torch.matmul {t2 * 1e3:.1f} us {fl / t2 / 1e9:.1f} TF/s")
+
+
+def bench_attention(iters):
+    h, s, hd = 32, 4096, 128
+    for dt in (torch.float32, torch.bfloat16):
+        for b in (1, 16, 64):
+            q = torch.randn(b, h, 1, hd, device="cuda").to(dt)
+            k = torch.randn(b, h, s, hd, device="cuda").to(dt)
+            v = torch.randn(b, h, s, hd, device="cuda").to(dt)
+            lens = torch.randint(1, s, (b,), generator=torch.Generator().manual_seed(1))
+            kv = lens.to(torch.uint32).cuda()
+            mx = torch.tensor([int(lens.max())], dtype=torch.uint32, device="cuda")
+            qk = torch.empty(b, h, 1, s, device="cuda", dtype=dt)
+            out = torch.empty(b, h, 1, hd, device="cuda", dtype=dt)
+            es = q.element_size()
+            keys = int(lens.sum())
+            for name, fn, nbytes in (
+                    ("scores", lambda: ops.decode_attention_scores(q, k, kv, mx, qk),
+                     keys * h * hd * es + b * h * int(mx) * es),
+                    ("scores+P.V", lambda: ops.decode_attention(q, k, v, kv, mx, qk, out),
+                     2 * keys * h * hd * es + b * h * int(mx) * es)):
+                ms = time_ms(fn, iters)
+                print(f"decode {name} {dt} b={b}: {ms * 1e3:.1f} us {nbytes / ms / 1e6:.1f} GB/s")
+
+
+def bench_pv(iters):
+    b, h, qc, s, hd = 8, 32, 2048, 2048, 128
+    qk = torch.rand(b, h, qc, s, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(b, h, s, hd, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(b, h, qc, hd, device="cuda", dtype=torch.bfloat16)
+    ms = time_ms(lambda: ops.launch_attention_qkv(qk, v, out, qc, s), iters)
+    nbytes = (qk.numel() + v.numel() + out.numel()) * 2
+    print(f"P.V bf16 {b}x{h}x{qc}x{s}: {ms * 1e3:.1f} us {nbytes / ms / 1e6:.1f} GB/s "
+          f"{2 * b * h * qc * s * hd / ms / 1e9:.1f} TF/s")
+
+
+def bench_unpad(iters):
+    b, h, qc, hd = 8, 32, 2048, 128
+    qkv = torch.randn(b, h, qc, hd, device="cuda", dtype=torch.bfloat16)
+    idx = torch.arange(b * qc, dtype=torch.int32, device="cuda")
+    out = torch.empty(b * qc, h * hd, device="cuda", dtype=torch.bfloat16)
+    ms = time_ms(lambda: ops.launch_fused_transpose_unpad(b * qc, qkv, idx, out), iters)
+    print(f"transpose+unpad bf16 {b * qc} tokens: {ms * 1e3:.1f} us {2 * qkv.numel() * 2 / ms / 1e6:.1f} GB/s")
+
+
+def bench_rope(iters):
+    b, qc, h, hd = 8, 2048, 32, 128
+    d, t = h * hd, b * qc
+    for dt in (torch.bfloat16, torch.float32):
+        inp = torch.randn(t, 3 * d, device="cuda").to(dt)
+        lens = torch.full((b,), qc, dtype=torch.int32, device="cuda")
+        idx = torch.arange(t, dtype=torch.int32, device="cuda")
+        q = torch.empty(b, h, qc, hd, device="cuda", dtype=dt)
+        k = torch.empty(b, h, qc, hd, device="cuda", dtype=dt)
+        v = torch.empty(b, h, qc, hd, device="cuda", dtype=dt)
+        ms = time_ms(lambda: ops.launch_fused_pad_reshape_transpose_rope_kvcache_llama2(inp, lens, lens, idx, q, k, v),
+                     iters)
+        print(f"prefill RoPE + KV append {dt} {t} tokens: {ms * 1e3:.1f} us "
+              f"{2 * inp.numel() * inp.element_size() / ms / 1e6:.1f} GB/s")
+
+
+def bench_layer(iters):
+    from .layer import DecoderLayer
+    for (b, dt) in ((64, torch.bfloat16), (1, torch.bfloat16), (64, torch.float32)):
+        layer = DecoderLayer(4096, 32, 32, 11008, 4096, b, dtype=dt, seed=0)
+        x = torch.randn(b, 4096, device="cuda").to(dt)
+        q_lens = torch.ones(b, dtype=torch.uint32, device="cuda")
+        lens = torch.randint(1, 4095, (b,), generator=torch.Generator().manual_seed(0))
+        kv = lens.to(torch.uint32).cuda()
+        max_lens = torch.zeros(2, dtype=torch.uint32, device="cuda")
+        ops.launch_update_q_kv_lens(q_lens, kv, max_lens[0:1], max_lens[1:2])
+        is_done = torch.zeros(b, dtype=torch.uint8, device="cuda")
+        pending = torch.randn(b, 4096, device="cuda").to(dt)
+        graph = layer.capture_decode(x, pending, kv, max_lens[1:2], is_done)
+        ms = time_ms(graph.replay, iters)
+        es = 2 if dt != torch.float32 else 4
+        wbytes = sum(t.numel() for t in layer.weights().values()) * es
+        kvb = 2 * int((lens + 1).sum()) * 4096 * es
+        print(f"7B decoder layer decode step {dt} b={b}: {ms * 1e3:.1f} us; weights {wbytes / 1e6:.0f} MB + "
+              f"K/V {kvb / 1e6:.0f} MB -> {(wbytes + kvb) / ms / 1e6:.0f} GB/s")
+        del layer, graph
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["gemm", "attention", "pv", "unpad", "rope", "layer"])
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args()
+    torch.manual_seed(0)
+    globals()["bench_" + args.what](args.iters)
+
+
+if __name__ == "__main__":
+    main()
