@@ -201,6 +201,10 @@ int attention_qkv_cuda_cores(const void *qk, const void *v, void *qkv, int64_t b
     return L2K_OK;
 }
 
+bool gemv_supported(int dtype, int trans_a, int trans_b, int64_t m, int64_t n, int64_t k, const void *b,
+                    int64_t ldb); // gemv.cu
+int gemv(int trans_b, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda, const void *b, int64_t ldb,
+         void *c, int64_t ldc, int dtype, cudaStream_t stream);
 bool gemm_tc_supported(int dtype, int trans_a, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda,
                        const void *b, int64_t ldb, const void *c); // gemm_tc.cu
 int gemm_tc(int trans_b, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda, const void *b, int64_t ldb,
@@ -242,7 +246,10 @@ extern "C" int l2k_linear(int trans_a, int trans_b, int64_t m, int64_t n, int64_
     if (batch_count == 0)
     {
         L2K_REQUIRE(a && b && c, "l2k_linear: null pointer");
-        // 16-bit with A not transposed: tcgen05 (A and B tiles by TMA, fp32 accumulator in tensor memory)
+        // 16-bit with A not transposed: up to 8 rows stream B on the CUDA cores,
+        // more on tcgen05 (A and B tiles by TMA, fp32 accumulator in tensor memory)
+        if (gemv_supported(dtype, trans_a, trans_b, m, n, k, b, ldb))
+            return gemv(trans_b, m, n, k, a, lda, b, ldb, c, ldc, dtype, stream);
         if (gemm_tc_supported(dtype, trans_a, m, n, k, a, lda, b, ldb, c))
             return gemm_tc(trans_b, m, n, k, a, lda, b, ldb, c, ldc, dtype, stream);
         g.batch = 1;

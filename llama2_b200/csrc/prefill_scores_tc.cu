@@ -490,6 +490,7 @@ int read_scores_error(bool clear); // decode_scores.cu
 int read_step_error(bool clear);   // decode_step.cu
 int read_pv_error(bool clear);     // attention_qkv_tc.cu
 int read_gemm_error(bool clear);   // gemm_tc.cu
+int read_gemv_error(bool clear);   // gemv.cu
 
 } // namespace l2k
 
@@ -509,7 +510,12 @@ extern "C" int l2k_device_error(int clear)
     const int v3 = l2k::read_step_error(clear != 0);
     const int v4 = l2k::read_pv_error(clear != 0);
     const int v5 = l2k::read_gemm_error(clear != 0);
-    if (v2 < 0 || v3 < 0 || v4 < 0 || v5 < 0)
+    const int v6 = l2k::read_gemv_error(clear != 0);
+    if (v2 < 0 || v3 < 0 || v4 < 0 || v5 < 0 || v6 < 0)
         return -1;
-    return v ? v : (v2 ? v2 : (v3 ? v3 : (v4 ? v4 : v5)));
+    const int others[] = {v2, v3, v4, v5, v6};
+    for (int o : others)
+        if (!v && o)
+            v = o;
+    return v;
 }

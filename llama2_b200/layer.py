@@ -20,7 +20,9 @@ The lengths are updated once per model step (launch_update_q_kv_lens) before
 the first layer; each layer reads the updated kv_lens and the device max.
 Weights are [in, out] row-major (the MN-major B operand of the tensor-core
 GEMM). Nine launches per layer; ``capture_decode`` records a layer step as a
-CUDA graph.
+CUDA graph. ``prefill`` runs the same layer over the new tokens of a batch of
+prompts (eleven launches: the scores, P.V and the unpad replace the fused
+decode attention).
 """
 from __future__ import annotations
 
@@ -109,6 +111,59 @@ class DecoderLayer:
             self.decode(x, pending, kv_lens, max_kv_len, is_done)
         return graph
 
+    def prefill(self, x: torch.Tensor, pending, q_lens: torch.Tensor, kv_lens: torch.Tensor, max_q: int,
+                max_kv: int, unpad_to_pad: torch.Tensor) -> torch.Tensor:
+        """One prefill pass of this layer over T new tokens (sequence-major,
+        unpadded). x: the residual stream [T, D], updated in place; pending:
+        the previous layer's addend [T, D] or None; kv_lens: the updated
+        lengths; max_q / max_kv: their maxima (host ints, as the reference
+        passes them); unpad_to_pad: the token -> padded slot map
+        (launch_build_padding_index_maps). Returns this layer's addend [T, D].
+
+        qkv -> padded RoPE + append -> tcgen05 scores (QK^T, causal mask,
+        softmax) -> P.V at the launch_linear site -> transpose + unpad -> O,
+        then the feed-forward half as in decode()."""
+        t, d, f, hd = x.shape[0], self.dim, self.hidden, self.head_dim
+        qc = unpad_to_pad.numel() // self.batch
+        buf = self._prefill_buffers(t, qc)
+        if pending is None:
+            ops.launch_fused_add_residual_rmsnorm(self.w_attn_norm, x, buf["h"], False)
+            h = buf["h"]
+        else:
+            ops.launch_fused_add_residual_rmsnorm(self.w_attn_norm, x, pending, True)
+            h = pending
+        ops.launch_linear(False, False, t, buf["qkv"].shape[1], d, h, self.w_qkv, buf["qkv"])
+        rope = (ops.launch_fused_pad_reshape_transpose_rope_kvcache_llama2 if self.pairing
+                else ops.launch_fused_pad_reshape_transpose_rope_kvcache)
+        rope(buf["qkv"], q_lens, kv_lens, unpad_to_pad.view(-1), buf["q"], self.k_cache, self.v_cache)
+        ops.prefill_attention_scores(buf["q"], self.k_cache, q_lens, kv_lens, max_q, max_kv, buf["qk"])
+        ops.launch_attention_qkv(buf["qk"], self.v_cache, buf["pv"], max_q, max_kv)
+        ops.launch_fused_transpose_unpad(t, buf["pv"], unpad_to_pad.view(-1), buf["attn"])
+        ops.launch_linear(False, False, t, d, d, buf["attn"], self.w_o, buf["o"])
+        ops.launch_fused_add_residual_rmsnorm(self.w_ffn_norm, x, buf["o"], True)
+        ops.launch_linear(False, False, t, 2 * f, d, buf["o"], self.w_gate_up, buf["gate_up"])
+        ops.launch_swiglu(buf["gate_up"], buf["act"])
+        ops.launch_linear(False, False, t, d, f, buf["act"], self.w_down, buf["down"])
+        del hd
+        return buf["down"]
+
+    def _prefill_buffers(self, t: int, qc: int) -> dict:
+        key = (t, qc)
+        if getattr(self, "_pf_key", None) != key:
+            b, h, kvh, hd, d, f = self.batch, self.heads, self.kv_heads, self.head_dim, self.dim, self.hidden
+            e = dict(dtype=self.dtype, device=self.device)
+            self._pf = {"h": torch.empty(t, d, **e), "qkv": torch.empty(t, (h + 2 * kvh) * hd, **e),
+                        "q": torch.zeros(b, h, qc, hd, **e), "qk": torch.zeros(b, h, qc, self.kv_cache_len, **e),
+                        "pv": torch.zeros(b, h, qc, hd, **e), "attn": torch.empty(t, d, **e),
+                        "o": torch.empty(t, d, **e), "gate_up": torch.empty(t, 2 * f, **e),
+                        "act": torch.empty(t, f, **e), "down": torch.empty(t, d, **e)}
+            self._pf_key = key
+        return self._pf
+
     @staticmethod
     def launches_per_step() -> int:
         return 9
+
+    @staticmethod
+    def launches_per_prefill() -> int:
+        return 11

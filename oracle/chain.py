@@ -160,3 +160,49 @@ def decode_layer(wts: dict, x, pending, kv_lens, max_kv, is_done, k, v, pairing:
     down = r(port.linear(act, w["w_down"], False, False, b, d, f))
     del h_n
     return {"x": x2, "down": down, "qk": r(qk), "attn": attn, "h": h, "qkv": qkv}
+
+
+def prefill_layer(wts: dict, x, pending, q_lens, kv_lens, max_q, max_kv, unpad, k, v, q_cache_len: int,
+                  pairing: int, dtype: str) -> dict:
+    """One decoder-layer prefill pass (llama2_b200.layer.DecoderLayer.prefill)
+    composed from the restated helpers: add-residual RMSNorm, the QKV
+    projection, the padded RoPE + append, QK^T + the intended causal mask +
+    softmax, P.V of the stored (rounded) probabilities over keys < max_kv for
+    rows < max_q (the launch_linear call site), transpose + unpad, the O
+    projection, the second norm, gate/up, SwiGLU, down. k, v are updated in
+    place (float32); kv_lens are the updated lengths."""
+    r = rounder(dtype)
+    w = {n: r(np.asarray(a, np.float32)) for n, a in wts.items()}
+    x = r(x)
+    t, d = x.shape
+    b = len(q_lens)
+    hd = k.shape[3]
+    hq = d // hd
+    s = k.shape[2]
+    f = w["w_down"].shape[0]
+    if pending is None:
+        x1, h = port.fused_add_residual_rmsnorm(x, np.zeros_like(x), w["w_attn_norm"], False)
+    else:
+        x1, h = port.fused_add_residual_rmsnorm(x, r(pending), w["w_attn_norm"], True)
+    x1, h = r(x1), r(h)
+    qkv = r(port.linear(h, w["w_qkv"], False, False, t, w["w_qkv"].shape[1], d))
+    q = np.zeros((b, hq, q_cache_len, hd), np.float32)
+    port.rope_kvcache_prefill(pairing, qkv, q_lens, kv_lens, unpad, q, k, v)
+    q = r(q)
+    k[...] = r(k)
+    v[...] = r(v)
+    qk = np.zeros((b, hq, q_cache_len, s), np.float32)
+    port.qk_scores(q, k, max_q, max_kv, qk)
+    mask = intended_mask(q_lens, kv_lens, max_q, max_kv, q_cache_len, s)
+    port.masked_attention_score(qk, mask, q_lens, max_kv, hd)
+    qk = r(qk)
+    pv = np.zeros((b, hq, q_cache_len, hd), np.float32)
+    port.attention_qkv(qk, v, max_q, max_kv, pv)
+    attn = port.transpose_unpad(r(pv), unpad, t)
+    o = r(port.linear(attn, w["w_o"], False, False, t, d, d))
+    x2, h2 = port.fused_add_residual_rmsnorm(x1, o, w["w_ffn_norm"], True)
+    x2, h2 = r(x2), r(h2)
+    gu = r(port.linear(h2, w["w_gate_up"], False, False, t, 2 * f, d))
+    act = r(port.swiglu(gu))
+    down = r(port.linear(act, w["w_down"], False, False, t, d, f))
+    return {"x": x2, "down": down, "qk": qk, "attn": attn}

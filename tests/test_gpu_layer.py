@@ -81,3 +81,47 @@ def test_two_decode_layers_against_oracle(dtype, tol, graph):
         xr, pend = ref["x"], ref["down"]
     assert _row_rel_err(host(x), xr) <= tol
     assert _row_rel_err(host(pending), pend) <= tol
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-2)])
+def test_two_prefill_layers_against_oracle(dtype, tol):
+    """Two layers over a batch of two prompts (64 and 40 new tokens after
+    0 and 10 cached ones), ragged, causal, against the oracle composition."""
+    b, d, heads, kvh, f, s, qc = 2, 256, 2, 2, 512, 128, 64
+    dev = torch.device("cuda")
+    layers = [DecoderLayer(d, heads, kvh, f, s, b, dtype=dtype, seed=20 + i) for i in range(2)]
+    q_lens_h = np.array([64, 40], np.uint32)
+    kv0_h = np.array([0, 10], np.uint32)
+    t = int(q_lens_h.sum())
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    x = torch.randn(t, d, generator=g, device=dev).to(dtype)
+    q_lens = torch.from_numpy(q_lens_h).cuda()
+    kv_lens = torch.from_numpy(kv0_h).cuda()
+    max_lens = torch.zeros(2, dtype=torch.uint32, device=dev)
+    unpad = torch.zeros(b, qc, dtype=torch.uint32, device=dev)
+    offsets = torch.zeros(b, dtype=torch.uint32, device=dev)
+    ops.launch_update_q_kv_lens(q_lens, kv_lens, max_lens[0:1], max_lens[1:2])
+    ops.launch_build_padding_index_maps(t, q_lens, unpad, offsets)
+    torch.cuda.synchronize()
+    kv_h = host(kv_lens).astype(np.uint32)
+    max_q, max_kv = int(host(max_lens)[0]), int(host(max_lens)[1])
+    unpad_h = host(unpad).reshape(-1)[:t].astype(np.uint32)
+    x0 = host(x)
+    caches = [(host(L.k_cache).copy(), host(L.v_cache).copy()) for L in layers]
+    wts = [{n: host(w) for n, w in L.weights().items()} for L in layers]
+
+    pending = None
+    for L in layers:
+        pending = L.prefill(x, pending, q_lens, kv_lens, max_q, max_kv, unpad)
+    torch.cuda.synchronize()
+
+    dt = "f32" if dtype == torch.float32 else "bf16"
+    xr, pend = x0, None
+    for i, L in enumerate(layers):
+        k, v = caches[i]
+        ref = ochain.prefill_layer(wts[i], xr, pend, q_lens_h, kv_h, max_q, max_kv, unpad_h, k, v, qc, 1, dt)
+        assert _row_rel_err(host(L.k_cache).reshape(-1, 128), k.reshape(-1, 128)) <= tol, f"layer {i} K"
+        xr, pend = ref["x"], ref["down"]
+    assert _row_rel_err(host(x), xr) <= tol
+    assert _row_rel_err(host(pending), pend) <= tol

@@ -1,4 +1,5 @@
-"""launch_linear on the tensor cores (plain 16-bit GEMMs, A not transposed)
+"""launch_linear's own kernels for plain 16-bit GEMMs with A not transposed
+(tcgen05 tensor cores; the CUDA-core B stream for at most 8 rows)
 against the oracle's restatement of the reference helper
 (compute_expected_linear, test/kernel/test_linear.cu:78-108) and, at sizes
 the CPU oracle cannot finish in seconds, against a torch fp32 product of the
@@ -56,6 +57,10 @@ def _call(a, b, c, trans_b, m, n, k):
     (257, 384, 320, 16),
     (64, 1024, 2048, 0),   # a batch-64 decode product: k split over a cluster of 2
     (16, 384, 1000, 8),    # a ragged last k block with the split
+    (3, 300, 1000, 4),     # few rows: the CUDA-core B stream (K x N layout; N x K falls back: unaligned rows)
+    (8, 996, 2048, 4),     # few rows, a ragged last column vector
+    (5, 4096, 11008, 0),   # few rows, the down projection's k split over a cluster of 8
+    (1, 12288, 4096, 0),   # one row, the QKV projection
 ])
 def test_linear_tensor_cores_against_oracle(dt, trans_b, m, n, k, pad):
     a, b = _operands(dt, m, n, k, trans_b, seed=m + n + k + trans_b, pad=pad)
