@@ -123,7 +123,7 @@ class DecoderLayer:
         qkv -> padded RoPE + append -> tcgen05 scores (QK^T, causal mask,
         softmax) -> P.V at the launch_linear site -> transpose + unpad -> O,
         then the feed-forward half as in decode()."""
-        t, d, f, hd = x.shape[0], self.dim, self.hidden, self.head_dim
+        t, d, f = x.shape[0], self.dim, self.hidden
         qc = unpad_to_pad.numel() // self.batch
         buf = self._prefill_buffers(t, qc)
         if pending is None:
@@ -144,7 +144,6 @@ class DecoderLayer:
         ops.launch_linear(False, False, t, 2 * f, d, buf["o"], self.w_gate_up, buf["gate_up"])
         ops.launch_swiglu(buf["gate_up"], buf["act"])
         ops.launch_linear(False, False, t, d, f, buf["act"], self.w_down, buf["down"])
-        del hd
         return buf["down"]
 
     def _prefill_buffers(self, t: int, qc: int) -> dict:

@@ -127,7 +127,6 @@ def decode_layer(wts: dict, x, pending, kv_lens, max_kv, is_done, k, v, pairing:
     w = {n: r(np.asarray(a, np.float32)) for n, a in wts.items()}
     x = r(x)
     b, d = x.shape
-    h_n = k.shape[1]
     hd = k.shape[3]
     hq = d // hd
     s = k.shape[2]
@@ -158,7 +157,6 @@ def decode_layer(wts: dict, x, pending, kv_lens, max_kv, is_done, k, v, pairing:
     gu = r(port.linear(h2, w["w_gate_up"], False, False, b, 2 * f, d))
     act = r(port.swiglu(gu))
     down = r(port.linear(act, w["w_down"], False, False, b, d, f))
-    del h_n
     return {"x": x2, "down": down, "qk": r(qk), "attn": attn, "h": h, "qkv": qkv}
 
 

@@ -14,7 +14,6 @@ from __future__ import annotations
 
 import concurrent.futures as cf
 import ctypes
-import os
 
 import numpy as np
 

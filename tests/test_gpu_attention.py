@@ -19,9 +19,6 @@ from tests.gpu_util import TORCH, dev, host, max_rel_err
 
 pytestmark = pytest.mark.gpu
 
-F32 = np.float32
-
-
 @pytest.fixture(autouse=True)
 def _lib(cuda_lib):
     yield
