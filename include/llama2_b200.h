@@ -388,6 +388,37 @@ int l2k_decode_step_supported(const l2k_decode_step_args *args);
 int l2k_decode_step(const l2k_decode_step_args *args, uint32_t *workspace, l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Paged K/V caches (decode). A paged cache is a pool of pages
+ * (num_pages, Hkv, page_rows, head_dim); sequence b's cache positions
+ * [j * page_rows, (j + 1) * page_rows) live in page block_table[b * max_pages
+ * + j] (u32, device). page_rows is l2k_paged_block_rows(head_dim, dtype)
+ * (16 KB of rows per page and kv head: one streamed block of the score
+ * kernels); 0 when the head size is not one the streaming kernels take.
+ * Page ids past the pool are not dereferenced (rows for them are not
+ * written; the attention reads page 0 and records l2k_device_error).
+ * No counterpart in the reference, whose caches are (batch, kv_head,
+ * kv_cache_len, head_dim) (include/kernel/fused_reshape_rope_kvcache_decode.h:11-12).
+ *
+ * l2k_fused_reshape_rope_kvcache_paged_decode: the decode RoPE + append
+ *   of l2k_fused_reshape_rope_kvcache[_llama2]_decode (pairing selects which)
+ *   with K/V row pos = kv_lens[b] - 1 written to its page.
+ * l2k_decode_attention_paged: l2k_decode_attention over the paged caches;
+ *   qk is (B, Hq, 1, max_pages * page_rows), qkv (B, Hq, 1, hd).
+ * ------------------------------------------------------------------------ */
+int64_t l2k_paged_block_rows(int64_t head_dim, int dtype);
+int l2k_fused_reshape_rope_kvcache_paged_decode(const void *input, const uint8_t *is_done, const uint32_t *kv_lens,
+                                                void *q, void *k_pages, void *v_pages, const uint32_t *block_table,
+                                                int64_t max_pages, int64_t num_pages, int64_t page_rows,
+                                                int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                                int64_t head_dim, const float *rope_table,
+                                                int64_t rope_table_positions, int pairing, int dtype,
+                                                l2k_stream_t stream);
+int l2k_decode_attention_paged(const void *q, const void *k_pages, const void *v_pages, const uint32_t *block_table,
+                               int64_t max_pages, int64_t num_pages, const uint32_t *kv_lens,
+                               const uint32_t *max_kv_len, void *qk, void *qkv, int64_t batch, int64_t q_head_num,
+                               int64_t kv_head_num, int64_t head_dim, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * The fused decode step with the attention output: everything
  * l2k_decode_step computes, and in the same launch
  *   attn_out[b, h, 0, :] = sum_{j <= pos} qk[b, h, 0, j] * v_cache[b, h / (Hq/Hkv), j, :]

@@ -65,6 +65,10 @@ SIGNATURES = {
     "l2k_fused_transpose_unpad": [i64, vp, vp, vp, i64, i64, i64, i64, cint, vp],
     "l2k_decode_attention_scores": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],
     "l2k_decode_attention": [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],
+    "l2k_paged_block_rows": ([i64, cint], i64),
+    "l2k_fused_reshape_rope_kvcache_paged_decode": [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64,
+                                                    vp, i64, cint, cint, vp],
+    "l2k_decode_attention_paged": [vp, vp, vp, vp, i64, i64, vp, vp, vp, vp, i64, i64, i64, i64, cint, vp],
     "l2k_prefill_attention_scores": [vp, vp, vp, vp, u32, u32, vp, i64, i64, i64, i64, i64, i64, cint, vp],
     "l2k_decode_step_workspace_bytes": ([], i64),
     "l2k_decode_step_supported": [ctypes.POINTER(DecodeStepArgs)],

@@ -318,6 +318,55 @@ extern "C" int l2k_decode_attention(const void *q, const void *k, const void *v,
                                     kv_cache_len, max_kv_len, dtype, stream);
 }
 
+extern "C" int64_t l2k_paged_block_rows(int64_t head_dim, int dtype)
+{
+    using namespace l2k;
+    if (!dtype_ok(dtype) || head_dim <= 0)
+        return 0;
+    const int64_t row_bytes = head_dim * (int64_t)dtype_size(dtype);
+    const int64_t lpr = row_bytes / 16;
+    if (row_bytes % 16 != 0 || !(lpr == 4 || lpr == 8 || lpr == 16 || lpr == 32))
+        return 0;
+    return kBlockBytes / row_bytes;
+}
+
+extern "C" int l2k_decode_attention_paged(const void *q, const void *k_pages, const void *v_pages,
+                                          const uint32_t *block_table, int64_t max_pages, int64_t num_pages,
+                                          const uint32_t *kv_lens, const uint32_t *max_kv_len, void *qk, void *qkv,
+                                          int64_t batch, int64_t q_head_num, int64_t kv_head_num, int64_t head_dim,
+                                          int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    L2K_REQUIRE(dtype_ok(dtype), "l2k_decode_attention_paged: unsupported dtype %d", dtype);
+    L2K_REQUIRE(batch >= 0 && q_head_num >= 0 && kv_head_num >= 0 && head_dim > 0 && max_pages >= 0 &&
+                    num_pages >= 0,
+                "l2k_decode_attention_paged: bad size");
+    if (batch == 0 || q_head_num == 0)
+        return L2K_OK;
+    L2K_REQUIRE(kv_head_num > 0 && q_head_num % kv_head_num == 0,
+                "l2k_decode_attention_paged: q_head_num must be a multiple of kv_head_num");
+    L2K_REQUIRE(max_pages > 0 && num_pages > 0, "l2k_decode_attention_paged: empty block table or page pool");
+    L2K_REQUIRE(q && k_pages && v_pages && block_table && kv_lens && max_kv_len && qk && qkv,
+                "l2k_decode_attention_paged: null pointer");
+    const int64_t page_rows = l2k_paged_block_rows(head_dim, dtype);
+    L2K_REQUIRE_SHAPE(page_rows > 0, "l2k_decode_attention_paged: head_dim * element size must be 64, 128, 256 or "
+                                     "512 bytes");
+    L2K_REQUIRE_SHAPE(batch * q_head_num * 16 < (int64_t(1) << 31), "l2k_decode_attention_paged: grid too large");
+    const int64_t S = max_pages * page_rows;
+    DecodeArgs a{q, k_pages, nullptr, kv_lens, max_kv_len, 0u, qk, q_head_num, q_head_num / kv_head_num,
+                 kv_head_num, 1, S, head_dim, 0, 1.f / sqrtf((float)head_dim)};
+    a.v = v_pages;
+    a.qkv = qkv;
+    a.block_table = block_table;
+    a.max_pages = max_pages;
+    a.num_pages = num_pages;
+    bool streamed = false;
+    L2K_DISPATCH(dtype, { streamed = stream_rows_ok<T>(a, true); });
+    L2K_REQUIRE_SHAPE(streamed, "l2k_decode_attention_paged: q, the pages, qkv must be 16-byte aligned");
+    L2K_DISPATCH(dtype, { return launch_attention_rows<T>(a, batch, stream); });
+    return L2K_OK;
+}
+
 extern "C" int l2k_decode_attention_scores(const void *q, const void *k, const uint32_t *kv_lens,
                                            const uint32_t *max_kv_len, void *qk, int64_t batch, int64_t q_head_num,
                                            int64_t kv_head_num, int64_t kv_cache_len, int64_t head_dim, int dtype,

@@ -59,7 +59,28 @@ struct RopeArgs
     int64_t S;
     const float2 *table;
     int64_t table_pos;
+    // Paged caches (decode only): k and v are (num_pages, Hkv, page_rows, hd);
+    // position pos of sequence b lives in page block_table[b][pos / page_rows].
+    const uint32_t *block_table;
+    int64_t max_pages;
+    int64_t num_pages;
+    int64_t page_rows;
 };
+
+// Start of cache row pos of (seq, kv head h): contiguous (B, Hkv, S, hd) or
+// paged; null when the page id is past the pool (nothing is written then).
+template <typename T>
+__device__ __forceinline__ T *cache_row(const RopeArgs &a, void *cache, int64_t seq, int64_t h, uint32_t pos)
+{
+    if (a.block_table)
+    {
+        const int64_t page = a.block_table[seq * a.max_pages + pos / a.page_rows];
+        if (page >= a.num_pages)
+            return nullptr;
+        return static_cast<T *>(cache) + ((page * a.hkv + h) * a.page_rows + pos % a.page_rows) * a.hd;
+    }
+    return static_cast<T *>(cache) + ((seq * a.hkv + h) * a.S + pos) * a.hd;
+}
 
 template <int BYTES>
 struct RawT;
@@ -177,7 +198,9 @@ __global__ void __launch_bounds__(256) rope_kvcache_kernel(const RopeArgs a)
         {
             // v: copy 2*VP elements into cache row pos.
             const int64_t h = head - a.hq - a.hkv;
-            T *dst = static_cast<T *>(a.v) + ((seq * a.hkv + h) * a.S + pos) * a.hd;
+            T *dst = cache_row<T>(a, a.v, seq, h, pos);
+            if (!dst)
+                continue;
             if constexpr (2 * VP * sizeof(T) == 32)
             {
                 const uint4 *s4 = reinterpret_cast<const uint4 *>(src + 2 * i0);
@@ -260,7 +283,9 @@ __global__ void __launch_bounds__(256) rope_kvcache_kernel(const RopeArgs a)
         if (head < a.hq)
             dst = static_cast<T *>(a.q) + ((seq * a.hq + head) * a.qc + t) * a.hd;
         else
-            dst = static_cast<T *>(a.k) + ((seq * a.hkv + (head - a.hq)) * a.S + pos) * a.hd;
+            dst = cache_row<T>(a, a.k, seq, head - a.hq, pos);
+        if (!dst)
+            continue;
         if constexpr (PAIRING == L2K_ROPE_INTERLEAVED)
         {
             float oo[2 * VP];
@@ -411,4 +436,29 @@ extern "C" int l2k_fused_pad_reshape_transpose_rope_kvcache_llama2(
                                    kv_head_num, head_dim, q_cache_len, kv_cache_len, rope_table,
                                    rope_table_positions),
                       L2K_ROPE_HALF, true, dtype, stream, "l2k_fused_pad_reshape_transpose_rope_kvcache_llama2");
+}
+
+extern "C" int l2k_fused_reshape_rope_kvcache_paged_decode(const void *input, const uint8_t *is_done,
+                                                           const uint32_t *kv_lens, void *q, void *k_pages,
+                                                           void *v_pages, const uint32_t *block_table,
+                                                           int64_t max_pages, int64_t num_pages, int64_t page_rows,
+                                                           int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                                           int64_t head_dim, const float *rope_table,
+                                                           int64_t rope_table_positions, int pairing, int dtype,
+                                                           l2k_stream_t stream)
+{
+    using namespace l2k;
+    L2K_REQUIRE(pairing == L2K_ROPE_INTERLEAVED || pairing == L2K_ROPE_HALF,
+                "l2k_fused_reshape_rope_kvcache_paged_decode: bad pairing %d", pairing);
+    L2K_REQUIRE(max_pages >= 0 && num_pages >= 0 && page_rows > 0,
+                "l2k_fused_reshape_rope_kvcache_paged_decode: bad page geometry");
+    L2K_REQUIRE(batch == 0 || (block_table && max_pages > 0 && num_pages > 0),
+                "l2k_fused_reshape_rope_kvcache_paged_decode: null or empty block table");
+    RopeArgs a = decode_args(input, is_done, kv_lens, q, k_pages, v_pages, batch, q_head_num, kv_head_num, head_dim,
+                             max_pages * page_rows, rope_table, rope_table_positions);
+    a.block_table = block_table;
+    a.max_pages = max_pages;
+    a.num_pages = num_pages;
+    a.page_rows = page_rows;
+    return rope_entry(a, pairing, false, dtype, stream, "l2k_fused_reshape_rope_kvcache_paged_decode");
 }

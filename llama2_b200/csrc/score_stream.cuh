@@ -71,6 +71,12 @@ struct DecodeArgs
     // PV rows only: the V cache and the attention output P.V
     const void *v;        // (B, Hkv, S, hd)
     void *qkv;            // (B, Hq, Qc, hd)
+    // Paged caches (decode only): k and v are (num_pages, Hkv, KB, hd), one
+    // key block per page; block g of sequence b is page block_table[b][g]
+    // (max_pages entries per sequence; S = max_pages * KB).
+    const uint32_t *block_table;
+    int64_t max_pages;
+    int64_t num_pages;
 };
 
 // Extra inputs of a score row inside the fused decode step. kv_lens and
@@ -358,21 +364,45 @@ __device__ __forceinline__ void step_ticket(const StepRowArgs &sa, int lane, boo
         step_update_lens(sa, lane, have, pq, pkv);
 }
 
+// Start of key block g of the (b, kv head) plane: in the contiguous cache
+// (B, Hkv, S, hd), or page block_table[b][g] of a paged one (a page id past
+// the pool is recorded as an error and read as page 0, so nothing outside
+// the pool is touched).
+template <int KB, int ROW_BYTES>
+__device__ __forceinline__ const char *block_ptr(const DecodeArgs &a, const void *cache, int64_t b, int64_t kvh,
+                                                 int64_t g, int *err)
+{
+    const char *base = static_cast<const char *>(cache);
+    if (a.block_table)
+    {
+        int64_t page = a.block_table[b * a.max_pages + g];
+        if (page >= a.num_pages)
+        {
+            atomicCAS(err, 0, 0x206);
+            page = 0;
+        }
+        return base + (page * a.Hkv + kvh) * (int64_t)KB * ROW_BYTES;
+    }
+    return base + ((b * a.Hkv + kvh) * a.S + g * KB) * (int64_t)ROW_BYTES;
+}
+
 // L2 prefetch of this rank's first two key blocks of the (b, kv head) plane,
 // issued before the lengths are known (they are needed to know how many
 // blocks there are): the blocks exist whatever the length, and the copies
 // that follow find them in L2 instead of waiting a DRAM round trip.
 template <int KB, int ROW_BYTES>
-__device__ __forceinline__ void prefetch_first_blocks(const DecodeArgs &a, int64_t b, int64_t kvh, int c, int C)
+__device__ __forceinline__ void prefetch_first_blocks(const DecodeArgs &a, int64_t b, int64_t kvh, int c, int C,
+                                                      int *err)
 {
-    const char *plane = static_cast<const char *>(a.k) + (b * a.Hkv + kvh) * a.S * (int64_t)ROW_BYTES;
     for (int i = 0; i < 2; ++i)
     {
         const int64_t g = c + (int64_t)C * i;
         if (g * KB >= a.S)
             break;
         const uint32_t bytes = (uint32_t)(min((int64_t)KB, a.S - g * KB) * ROW_BYTES);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(plane + g * KB * ROW_BYTES), "r"(bytes)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(block_ptr<KB, ROW_BYTES>(a, a.k, b, kvh, g,
+                                                                                                   err)),
+                     "r"(bytes)
                      : "memory");
     }
 }
@@ -646,7 +676,7 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                 pkv = sa.kv_lens[lane];
             }
             if (lane == 0)
-                prefetch_first_blocks<KB, ROW_BYTES>(a, ri.b, ri.h / a.group, c, C);
+                prefetch_first_blocks<KB, ROW_BYTES>(a, ri.b, ri.h / a.group, c, C, err);
         }
         kv_new = kvl + ql;
         pos = kv_new - 1u;
@@ -660,7 +690,7 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
         if (warp == kCW && lane == 0)
         {
             const int64_t bh = row / a.Qc, b = bh / a.Hq;
-            prefetch_first_blocks<KB, ROW_BYTES>(a, b, (bh - b * a.Hq) / a.group, c, C);
+            prefetch_first_blocks<KB, ROW_BYTES>(a, b, (bh - b * a.Hq) / a.group, c, C, err);
         }
         ri = row_info(a, row);
         if (!ri.active)
@@ -678,7 +708,6 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
     const int64_t n_keys = max((int64_t)0, ri.limit + 1);
     const int64_t n_blk = (n_keys + KB - 1) / KB; // blocks holding valid keys
     const int n_mine = n_blk > c ? (int)((n_blk - c + C - 1) / C) : 0;
-    const char *kbase = static_cast<const char *>(a.k) + (ri.b * a.Hkv + kvh) * a.S * (int64_t)ROW_BYTES;
 
     // Ring sequence number i: K block i for i < n_mine, V block i - n_mine
     // after (PV rows); sequence i lands in stage i % kNS.
@@ -690,14 +719,11 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
         const int64_t g = c + (int64_t)C * (is_v ? i - n_mine : i);
         const uint32_t bytes = (uint32_t)(min((int64_t)KB, a.S - g * KB) * ROW_BYTES);
         const uint32_t bar = smem_addr(&sh.full[st]);
-        const char *base = kbase;
-        if constexpr (PV)
-            if (is_v)
-                base = static_cast<const char *>(a.v) + (ri.b * a.Hkv + kvh) * a.S * (int64_t)ROW_BYTES;
+        const char *src = block_ptr<KB, ROW_BYTES>(a, is_v ? a.v : a.k, ri.b, kvh, g, err);
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                          smem_addr(smem + st * kBlockBytes)),
-                     "l"(base + g * KB * ROW_BYTES), "r"(bytes), "r"(bar)
+                     "l"(src), "r"(bytes), "r"(bar)
                      : "memory");
     };
     // Producer lane: issues sequences up to `end`, each after its stage's

@@ -346,6 +346,44 @@ def decode_attention(q, k, v, kv_lens, max_kv_len, qk, qkv):
               max_kv_len.data_ptr(), qk.data_ptr(), qkv.data_ptr(), b, hq, hkv, s, hd, _code(q), _stream())
 
 
+def paged_block_rows(head_dim: int, dtype: torch.dtype) -> int:
+    """Rows per page (and kv head) of the paged caches: one 16 KB streamed block."""
+    return int(capi.lib().l2k_paged_block_rows(head_dim, _DT[dtype]))
+
+
+def launch_rope_kvcache_paged_decode(input, is_done, kv_lens, q, k_pages, v_pages, block_table, *, pairing,
+                                     use_table=True):
+    """Decode RoPE + K/V append into paged caches k_pages / v_pages
+    (num_pages, Hkv, page_rows, hd); block_table (B, max_pages) u32."""
+    _dev(input, is_done, kv_lens, q, k_pages, v_pages, block_table)
+    _u32(block_table, "block_table")
+    b, hq, _, hd = q.shape
+    n_pages, hkv, page_rows, _ = k_pages.shape
+    _require(tuple(v_pages.shape) == tuple(k_pages.shape), "Incorrect v_pages size")
+    table = rope_table(hd, q.device) if use_table else None
+    capi.call("l2k_fused_reshape_rope_kvcache_paged_decode", input.data_ptr(), is_done.data_ptr(),
+              kv_lens.data_ptr(), q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(),
+              block_table.shape[1], n_pages, page_rows, b, hq, hkv, hd,
+              table.data_ptr() if table is not None else None, ROPE_TABLE_POSITIONS if table is not None else 0,
+              int(pairing), _code(q), _stream())
+
+
+def decode_attention_paged(q, k_pages, v_pages, block_table, kv_lens, max_kv_len, qk, qkv):
+    """decode_attention over paged caches (num_pages, Hkv, page_rows, hd)
+    with page_rows = paged_block_rows(hd, dtype); qk (B, Hq, 1, max_pages * page_rows)."""
+    _dev(q, k_pages, v_pages, block_table, kv_lens, max_kv_len, qk, qkv)
+    _u32(block_table, "block_table")
+    b, hq, _, hd = q.shape
+    n_pages, hkv, page_rows, _ = k_pages.shape
+    _require(page_rows == paged_block_rows(hd, q.dtype), "page_rows must be paged_block_rows(head_dim, dtype)")
+    max_pages = block_table.shape[1]
+    _require(tuple(qk.shape) == (b, hq, 1, max_pages * page_rows), "Incorrect qk size")
+    _require(tuple(qkv.shape) == (b, hq, 1, hd), "Incorrect qkv size")
+    capi.call("l2k_decode_attention_paged", q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
+              block_table.data_ptr(), max_pages, n_pages, kv_lens.data_ptr(), max_kv_len.data_ptr(), qk.data_ptr(),
+              qkv.data_ptr(), b, hq, hkv, hd, _code(q), _stream())
+
+
 def prefill_attention_scores(q, k, q_lens, kv_lens, max_q_len, max_kv_len, qk):
     """Fused QK^T + scale + causal mask + softmax for q_len query rows per sequence."""
     _dev(q, k, q_lens, kv_lens, qk)

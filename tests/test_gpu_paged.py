@@ -1,0 +1,113 @@
+"""Paged K/V caches (decode): the paged RoPE + append and the paged fused
+decode attention against the contiguous operators on the same data.
+
+A pool of pages (num_pages, Hkv, page_rows, hd) holds each sequence's cache
+in pages scattered by a shuffled block table; gathering the pages back into
+the (B, Hkv, S, hd) layout must give exactly the contiguous cache, and the
+attention over the pages exactly the contiguous attention's bits (the same
+blocks are streamed in the same order).
+"""
+import numpy as np
+import pytest
+import torch
+
+from llama2_b200 import capi, ops
+from tests.gpu_util import bits_equal, host
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _lib(cuda_lib):
+    yield
+
+
+def _paged_setup(dtype, b, hq, hkv, hd, max_pages, spare, seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    rows = ops.paged_block_rows(hd, dtype)
+    s = max_pages * rows
+    k = torch.randn(b, hkv, s, hd, generator=g, device="cuda").to(dtype)
+    v = torch.randn(b, hkv, s, hd, generator=g, device="cuda").to(dtype)
+    n_pages = b * max_pages + spare
+    perm = torch.randperm(n_pages, generator=torch.Generator().manual_seed(seed))[: b * max_pages]
+    table = perm.view(b, max_pages).to(torch.int32)
+    kp = torch.randn(n_pages, hkv, rows, hd, generator=g, device="cuda").to(dtype)
+    vp = torch.randn(n_pages, hkv, rows, hd, generator=g, device="cuda").to(dtype)
+    for bi in range(b):
+        for j in range(max_pages):
+            p = int(table[bi, j])
+            kp[p] = k[bi, :, j * rows:(j + 1) * rows]
+            vp[p] = v[bi, :, j * rows:(j + 1) * rows]
+    return k, v, kp, vp, table.cuda(), rows
+
+
+def _gather(pages, table, rows):
+    b, max_pages = table.shape
+    out = []
+    for bi in range(b):
+        out.append(torch.cat([pages[int(table[bi, j])] for j in range(max_pages)], dim=1))
+    return torch.stack(out)
+
+
+@pytest.mark.parametrize("dtype,pairing", [(torch.float32, 1), (torch.bfloat16, 1), (torch.bfloat16, 0)])
+def test_paged_rope_append_matches_contiguous(dtype, pairing):
+    b, hq, hkv, hd, max_pages = 3, 8, 2, 128, 6
+    k, v, kp, vp, table, rows = _paged_setup(dtype, b, hq, hkv, hd, max_pages, spare=5, seed=1)
+    s = max_pages * rows
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    qkv = torch.randn(b, (hq + 2 * hkv) * hd, generator=g, device="cuda").to(dtype)
+    kv_lens = torch.tensor([s, 1, rows + 5], dtype=torch.uint32, device="cuda")   # last row, first row, page 2
+    is_done = torch.tensor([0, 0, 0], dtype=torch.uint8, device="cuda")
+    q1 = torch.zeros(b, hq, 1, hd, dtype=dtype, device="cuda")
+    q2 = torch.zeros_like(q1)
+    rope = ops.launch_fused_reshape_rope_kvcache_llama2_decode if pairing else ops.launch_fused_reshape_rope_kvcache_decode
+    rope(qkv, is_done, kv_lens, q1, k, v)
+    ops.launch_rope_kvcache_paged_decode(qkv, is_done, kv_lens, q2, kp, vp, table, pairing=pairing)
+    torch.cuda.synchronize()
+    assert bits_equal(host(q1), host(q2))
+    assert bits_equal(host(_gather(kp, table, rows)), host(k))
+    assert bits_equal(host(_gather(vp, table, rows)), host(v))
+
+
+@pytest.mark.parametrize("dtype,b,hq,hkv,max_pages,kv", [
+    (torch.float32, 3, 4, 4, 40, [1280, 7, 640]),     # 32-row pages, a full cache, one partial page
+    (torch.bfloat16, 4, 8, 2, 64, [4096, 1, 2000, 64]),  # 64-row pages, GQA, 7B-length caches
+])
+def test_paged_attention_matches_contiguous(dtype, b, hq, hkv, max_pages, kv):
+    hd = 128
+    k, v, kp, vp, table, rows = _paged_setup(dtype, b, hq, hkv, hd, max_pages, spare=3, seed=7)
+    s = max_pages * rows
+    g = torch.Generator(device="cuda")
+    g.manual_seed(9)
+    q = torch.randn(b, hq, 1, hd, generator=g, device="cuda").to(dtype)
+    kv_lens = torch.tensor(kv, dtype=torch.uint32, device="cuda")
+    mx = torch.tensor([max(kv)], dtype=torch.uint32, device="cuda")
+    qk1 = torch.full((b, hq, 1, s), 7.0, dtype=dtype, device="cuda")
+    qk2 = torch.full_like(qk1, 7.0)
+    o1 = torch.empty(b, hq, 1, hd, dtype=dtype, device="cuda")
+    o2 = torch.empty_like(o1)
+    ops.decode_attention(q, k, v, kv_lens, mx, qk1, o1)
+    ops.decode_attention_paged(q, kp, vp, table, kv_lens, mx, qk2, o2)
+    torch.cuda.synchronize()
+    assert bits_equal(host(qk1), host(qk2))
+    assert bits_equal(host(o1), host(o2))
+
+
+def test_paged_attention_page_past_the_pool_is_an_error_not_a_read():
+    """A block-table entry past the pool reads page 0 and records an error
+    code (l2k_device_error), without touching memory outside the pool."""
+    dtype, b, hq, hkv, hd, max_pages = torch.float32, 2, 2, 2, 128, 4
+    k, v, kp, vp, table, rows = _paged_setup(dtype, b, hq, hkv, hd, max_pages, spare=0, seed=2)
+    capi.lib().l2k_device_error(1)
+    table[1, 1] = 1 << 20  # used by sequence 1 (kv_len covers page 1)
+    q = torch.randn(b, hq, 1, hd, device="cuda")
+    kv_lens = torch.tensor([rows, 2 * rows], dtype=torch.uint32, device="cuda")
+    mx = torch.tensor([2 * rows], dtype=torch.uint32, device="cuda")
+    qk = torch.zeros(b, hq, 1, max_pages * rows, device="cuda")
+    o = torch.empty(b, hq, 1, hd, device="cuda")
+    ops.decode_attention_paged(q, kp, vp, table, kv_lens, mx, qk, o)
+    torch.cuda.synchronize()
+    assert capi.lib().l2k_device_error(1) == 0x206
+    assert np.isfinite(host(qk)).all() and np.isfinite(host(o)).all()
