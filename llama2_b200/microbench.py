@@ -1,6 +1,6 @@
 """Timings of single operators and of the decoder layer on one GPU.
 
-    python -m llama2_b200.microbench {gemm,attention,pv,unpad,rope,layer} [--iters N]
+    python -m llama2_b200.microbench {gemm,attention,paged,pv,unpad,rope,layer} [--iters N]
 
 Each prints one line per shape. Kernels are timed with CUDA events on the
 current stream; ``gemm`` times back-to-back launches (compute-bound, L2
@@ -94,6 +94,37 @@ def bench_attention(iters):
                 print(f"decode {name} {dt} b={b}: {ms * 1e3:.1f} us {nbytes / ms / 1e6:.1f} GB/s")
 
 
+def bench_paged(iters):
+    """Fused decode attention over a paged pool (shuffled block table) next
+    to the same attention over the contiguous cache."""
+    h, s, hd = 32, 4096, 128
+    for dt in (torch.float32, torch.bfloat16):
+        rows = ops.paged_block_rows(hd, dt)
+        max_pages = s // rows
+        for b in (1, 64):
+            q = torch.randn(b, h, 1, hd, device="cuda").to(dt)
+            k = torch.randn(b, h, s, hd, device="cuda").to(dt)
+            v = torch.randn(b, h, s, hd, device="cuda").to(dt)
+            perm = torch.randperm(b * max_pages, generator=torch.Generator().manual_seed(2))
+            table = perm.view(b, max_pages).to(torch.int32).cuda()
+            kp = torch.empty(b * max_pages, h, rows, hd, device="cuda", dtype=dt)
+            vp = torch.empty_like(kp)
+            kp[perm] = k.view(b, h, max_pages, rows, hd).transpose(1, 2).reshape(b * max_pages, h, rows, hd)
+            vp[perm] = v.view(b, h, max_pages, rows, hd).transpose(1, 2).reshape(b * max_pages, h, rows, hd)
+            lens = torch.randint(1, s, (b,), generator=torch.Generator().manual_seed(1))
+            kv = lens.to(torch.uint32).cuda()
+            mx = torch.tensor([int(lens.max())], dtype=torch.uint32, device="cuda")
+            qk = torch.empty(b, h, 1, s, device="cuda", dtype=dt)
+            out = torch.empty(b, h, 1, hd, device="cuda", dtype=dt)
+            es = q.element_size()
+            nbytes = 2 * int(lens.sum()) * h * hd * es + b * h * int(mx) * es
+            t1 = time_ms(lambda: ops.decode_attention(q, k, v, kv, mx, qk, out), iters)
+            t2 = time_ms(lambda: ops.decode_attention_paged(q, kp, vp, table, kv, mx, qk, out), iters)
+            print(f"decode attention {dt} b={b}: contiguous {t1 * 1e3:.1f} us {nbytes / t1 / 1e6:.1f} GB/s | "
+                  f"paged ({rows}-row pages) {t2 * 1e3:.1f} us {nbytes / t2 / 1e6:.1f} GB/s")
+            del k, v, kp, vp
+
+
 def bench_pv(iters):
     b, h, qc, s, hd = 8, 32, 2048, 2048, 128
     qk = torch.rand(b, h, qc, s, device="cuda", dtype=torch.bfloat16)
@@ -154,7 +185,7 @@ def bench_layer(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "pv", "unpad", "rope", "layer"])
+    ap.add_argument("what", choices=["gemm", "attention", "paged", "pv", "unpad", "rope", "layer"])
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
     torch.manual_seed(0)
