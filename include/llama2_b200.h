@@ -251,6 +251,45 @@ int l2k_swiglu(const void *input, void *output, int64_t num_tokens, int64_t inte
                l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Projection GEMMs with the following operator in their epilogue (tcgen05,
+ * 16-bit, trans_A = false; B row-major K x N, or N x K with trans_b). The
+ * product is never stored: results are bit-identical to l2k_linear into a
+ * [m, n] buffer followed by the separate operator on that buffer (when
+ * l2k_linear takes its tensor-core path, i.e. m > 8). Shapes these kernels
+ * do not take return L2K_ERR_UNSUPPORTED_SHAPE, f32 returns
+ * L2K_ERR_UNSUPPORTED_DTYPE: run the two operators instead.
+ *
+ * l2k_linear_swiglu: out[t, i] = silu(P[t, i]) * P[t, inter + i],
+ *   P = A op(B) with op(B) k x 2 inter (gate columns, then up columns):
+ *   launch_linear (src/kernel/linear.cu:42-155) then launch_swiglu
+ *   (src/kernel/swiglu.cu:55-72). inter % 8 == 0.
+ * l2k_linear_rope_kvcache_decode: P = A op(B), A = the batch's normed rows
+ *   [batch, dim], op(B) dim x (Hq + 2 Hkv) hd; then the decode RoPE + K/V
+ *   append of l2k_fused_reshape_rope_kvcache[_llama2]_decode on P (pairing
+ *   selects which; src/kernel/fused_reshape_rope_kvcache_decode.cu:11-84,
+ *   ..._llama2_decode.cu:11-74). head_dim 64 or 128; q, k, v and the table
+ *   16-byte aligned.
+ * l2k_linear_pad_rope_kvcache_prefill: the same for num_tokens unpadded
+ *   token rows, then l2k_fused_pad_reshape_transpose_rope_kvcache[_llama2]
+ *   (src/kernel/fused_pad_reshape_transpose_rope_kvcache.cu:11-83,
+ *   ..._llama2.cu:11-75).
+ * ------------------------------------------------------------------------ */
+int l2k_linear_swiglu(int trans_b, int64_t m, int64_t inter, int64_t k, const void *a, int64_t lda, const void *b,
+                      int64_t ldb, void *out, int64_t ldo, int dtype, l2k_stream_t stream);
+int l2k_linear_rope_kvcache_decode(int trans_b, const void *a, int64_t lda, const void *b, int64_t ldb, int64_t dim,
+                                   const uint8_t *is_done, const uint32_t *kv_lens, void *q, void *k, void *v,
+                                   int64_t batch, int64_t q_head_num, int64_t kv_head_num, int64_t head_dim,
+                                   int64_t kv_cache_len, const float *rope_table, int64_t rope_table_positions,
+                                   int pairing, int dtype, l2k_stream_t stream);
+int l2k_linear_pad_rope_kvcache_prefill(int trans_b, const void *a, int64_t lda, const void *b, int64_t ldb,
+                                        int64_t dim, const uint32_t *q_lens, const uint32_t *kv_lens,
+                                        const uint32_t *unpad_to_pad_idx, void *q, void *k, void *v,
+                                        int64_t num_tokens, int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                        int64_t head_dim, int64_t q_cache_len, int64_t kv_cache_len,
+                                        const float *rope_table, int64_t rope_table_positions, int pairing,
+                                        int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Transpose + unpad of the attention output (a byte-exact copy):
  *   unpad_qkv[t, h * hd + d] = qkv[b, h, i, d]
  * for t < num_input_tokens, with b * q_cache_len + i = unpad_to_pad_idx[t].

@@ -62,6 +62,11 @@ SIGNATURES = {
     "l2k_attention_qkv": [vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, i64, cint, vp],
     "l2k_compute_masked_attention_score": [i64, u32, u32, vp, vp, vp, i64, i64, i64, i64, cint, vp],
     "l2k_swiglu": [vp, vp, i64, i64, cint, vp],
+    "l2k_linear_swiglu": [cint, i64, i64, i64, vp, i64, vp, i64, vp, i64, cint, vp],
+    "l2k_linear_rope_kvcache_decode": [cint, vp, i64, vp, i64, i64, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64,
+                                       vp, i64, cint, cint, vp],
+    "l2k_linear_pad_rope_kvcache_prefill": [cint, vp, i64, vp, i64, i64, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64,
+                                            i64, i64, i64, vp, i64, cint, cint, vp],
     "l2k_fused_transpose_unpad": [i64, vp, vp, vp, i64, i64, i64, i64, cint, vp],
     "l2k_decode_attention_scores": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],
     "l2k_decode_attention": [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],

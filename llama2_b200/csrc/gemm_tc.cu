@@ -24,10 +24,28 @@
 // Every mbarrier wait is bounded; on expiry the kernel records an error code
 // (l2k_device_error) and leaves after its copies and MMAs have drained.
 //
+// Two epilogues replace the store with the operator that follows the
+// product in a Llama-2 layer, so the product never goes to HBM:
+//   * SwiGLU (gate/up projection): a tile takes BN/2 gate columns and the
+//     BN/2 up columns F apart (two B loads per k block) and stores
+//     silu(g) * u for its BN/2 output columns;
+//   * RoPE + K/V append (QKV projection): a tile covers whole heads of a
+//     token row; q and k heads are rotated at the token's position (decode:
+//     kv_len - 1; prefill: kv_len - q_len + slot through the unpad -> pad
+//     map) and written to the q buffer and the K cache row, v heads to the V
+//     cache row.
+// Both round the fp32 accumulator to the 16-bit type first (where the
+// separate launches read the stored product), then evaluate the separate
+// operator's arithmetic, so results are those of launch_linear followed by
+// launch_swiglu / the fused RoPE operator for the same tile configuration.
+//
 // Reference: src/kernel/linear.cu:42-155 (cublasGemmEx with op_A/op_B from
 // trans_B/trans_A on the swapped operands; 16-bit data accumulates in 16
-// bits there).
+// bits there); the epilogues follow src/kernel/swiglu.cu:10-72 and
+// src/kernel/fused_reshape_rope_kvcache[_llama2]_decode.cu,
+// src/kernel/fused_pad_reshape_transpose_rope_kvcache[_llama2].cu.
 #include "common.cuh"
+#include "rope_math.cuh"
 #include "tcgen05.cuh"
 
 #include <algorithm>
@@ -37,6 +55,9 @@ namespace l2k
 {
 
 __device__ int g_gemm_error = 0; // first error code recorded by the kernel of this file
+
+bool gemm_tc_supported(int dtype, int trans_a, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda,
+                       const void *b, int64_t ldb, const void *c);
 
 namespace
 {
@@ -66,16 +87,93 @@ enum GemmError
     ERR_GEMM_SMEM_ALIGN = 0x404
 };
 
+enum Epilogue
+{
+    EPI_STORE = 0,  // C = A op(B)
+    EPI_SWIGLU = 1, // C[:, j] = silu(P[:, j]) * P[:, up_col + j], P = A op(B)
+    EPI_ROPE = 2    // P's token rows rotated and written to q / the K and V caches
+};
+
+// EPI_ROPE: where a token row's heads go (the fused RoPE operators' arguments).
+struct RopeEpi
+{
+    void *q, *k, *v;
+    const uint8_t *is_done;        // decode
+    const uint32_t *q_lens;        // prefill
+    const uint32_t *kv_lens;
+    const uint32_t *unpad_to_pad;  // prefill
+    int64_t batch, hq, hkv, hd, qc, S;
+    const float2 *table;           // cos/sin table (16-byte aligned) or null
+    int64_t table_pos;
+    int pairing;
+    int prefill;
+};
+
 struct GemmTcArgs
 {
     void *c;
     int64_t ldc;
-    int64_t m, n;
-    int n_kb;   // k blocks
-    int n_nt;   // column tiles
-    int wide;   // C rows are 16-byte aligned: 16-byte stores
-    int split;  // SPLIT: CTAs per cluster sharing one C tile, each a K range
+    int64_t m, n;   // n: columns of C (EPI_SWIGLU: output columns F; EPI_ROPE: q/k/v columns)
+    int n_kb;       // k blocks
+    int n_nt;       // column tiles
+    int wide;       // C rows are 16-byte aligned: 16-byte stores
+    int split;      // SPLIT: CTAs per cluster sharing one C tile, each a K range
+    int64_t up_col; // EPI_SWIGLU: column of op(B) where the up half starts
+    RopeEpi rope;
 };
+
+// Rounds an fp32 accumulator to T and back (the value a separate launch reads).
+template <typename T>
+__device__ __forceinline__ float round_t(uint32_t bits)
+{
+    return to_f(from_f<T>(__uint_as_float(bits)));
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float *o)
+{
+    uint4 w;
+    w.x = pack2<T>(o[0], o[1]);
+    w.y = pack2<T>(o[2], o[3]);
+    w.z = pack2<T>(o[4], o[5]);
+    w.w = pack2<T>(o[6], o[7]);
+    return w;
+}
+
+// 32 consecutive values to a 16-byte aligned run of T.
+template <typename T>
+__device__ __forceinline__ void store32(T *dst, const float (&o)[32])
+{
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+        stg(dst + 8 * v, pack8<T>(o + 8 * v));
+}
+
+// Columns [col, col + 32) of a row, bounded at n: 16-byte stores when wide,
+// element stores at a ragged end.
+template <typename T>
+__device__ __forceinline__ void store_run(T *out, int64_t col, int64_t n, bool wide, const float (&o)[32])
+{
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+    {
+        const int64_t cv = col + 8 * v;
+        if (cv >= n)
+            break;
+        const uint4 w = pack8<T>(o + 8 * v);
+        if (wide && cv + 8 <= n)
+            stg(out + cv, w);
+        else
+        {
+            const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
+            for (int e = 0; e < 8 && cv + e < n; ++e)
+            {
+                const uint16_t bits = (uint16_t)(e & 1 ? (w4[e / 2] >> 16) : (w4[e / 2] & 0xFFFF));
+                reinterpret_cast<uint16_t *>(out)[cv + e] = bits;
+            }
+        }
+    }
+}
 
 // Pushes 4 floats into cluster rank 0's copy of *local_slot (16-byte
 // aligned) and signals 16 bytes on rank 0's copy of *local_bar.
@@ -115,10 +213,10 @@ __device__ __forceinline__ void gemm_fail(int code, volatile int *abort_flag)
 // contiguous range of the k blocks; once every rank's MMAs are done (cluster
 // barrier) ranks 1.. push their fp32 rows into rank 0's idle ring with
 // st.async, and rank 0 adds them to its own in rank order and stores.
-template <typename T, bool B_MN, int BN, int STAGES, bool SPLIT>
+template <typename T, bool B_MN, int BN, int STAGES, bool SPLIT, int EPI>
 __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                   const GemmTcArgs a)
+                   const __grid_constant__ GemmTcArgs a)
 {
     using C = Cfg<BN, STAGES>;
     constexpr int kStages = STAGES;
@@ -143,7 +241,10 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
     const int rank = SPLIT ? (int)(blockIdx.x % split) : 0;
     const int tile = (int)(blockIdx.x / split);
     const int mt = tile / a.n_nt, nt = tile % a.n_nt;
-    const int row0 = mt * BM, col0 = nt * BN;
+    const int row0 = mt * BM;
+    // first column of the tile in op(B) (EPI_SWIGLU: of the gate half, the up
+    // half starts at up_col + col0; also the first output column)
+    const int64_t col0 = EPI == EPI_SWIGLU ? (int64_t)nt * (BN / 2) : (int64_t)nt * BN;
     // this CTA's k blocks: [kb0, kb0 + n_kb)
     const int kb0 = (int)((int64_t)rank * a.n_kb / split);
     const int n_kb = (int)((int64_t)(rank + 1) * a.n_kb / split) - kb0;
@@ -194,10 +295,21 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
             {
 #pragma unroll
                 for (int h = 0; h < BN / 64; ++h)
-                    tma_load_3d(dst + kABox + h * BK * 128, &tm_b, col0 + 64 * h, kx, 0, bar);
+                {
+                    // EPI_SWIGLU: the second half of the boxes comes from the up columns
+                    const int64_t cx = EPI == EPI_SWIGLU && h >= BN / 128 ? a.up_col + col0 + 64 * (h - BN / 128)
+                                                                          : col0 + 64 * h;
+                    tma_load_3d(dst + kABox + h * BK * 128, &tm_b, (int)cx, kx, 0, bar);
+                }
+            }
+            else if constexpr (EPI == EPI_SWIGLU)
+            {
+                // two boxes of BN/2 rows, gate then up (whole 8-row swizzle groups)
+                tma_load_3d(dst + kABox, &tm_b, kx, (int)col0, 0, bar);
+                tma_load_3d(dst + kABox + (BN / 2) * 128, &tm_b, kx, (int)(a.up_col + col0), 0, bar);
             }
             else
-                tma_load_3d(dst + kABox, &tm_b, kx, col0, 0, bar);
+                tma_load_3d(dst + kABox, &tm_b, kx, (int)col0, 0, bar);
             issued = kb + 1;
         }
     }
@@ -231,12 +343,65 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
 
     // -------- epilogue: warp w holds rows row0 + 32 w + lane --------
     const int64_t row = row0 + 32 * warp + lane;
-    T *out = static_cast<T *>(a.c) + row * a.ldc;
     const bool store = row < a.m;
     const bool wide = a.wide != 0;
     const int lrow = 32 * warp + lane;          // row within the tile
     float *red = reinterpret_cast<float *>(smem); // SPLIT, rank 0: [split - 1][m][BN] peer rows (in the idle ring)
     const int m_tile = (int)min((int64_t)BM, a.m - row0);
+
+    // EPI_ROPE: this row's token, read before the MMAs are waited for. Tokens
+    // of finished sequences, padding slots past the batch and positions
+    // outside the cache are not written (as in the separate RoPE operators).
+    bool live = false;
+    int64_t seq = 0, slot = 0;
+    uint32_t kv_len = 0, pos = 0;
+    if constexpr (EPI == EPI_ROPE)
+    {
+        const RopeEpi &R = a.rope;
+        if (store)
+        {
+            if (R.prefill)
+            {
+                const int64_t padded = R.unpad_to_pad[row];
+                seq = padded / R.qc;
+                slot = padded - seq * R.qc;
+                if (seq < R.batch)
+                {
+                    kv_len = R.kv_lens[seq];
+                    pos = kv_len - R.q_lens[seq] + (uint32_t)slot;
+                    live = true;
+                }
+            }
+            else
+            {
+                seq = row;
+                kv_len = R.kv_lens[seq];
+                pos = kv_len - 1u;
+                live = R.is_done[seq] == 0;
+            }
+            live = live && (int64_t)pos < R.S;
+        }
+    }
+
+    // TMEM columns [c0, c0 + 32) of this warp's rows (every lane: the load is
+    // warp-wide), plus, on rank 0 of a SPLIT cluster, the peers' partial rows
+    // in rank order.
+    auto acc32 = [&](int c0, uint32_t(&r)[32]) {
+        tmem_ld32_async(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, r);
+        tmem_wait_ld();
+        if constexpr (SPLIT)
+        {
+            if (store)
+                for (int p = 1; p < split; ++p)
+                {
+                    const float *src = red + ((int64_t)(p - 1) * m_tile + lrow) * BN + c0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        r[j] = __float_as_uint(__uint_as_float(r[j]) + src[j]);
+                }
+        }
+    };
+
     if (n_kb > 0)
     {
         if (!mbar_wait(bar_done, 0, abort_flag))
@@ -279,52 +444,163 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
         }
         if (!*abort_flag && (!SPLIT || rank == 0))
         {
-#pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32)
+            if constexpr (EPI == EPI_STORE)
             {
-                uint32_t r[32];
-                tmem_ld32_async(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, r);
-                tmem_wait_ld();
-                if (!store)
-                    continue;
-                if constexpr (SPLIT)
+                T *out = static_cast<T *>(a.c) + row * a.ldc;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32)
                 {
-                    for (int p = 1; p < split; ++p)
-                    {
-                        const float *src = red + ((int64_t)(p - 1) * m_tile + lrow) * BN + c0;
+                    uint32_t r[32];
+                    acc32(c0, r);
+                    if (!store)
+                        continue;
+                    float o[32];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            r[j] = __float_as_uint(__uint_as_float(r[j]) + src[j]);
-                    }
+                    for (int j = 0; j < 32; ++j)
+                        o[j] = __uint_as_float(r[j]);
+                    store_run<T>(out, col0 + c0, a.n, wide, o);
                 }
-#pragma unroll
-                for (int v = 0; v < 4; ++v)
+            }
+            else if constexpr (EPI == EPI_SWIGLU)
+            {
+                // TMEM columns [0, BN/2): gate; [BN/2, BN): up
+                T *out = static_cast<T *>(a.c) + row * a.ldc;
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN / 2; c0 += 32)
                 {
-                    const int64_t col = (int64_t)col0 + c0 + 8 * v;
-                    if (col >= a.n)
-                        break;
-                    uint4 w;
-                    w.x = pack2<T>(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
-                    w.y = pack2<T>(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
-                    w.z = pack2<T>(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
-                    w.w = pack2<T>(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
-                    if (wide && col + 8 <= a.n)
-                        stg(out + col, w);
+                    uint32_t g[32], u[32];
+                    acc32(c0, g);
+                    acc32(BN / 2 + c0, u);
+                    if (!store)
+                        continue;
+                    float o[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        o[j] = silu_mul(round_t<T>(g[j]), round_t<T>(u[j]));
+                    store_run<T>(out, col0 + c0, a.n, wide, o);
+                }
+            }
+            else
+            {
+                // whole heads: TMEM columns [j hd, (j + 1) hd) hold head col0 / hd + j
+                const RopeEpi &R = a.rope;
+                const int hd = (int)R.hd, half = hd / 2;
+                const int64_t total_heads = R.hq + 2 * R.hkv;
+                const bool use_table = R.table && kv_len <= 4096u && (int64_t)pos < R.table_pos;
+                const float2 *trow = use_table ? R.table + (int64_t)pos * half : nullptr;
+                // cos/sin of pairs i and i + 1 (i even: one 16-byte table load)
+                auto cs2 = [&](int i, float(&c)[2], float(&s)[2]) {
+                    if (use_table)
+                    {
+                        const float4 cs = __ldg(reinterpret_cast<const float4 *>(trow + i));
+                        c[0] = cs.x;
+                        s[0] = cs.y;
+                        c[1] = cs.z;
+                        s[1] = cs.w;
+                    }
                     else
                     {
-                        const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
-                        for (int e = 0; e < 8 && col + e < a.n; ++e)
+                        rope_cos_sin_device(i, hd, pos, kv_len, c[0], s[0]);
+                        rope_cos_sin_device(i + 1, hd, pos, kv_len, c[1], s[1]);
+                    }
+                };
+#pragma unroll 1
+                for (int j = 0; j < BN / hd; ++j)
+                {
+                    const int64_t head = col0 / hd + j;
+                    if (head >= total_heads)
+                        break;
+                    const int hc = j * hd;
+                    T *dst = nullptr;
+                    if (live)
+                    {
+                        if (head < R.hq)
+                            dst = static_cast<T *>(R.q) + ((seq * R.hq + head) * R.qc + slot) * hd;
+                        else if (head < R.hq + R.hkv)
+                            dst = static_cast<T *>(R.k) + ((seq * R.hkv + head - R.hq) * R.S + pos) * hd;
+                        else
+                            dst = static_cast<T *>(R.v) + ((seq * R.hkv + head - R.hq - R.hkv) * R.S + pos) * hd;
+                    }
+                    if (head >= R.hq + R.hkv)
+                    {
+                        // v: copied unrotated
+#pragma unroll 1
+                        for (int c0 = 0; c0 < hd; c0 += 32)
                         {
-                            const uint16_t bits = (uint16_t)(e & 1 ? (w4[e / 2] >> 16) : (w4[e / 2] & 0xFFFF));
-                            reinterpret_cast<uint16_t *>(out)[col + e] = bits;
+                            uint32_t r[32];
+                            acc32(hc + c0, r);
+                            if (!dst)
+                                continue;
+                            float o[32];
+#pragma unroll
+                            for (int e = 0; e < 32; ++e)
+                                o[e] = round_t<T>(r[e]);
+                            store32<T>(dst + c0, o);
+                        }
+                    }
+                    else if (R.pairing == L2K_ROPE_INTERLEAVED)
+                    {
+                        // pairs (2i, 2i + 1): chunk c0 holds pairs c0/2 .. c0/2 + 15
+#pragma unroll 1
+                        for (int c0 = 0; c0 < hd; c0 += 32)
+                        {
+                            uint32_t r[32];
+                            acc32(hc + c0, r);
+                            if (!dst)
+                                continue;
+                            float o[32];
+#pragma unroll
+                            for (int e = 0; e < 16; e += 2)
+                            {
+                                float c[2], s[2];
+                                cs2(c0 / 2 + e, c, s);
+#pragma unroll
+                                for (int f = 0; f < 2; ++f)
+                                {
+                                    const float x0 = round_t<T>(r[2 * (e + f)]), x1 = round_t<T>(r[2 * (e + f) + 1]);
+                                    o[2 * (e + f)] = rope_o0(c[f], s[f], x0, x1);
+                                    o[2 * (e + f) + 1] = rope_o1(c[f], s[f], x0, x1);
+                                }
+                            }
+                            store32<T>(dst + c0, o);
+                        }
+                    }
+                    else
+                    {
+                        // pairs (i, i + hd/2): chunk c0 of each half
+#pragma unroll 1
+                        for (int c0 = 0; c0 < half; c0 += 32)
+                        {
+                            uint32_t r0[32], r1[32];
+                            acc32(hc + c0, r0);
+                            acc32(hc + half + c0, r1);
+                            if (!dst)
+                                continue;
+                            float o0[32], o1[32];
+#pragma unroll
+                            for (int e = 0; e < 32; e += 2)
+                            {
+                                float c[2], s[2];
+                                cs2(c0 + e, c, s);
+#pragma unroll
+                                for (int f = 0; f < 2; ++f)
+                                {
+                                    const float x0 = round_t<T>(r0[e + f]), x1 = round_t<T>(r1[e + f]);
+                                    o0[e + f] = rope_o0(c[f], s[f], x0, x1);
+                                    o1[e + f] = rope_o1(c[f], s[f], x0, x1);
+                                }
+                            }
+                            store32<T>(dst + c0, o0);
+                            store32<T>(dst + half + c0, o1);
                         }
                     }
                 }
             }
         }
     }
-    else if (store)
+    else if (EPI == EPI_STORE && store)
     {
+        T *out = static_cast<T *>(a.c) + row * a.ldc;
         for (int64_t col = col0; col < min((int64_t)col0 + BN, a.n); ++col)
             out[col] = from_f<T>(0.f); // K = 0: a zero tile
     }
@@ -347,32 +623,48 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
     }
 }
 
-template <typename T, bool B_MN, int BN, int STAGES, bool SPLIT = false>
-int launch_gemm_tc(const void *A, int64_t lda, const void *B, int64_t ldb, void *C, int64_t ldc, int64_t m,
-                   int64_t n, int64_t k, cudaStream_t stream, int split = 1)
+// One GEMM and its epilogue: A (m x k, row stride lda), B (row stride ldb)
+// whose op(B) has nb columns, and the kernel arguments the caller fills (c,
+// ldc, n, up_col, rope).
+struct GemmProblem
+{
+    const void *a;
+    int64_t lda;
+    const void *b;
+    int64_t ldb;
+    int64_t m, nb, k;
+    GemmTcArgs args;
+};
+
+template <typename T, bool B_MN, int BN, int STAGES, bool SPLIT, int EPI>
+int launch_gemm_tc(const GemmProblem &p, cudaStream_t stream, int split)
 {
     constexpr uint32_t kSmemBytes = Cfg<BN, STAGES>::kSmemBytes;
     const CUtensorMapDataType dt =
         std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t m = (uint64_t)p.m, nb = (uint64_t)p.nb, k = (uint64_t)p.k;
+    const uint64_t lda = (uint64_t)p.lda, ldb = (uint64_t)p.ldb;
     CUtensorMap ma, mb;
-    bool ok = make_map(&ma, dt, A, (uint64_t)k, (uint64_t)m, 1, (uint64_t)lda * 2, (uint64_t)(lda * 2 * m), BM, BK);
+    bool ok = make_map(&ma, dt, p.a, k, m, 1, lda * 2, lda * 2 * m, BM, BK);
     if (B_MN) // B stored K x N: boxes of 64 k rows x 64 columns
-        ok = ok && make_map(&mb, dt, B, (uint64_t)n, (uint64_t)k, 1, (uint64_t)ldb * 2, (uint64_t)(ldb * 2 * k), BK,
-                            64);
-    else // B stored N x K: boxes of BN n rows x 64 k
-        ok = ok && make_map(&mb, dt, B, (uint64_t)k, (uint64_t)n, 1, (uint64_t)ldb * 2, (uint64_t)(ldb * 2 * n), BN,
-                            BK);
+        ok = ok && make_map(&mb, dt, p.b, nb, k, 1, ldb * 2, ldb * 2 * k, BK, 64);
+    else // B stored N x K: boxes of BN n rows x 64 k (EPI_SWIGLU: two boxes of BN/2 rows)
+        ok = ok && make_map(&mb, dt, p.b, k, nb, 1, ldb * 2, ldb * 2 * nb, EPI == EPI_SWIGLU ? BN / 2 : BN, BK);
     if (!ok)
         return set_error(L2K_ERR_CUDA, "l2k_linear: tensor map encoding failed");
-    GemmTcArgs a{C, ldc, m, n, (int)ceil_div(k, BK), (int)ceil_div(n, BN),
-                 (ldc * 2) % 16 == 0 && is_aligned(C, 16) ? 1 : 0, split};
-    auto kernel = gemm_tc_kernel<T, B_MN, BN, STAGES, SPLIT>;
+    GemmTcArgs a = p.args;
+    a.m = p.m;
+    a.n_kb = (int)ceil_div(p.k, BK);
+    a.n_nt = (int)ceil_div(a.n, EPI == EPI_SWIGLU ? BN / 2 : BN);
+    a.wide = EPI != EPI_ROPE && (a.ldc * 2) % 16 == 0 && is_aligned(a.c, 16) ? 1 : 0;
+    a.split = split;
+    auto kernel = gemm_tc_kernel<T, B_MN, BN, STAGES, SPLIT, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e == cudaSuccess) // two CTAs per SM need the whole shared-memory carveout
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess)
         return set_error(L2K_ERR_CUDA, "l2k_linear: %s", cudaGetErrorString(e));
-    const int64_t grid = ceil_div(m, BM) * a.n_nt * split;
+    const int64_t grid = ceil_div(p.m, BM) * a.n_nt * split;
     if (!SPLIT)
     {
         kernel<<<(unsigned)grid, kThreads, kSmemBytes, stream>>>(ma, mb, a);
@@ -396,6 +688,74 @@ int launch_gemm_tc(const void *A, int64_t lda, const void *B, int64_t ldb, void 
     return check_launch("l2k_linear (tcgen05, split k)");
 }
 
+// Tile shape by M: above 128 rows, 128 x 256 tiles (N = 256 MMAs read half
+// the A operand per FLOP from shared memory) in a 2-stage ring, two CTAs per
+// SM; up to 128 rows (decode-sized products, bound by reading B), 128 x 128
+// tiles for twice the CTAs, in a 4-stage ring. The choice depends on m, the
+// columns of op(B) and k only, so an epilogue variant runs the same tiles
+// (and accumulates the same sums) as the plain product.
+template <typename T, bool B_MN, int EPI>
+int launch_tiles(const GemmProblem &p, cudaStream_t stream)
+{
+    if (p.m > BM)
+        return launch_gemm_tc<T, B_MN, 256, 2, false, EPI>(p, stream, 1);
+    // One row tile: too few CTAs to stream B at full bandwidth unless K is
+    // split across a cluster (the peers' fp32 rows must fit rank 0's ring).
+    constexpr int kSplitStages = 3;
+    const int64_t tiles = ceil_div(p.nb, 128), n_kb = ceil_div(p.k, BK);
+    const int64_t ring = (int64_t)kSplitStages * Cfg<128, kSplitStages>::kStageBytes;
+    int split = 1;
+    while (split < 8 && tiles * split * 2 <= 2LL * num_sms() && split * 2 <= n_kb &&
+           (int64_t)(split * 2 - 1) * p.m * 128 * 4 <= ring)
+        split *= 2;
+    if (split > 1)
+        return launch_gemm_tc<T, B_MN, 128, kSplitStages, true, EPI>(p, stream, split);
+    return launch_gemm_tc<T, B_MN, 128, 4, false, EPI>(p, stream, 1);
+}
+
+template <int EPI>
+int dispatch_tc(int trans_b, int dtype, const GemmProblem &p, cudaStream_t stream)
+{
+    if (dtype == L2K_BF16)
+        return trans_b ? launch_tiles<__nv_bfloat16, false, EPI>(p, stream)
+                       : launch_tiles<__nv_bfloat16, true, EPI>(p, stream);
+    return trans_b ? launch_tiles<__half, false, EPI>(p, stream) : launch_tiles<__half, true, EPI>(p, stream);
+}
+
+// Checks and launch of the RoPE epilogue (m token rows of A).
+int rope_gemm_entry(int trans_b, const void *a, int64_t lda, const void *b, int64_t ldb, int64_t dim,
+                    const RopeEpi &r, int64_t m, int dtype, cudaStream_t stream, const char *name)
+{
+    L2K_REQUIRE(dtype_ok(dtype), "%s: unsupported dtype %d", name, dtype);
+    L2K_REQUIRE(r.pairing == L2K_ROPE_INTERLEAVED || r.pairing == L2K_ROPE_HALF, "%s: bad pairing %d", name,
+                r.pairing);
+    L2K_REQUIRE(m >= 0 && dim >= 0 && r.batch >= 0 && r.hq >= 0 && r.hkv >= 0 && r.hd >= 0 && r.S >= 0 &&
+                    r.qc >= 0 && r.table_pos >= 0,
+                "%s: negative size", name);
+    const int64_t n = (r.hq + 2 * r.hkv) * r.hd;
+    L2K_REQUIRE(lda >= dim && ldb >= (trans_b ? dim : n), "%s: leading dimension too small", name);
+    if (m == 0 || n == 0)
+        return L2K_OK;
+    L2K_REQUIRE(a && b && r.kv_lens && r.q && (r.hkv == 0 || (r.k && r.v)), "%s: null pointer", name);
+    if (r.prefill)
+        L2K_REQUIRE(r.q_lens && r.unpad_to_pad && r.qc > 0, "%s: null q_lens/unpad_to_pad or q_cache_len 0", name);
+    else
+        L2K_REQUIRE(r.is_done, "%s: null is_done", name);
+    if (dtype == L2K_F32)
+        return set_error(L2K_ERR_UNSUPPORTED_DTYPE, "%s: tensor cores take 16-bit data only", name);
+    L2K_REQUIRE_SHAPE((r.hd == 64 || r.hd == 128) && is_aligned(r.q, 16) &&
+                          (r.hkv == 0 || (is_aligned(r.k, 16) && is_aligned(r.v, 16))) &&
+                          (r.table == nullptr || is_aligned(r.table, 16)) &&
+                          gemm_tc_supported(dtype, 0, m, n, dim, a, lda, b, ldb, r.q),
+                      "%s: needs head_dim 64 or 128, 16-byte aligned q/k/v/table and operands, k >= 1 "
+                      "(run l2k_linear and the RoPE operator instead)",
+                      name);
+    GemmProblem p{a, lda, b, ldb, m, n, dim, GemmTcArgs{}};
+    p.args.n = n;
+    p.args.rope = r;
+    return dispatch_tc<EPI_ROPE>(trans_b ? 1 : 0, dtype, p, stream);
+}
+
 } // namespace
 
 // Whether the tensor-core path takes this plain GEMM: 16-bit, trans_A false,
@@ -409,38 +769,14 @@ bool gemm_tc_supported(int dtype, int trans_a, int64_t m, int64_t n, int64_t k, 
            n < (int64_t(1) << 31) && k < (int64_t(1) << 31) && encode_fn() != nullptr;
 }
 
-// Tile shape by M: above 128 rows, 128 x 256 tiles (N = 256 MMAs read half
-// the A operand per FLOP from shared memory) in a 2-stage ring, two CTAs per
-// SM; up to 128 rows (decode-sized products, bound by reading B), 128 x 128
-// tiles for twice the CTAs, in a 4-stage ring.
-template <typename T, bool B_MN>
-int launch_tiles(const void *a, int64_t lda, const void *b, int64_t ldb, void *c, int64_t ldc, int64_t m, int64_t n,
-                 int64_t k, cudaStream_t stream)
-{
-    if (m > BM)
-        return launch_gemm_tc<T, B_MN, 256, 2>(a, lda, b, ldb, c, ldc, m, n, k, stream);
-    // One row tile: too few CTAs to stream B at full bandwidth unless K is
-    // split across a cluster (the peers' fp32 rows must fit rank 0's ring).
-    constexpr int kSplitStages = 3;
-    const int64_t tiles = ceil_div(n, 128), n_kb = ceil_div(k, BK);
-    const int64_t ring = (int64_t)kSplitStages * Cfg<128, kSplitStages>::kStageBytes;
-    int split = 1;
-    while (split < 8 && tiles * split * 2 <= 2LL * num_sms() && split * 2 <= n_kb &&
-           (int64_t)(split * 2 - 1) * m * 128 * 4 <= ring)
-        split *= 2;
-    if (split > 1)
-        return launch_gemm_tc<T, B_MN, 128, kSplitStages, true>(a, lda, b, ldb, c, ldc, m, n, k, stream, split);
-    return launch_gemm_tc<T, B_MN, 128, 4>(a, lda, b, ldb, c, ldc, m, n, k, stream);
-}
-
 int gemm_tc(int trans_b, int64_t m, int64_t n, int64_t k, const void *a, int64_t lda, const void *b, int64_t ldb,
             void *c, int64_t ldc, int dtype, cudaStream_t stream)
 {
-    if (dtype == L2K_BF16)
-        return trans_b ? launch_tiles<__nv_bfloat16, false>(a, lda, b, ldb, c, ldc, m, n, k, stream)
-                       : launch_tiles<__nv_bfloat16, true>(a, lda, b, ldb, c, ldc, m, n, k, stream);
-    return trans_b ? launch_tiles<__half, false>(a, lda, b, ldb, c, ldc, m, n, k, stream)
-                   : launch_tiles<__half, true>(a, lda, b, ldb, c, ldc, m, n, k, stream);
+    GemmProblem p{a, lda, b, ldb, m, n, k, GemmTcArgs{}};
+    p.args.c = c;
+    p.args.ldc = ldc;
+    p.args.n = n;
+    return dispatch_tc<EPI_STORE>(trans_b, dtype, p, stream);
 }
 
 int read_gemm_error(bool clear)
@@ -458,3 +794,60 @@ int read_gemm_error(bool clear)
 }
 
 } // namespace l2k
+
+extern "C" int l2k_linear_swiglu(int trans_b, int64_t m, int64_t inter, int64_t k, const void *a, int64_t lda,
+                                 const void *b, int64_t ldb, void *out, int64_t ldo, int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    L2K_REQUIRE(dtype_ok(dtype), "l2k_linear_swiglu: unsupported dtype %d", dtype);
+    L2K_REQUIRE(m >= 0 && inter >= 0 && k >= 0, "l2k_linear_swiglu: negative size");
+    L2K_REQUIRE(ldo >= inter && lda >= k && ldb >= (trans_b ? k : 2 * inter),
+                "l2k_linear_swiglu: leading dimension too small");
+    if (m == 0 || inter == 0)
+        return L2K_OK;
+    L2K_REQUIRE(a && b && out, "l2k_linear_swiglu: null pointer");
+    if (dtype == L2K_F32)
+        return set_error(L2K_ERR_UNSUPPORTED_DTYPE, "l2k_linear_swiglu: tensor cores take 16-bit data only");
+    L2K_REQUIRE_SHAPE(inter % 8 == 0 && gemm_tc_supported(dtype, 0, m, 2 * inter, k, a, lda, b, ldb, out),
+                      "l2k_linear_swiglu: needs inter %% 8 == 0, 16-byte aligned operands and k >= 1 "
+                      "(run l2k_linear and l2k_swiglu instead)");
+    GemmProblem p{a, lda, b, ldb, m, 2 * inter, k, GemmTcArgs{}};
+    p.args.c = out;
+    p.args.ldc = ldo;
+    p.args.n = inter;
+    p.args.up_col = inter;
+    return dispatch_tc<EPI_SWIGLU>(trans_b ? 1 : 0, dtype, p, stream);
+}
+
+extern "C" int l2k_linear_rope_kvcache_decode(int trans_b, const void *a, int64_t lda, const void *b, int64_t ldb,
+                                              int64_t dim, const uint8_t *is_done, const uint32_t *kv_lens, void *q,
+                                              void *k, void *v, int64_t batch, int64_t q_head_num,
+                                              int64_t kv_head_num, int64_t head_dim, int64_t kv_cache_len,
+                                              const float *rope_table, int64_t rope_table_positions, int pairing,
+                                              int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    const RopeEpi r{q,         k,           v,        is_done,     nullptr, kv_lens, nullptr,
+                    batch,     q_head_num,  kv_head_num, head_dim, 1,       kv_cache_len,
+                    reinterpret_cast<const float2 *>(rope_table), rope_table ? rope_table_positions : 0,
+                    pairing,   0};
+    return rope_gemm_entry(trans_b, a, lda, b, ldb, dim, r, batch, dtype, stream, "l2k_linear_rope_kvcache_decode");
+}
+
+extern "C" int l2k_linear_pad_rope_kvcache_prefill(int trans_b, const void *a, int64_t lda, const void *b,
+                                                   int64_t ldb, int64_t dim, const uint32_t *q_lens,
+                                                   const uint32_t *kv_lens, const uint32_t *unpad_to_pad_idx, void *q,
+                                                   void *k, void *v, int64_t num_tokens, int64_t batch,
+                                                   int64_t q_head_num, int64_t kv_head_num, int64_t head_dim,
+                                                   int64_t q_cache_len, int64_t kv_cache_len,
+                                                   const float *rope_table, int64_t rope_table_positions, int pairing,
+                                                   int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    const RopeEpi r{q,           k,          v,           nullptr,  q_lens,      kv_lens, unpad_to_pad_idx,
+                    batch,       q_head_num, kv_head_num, head_dim, q_cache_len, kv_cache_len,
+                    reinterpret_cast<const float2 *>(rope_table), rope_table ? rope_table_positions : 0,
+                    pairing,     1};
+    return rope_gemm_entry(trans_b, a, lda, b, ldb, dim, r, num_tokens, dtype, stream,
+                           "l2k_linear_pad_rope_kvcache_prefill");
+}

@@ -23,6 +23,12 @@ GEMM). Nine launches per layer; ``capture_decode`` records a layer step as a
 CUDA graph. ``prefill`` runs the same layer over the new tokens of a batch of
 prompts (eleven launches: the scores, P.V and the unpad replace the fused
 decode attention).
+
+With 16-bit weights and more than 8 rows (where launch_linear runs on the
+tensor cores) the QKV projection takes the RoPE + K/V append into its
+epilogue and the gate/up projection the SwiGLU (``fuse_epilogues``, on by
+default): two launches fewer and neither product goes to HBM, with results
+bit-identical to the separate launches.
 """
 from __future__ import annotations
 
@@ -35,12 +41,15 @@ from . import ops
 
 class DecoderLayer:
     def __init__(self, dim: int, heads: int, kv_heads: int, hidden: int, kv_cache_len: int, batch: int,
-                 dtype=torch.bfloat16, device="cuda", seed: int = 0, pairing: int = 1):
+                 dtype=torch.bfloat16, device="cuda", seed: int = 0, pairing: int = 1, fuse_epilogues: bool = True):
         if dim % heads or heads % kv_heads:
             raise ValueError("dim must be a multiple of heads, heads of kv_heads")
         self.dim, self.heads, self.kv_heads, self.hidden = dim, heads, kv_heads, hidden
         self.head_dim = dim // heads
         self.kv_cache_len, self.batch, self.dtype, self.pairing = kv_cache_len, batch, dtype, pairing
+        # the epilogue kernels' shape rules (16-bit, head_dim 64 or 128, F % 8 == 0)
+        self.fuse_epilogues = (fuse_epilogues and dtype != torch.float32 and self.head_dim in (64, 128)
+                               and hidden % 8 == 0)
         self.device = torch.device(device)
         hd, d, f = self.head_dim, dim, hidden
         g = torch.Generator(device=self.device)
@@ -61,12 +70,13 @@ class DecoderLayer:
         # activations of one step
         e = dict(dtype=dtype, device=self.device)
         self.h = torch.empty(batch, d, **e)
-        self.qkv = torch.empty(batch, (heads + 2 * kv_heads) * hd, **e)
+        unfused = not self._fused(batch)  # products the epilogue kernels do not store
+        self.qkv = torch.empty(batch if unfused else 0, (heads + 2 * kv_heads) * hd, **e)
         self.q = torch.zeros(batch, heads, 1, hd, **e)  # finished sequences keep this (RoPE skips them)
         self.qk = torch.zeros(batch, heads, 1, kv_cache_len, **e)
         self.attn = torch.empty(batch, heads, 1, hd, **e)
         self.o = torch.empty(batch, d, **e)
-        self.gate_up = torch.empty(batch, 2 * f, **e)
+        self.gate_up = torch.empty(batch if unfused else 0, 2 * f, **e)
         self.act = torch.empty(batch, f, **e)
         self.down = torch.empty(batch, d, **e)
         ops.rope_table(hd, self.device)  # built before any graph capture
@@ -87,17 +97,33 @@ class DecoderLayer:
         else:
             ops.launch_fused_add_residual_rmsnorm(self.w_attn_norm, x, pending, True)
             h = pending  # the normed rows land in the residual argument
-        ops.launch_linear(False, False, b, self.qkv.shape[1], d, h, self.w_qkv, self.qkv)
-        rope = (ops.launch_fused_reshape_rope_kvcache_llama2_decode if self.pairing
-                else ops.launch_fused_reshape_rope_kvcache_decode)
-        rope(self.qkv, is_done, kv_lens, self.q, self.k_cache, self.v_cache)
+        fuse = self._fused(b)
+        if fuse:
+            ops.linear_rope_kvcache_decode(h, self.w_qkv, is_done, kv_lens, self.q, self.k_cache, self.v_cache,
+                                           pairing=self.pairing)
+        else:
+            ops.launch_linear(False, False, b, self.qkv.shape[1], d, h, self.w_qkv, self.qkv)
+            rope = (ops.launch_fused_reshape_rope_kvcache_llama2_decode if self.pairing
+                    else ops.launch_fused_reshape_rope_kvcache_decode)
+            rope(self.qkv, is_done, kv_lens, self.q, self.k_cache, self.v_cache)
         ops.decode_attention(self.q, self.k_cache, self.v_cache, kv_lens, max_kv_len, self.qk, self.attn)
         ops.launch_linear(False, False, b, d, d, self.attn.view(b, d), self.w_o, self.o)
         ops.launch_fused_add_residual_rmsnorm(self.w_ffn_norm, x, self.o, True)
-        ops.launch_linear(False, False, b, 2 * f, d, self.o, self.w_gate_up, self.gate_up)
-        ops.launch_swiglu(self.gate_up, self.act)
+        self._gate_up_swiglu(b, self.o, self.gate_up, self.act, fuse)
         ops.launch_linear(False, False, b, d, f, self.act, self.w_down, self.down)
         return self.down
+
+    def _fused(self, rows: int) -> bool:
+        """Whether this pass uses the epilogue kernels: above 8 rows, where
+        launch_linear itself runs on the tensor cores."""
+        return self.fuse_epilogues and rows > 8
+
+    def _gate_up_swiglu(self, rows, h, gate_up, act, fuse):
+        if fuse:
+            ops.linear_swiglu(h, self.w_gate_up, act)
+        else:
+            ops.launch_linear(False, False, rows, 2 * self.hidden, self.dim, h, self.w_gate_up, gate_up)
+            ops.launch_swiglu(gate_up, act)
 
     def capture_decode(self, x, pending, kv_lens, max_kv_len, is_done):
         """A CUDA graph of one decode() call on these tensors."""
@@ -132,17 +158,21 @@ class DecoderLayer:
         else:
             ops.launch_fused_add_residual_rmsnorm(self.w_attn_norm, x, pending, True)
             h = pending
-        ops.launch_linear(False, False, t, buf["qkv"].shape[1], d, h, self.w_qkv, buf["qkv"])
-        rope = (ops.launch_fused_pad_reshape_transpose_rope_kvcache_llama2 if self.pairing
-                else ops.launch_fused_pad_reshape_transpose_rope_kvcache)
-        rope(buf["qkv"], q_lens, kv_lens, unpad_to_pad.view(-1), buf["q"], self.k_cache, self.v_cache)
+        fuse = self._fused(t)
+        if fuse:
+            ops.linear_pad_rope_kvcache_prefill(h, self.w_qkv, q_lens, kv_lens, unpad_to_pad.view(-1), buf["q"],
+                                                self.k_cache, self.v_cache, pairing=self.pairing)
+        else:
+            ops.launch_linear(False, False, t, buf["qkv"].shape[1], d, h, self.w_qkv, buf["qkv"])
+            rope = (ops.launch_fused_pad_reshape_transpose_rope_kvcache_llama2 if self.pairing
+                    else ops.launch_fused_pad_reshape_transpose_rope_kvcache)
+            rope(buf["qkv"], q_lens, kv_lens, unpad_to_pad.view(-1), buf["q"], self.k_cache, self.v_cache)
         ops.prefill_attention_scores(buf["q"], self.k_cache, q_lens, kv_lens, max_q, max_kv, buf["qk"])
         ops.launch_attention_qkv(buf["qk"], self.v_cache, buf["pv"], max_q, max_kv)
         ops.launch_fused_transpose_unpad(t, buf["pv"], unpad_to_pad.view(-1), buf["attn"])
         ops.launch_linear(False, False, t, d, d, buf["attn"], self.w_o, buf["o"])
         ops.launch_fused_add_residual_rmsnorm(self.w_ffn_norm, x, buf["o"], True)
-        ops.launch_linear(False, False, t, 2 * f, d, buf["o"], self.w_gate_up, buf["gate_up"])
-        ops.launch_swiglu(buf["gate_up"], buf["act"])
+        self._gate_up_swiglu(t, buf["o"], buf["gate_up"], buf["act"], fuse)
         ops.launch_linear(False, False, t, d, f, buf["act"], self.w_down, buf["down"])
         return buf["down"]
 
@@ -151,18 +181,18 @@ class DecoderLayer:
         if getattr(self, "_pf_key", None) != key:
             b, h, kvh, hd, d, f = self.batch, self.heads, self.kv_heads, self.head_dim, self.dim, self.hidden
             e = dict(dtype=self.dtype, device=self.device)
-            self._pf = {"h": torch.empty(t, d, **e), "qkv": torch.empty(t, (h + 2 * kvh) * hd, **e),
+            # the products that the epilogue kernels never store are not allocated for them
+            unfused = not self._fused(t)
+            self._pf = {"h": torch.empty(t, d, **e), "qkv": torch.empty(t if unfused else 0, (h + 2 * kvh) * hd, **e),
                         "q": torch.zeros(b, h, qc, hd, **e), "qk": torch.zeros(b, h, qc, self.kv_cache_len, **e),
                         "pv": torch.zeros(b, h, qc, hd, **e), "attn": torch.empty(t, d, **e),
-                        "o": torch.empty(t, d, **e), "gate_up": torch.empty(t, 2 * f, **e),
+                        "o": torch.empty(t, d, **e), "gate_up": torch.empty(t if unfused else 0, 2 * f, **e),
                         "act": torch.empty(t, f, **e), "down": torch.empty(t, d, **e)}
             self._pf_key = key
         return self._pf
 
-    @staticmethod
-    def launches_per_step() -> int:
-        return 9
+    def launches_per_step(self) -> int:
+        return 7 if self._fused(self.batch) else 9
 
-    @staticmethod
-    def launches_per_prefill() -> int:
-        return 11
+    def launches_per_prefill(self, tokens: int) -> int:
+        return 9 if self._fused(tokens) else 11

@@ -163,8 +163,9 @@ def bench_rope(iters):
 
 def bench_layer(iters):
     from .layer import DecoderLayer
-    for (b, dt) in ((64, torch.bfloat16), (1, torch.bfloat16), (64, torch.float32)):
-        layer = DecoderLayer(4096, 32, 32, 11008, 4096, b, dtype=dt, seed=0)
+    for (b, dt, fuse) in ((64, torch.bfloat16, True), (64, torch.bfloat16, False), (1, torch.bfloat16, True),
+                          (64, torch.float32, True)):
+        layer = DecoderLayer(4096, 32, 32, 11008, 4096, b, dtype=dt, seed=0, fuse_epilogues=fuse)
         x = torch.randn(b, 4096, device="cuda").to(dt)
         q_lens = torch.ones(b, dtype=torch.uint32, device="cuda")
         lens = torch.randint(1, 4095, (b,), generator=torch.Generator().manual_seed(0))
@@ -178,9 +179,24 @@ def bench_layer(iters):
         es = 2 if dt != torch.float32 else 4
         wbytes = sum(t.numel() for t in layer.weights().values()) * es
         kvb = 2 * int((lens + 1).sum()) * 4096 * es
-        print(f"7B decoder layer decode step {dt} b={b}: {ms * 1e3:.1f} us; weights {wbytes / 1e6:.0f} MB + "
+        print(f"7B decoder layer decode step {dt} b={b} ({layer.launches_per_step()} launches): "
+              f"{ms * 1e3:.1f} us; weights {wbytes / 1e6:.0f} MB + "
               f"K/V {kvb / 1e6:.0f} MB -> {(wbytes + kvb) / ms / 1e6:.0f} GB/s")
         del layer, graph
+    # prefill pass of 8 prompts x 2048 new tokens (16384 token rows)
+    b, qc = 8, 2048
+    t = b * qc
+    for fuse in (True, False):
+        layer = DecoderLayer(4096, 32, 32, 11008, qc, b, dtype=torch.bfloat16, seed=0, fuse_epilogues=fuse)
+        x = torch.randn(t, 4096, device="cuda").to(torch.bfloat16)
+        q_lens = torch.full((b,), qc, dtype=torch.uint32, device="cuda")
+        unpad = torch.zeros(b, qc, dtype=torch.uint32, device="cuda")
+        offsets = torch.zeros(b, dtype=torch.uint32, device="cuda")
+        ops.launch_build_padding_index_maps(t, q_lens, unpad, offsets)
+        ms = time_ms(lambda: layer.prefill(x, None, q_lens, q_lens, qc, qc, unpad), iters)
+        print(f"7B decoder layer prefill bf16 {t} tokens ({layer.launches_per_prefill(t)} launches): "
+              f"{ms * 1e3:.1f} us, {t / ms / 1e3:.2f} M tokens/s")
+        del layer
 
 
 def main():

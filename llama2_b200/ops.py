@@ -303,6 +303,71 @@ def launch_swiglu(input, output):
     capi.call("l2k_swiglu", input.data_ptr(), output.data_ptr(), n, f, _code(output), _stream())
 
 
+def linear_swiglu(A, B, out, *, trans_B=False):
+    """out = swiglu(A op(B)) in one launch: the gate/up projection with
+    launch_swiglu in its epilogue (A [T, K]; B [K, 2F], or [2F, K] with
+    trans_B; out [T, F]). Raises capi.L2KError (status 3) for shapes the
+    tensor-core kernel does not take."""
+    _dev(A, B, out)
+    _same(A, B, "linear_swiglu")
+    _same(A, out, "linear_swiglu")
+    t, k = A.shape
+    f = out.shape[1]
+    _require(out.shape[0] == t, "Incorrect output size")
+    _require(tuple(B.shape) == ((2 * f, k) if trans_B else (k, 2 * f)), "Incorrect weight size")
+    capi.call("l2k_linear_swiglu", int(bool(trans_B)), t, f, k, A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0),
+              out.data_ptr(), out.stride(0), _code(out), _stream())
+
+
+def linear_rope_kvcache_decode(A, B, is_done, kv_lens, q, k, v, *, pairing, trans_B=False, use_table=True):
+    """The QKV projection of a decode step with the decode RoPE + K/V append
+    in its epilogue: P = A op(B) (A [B, D]; B [D, (Hq + 2 Hkv) hd] or its
+    transpose), then launch_fused_reshape_rope_kvcache[_llama2]_decode(P, ...)
+    without storing P."""
+    _dev(A, B, is_done, kv_lens, q, k, v)
+    _u32(kv_lens, "kv_lens")
+    for t in (B, q, k, v):
+        _same(A, t, "linear_rope_kvcache_decode")
+    b, hq, one, hd = q.shape
+    hkv, s = k.shape[1], k.shape[2]
+    n = (hq + 2 * hkv) * hd
+    _require(one == 1 and A.shape[0] == b, "Incorrect batch size")
+    _require(tuple(B.shape) == ((n, A.shape[1]) if trans_B else (A.shape[1], n)), "Incorrect weight size")
+    _require(tuple(k.shape) == (b, hkv, s, hd) and tuple(v.shape) == (b, hkv, s, hd), "Incorrect k v cache size")
+    tab = rope_table(hd, q.device) if use_table else None
+    capi.call("l2k_linear_rope_kvcache_decode", int(bool(trans_B)), A.data_ptr(), A.stride(0), B.data_ptr(),
+              B.stride(0), A.shape[1], is_done.data_ptr(), kv_lens.data_ptr(), q.data_ptr(), k.data_ptr(),
+              v.data_ptr(), b, hq, hkv, hd, s, tab.data_ptr() if tab is not None else None,
+              ROPE_TABLE_POSITIONS if tab is not None else 0, int(pairing), _code(q), _stream())
+
+
+def linear_pad_rope_kvcache_prefill(A, B, q_lens, kv_lens, unpad_to_pad_idx, q, k, v, *, pairing, trans_B=False,
+                                    use_table=True):
+    """The QKV projection of a prefill pass with the padded RoPE + K/V append
+    in its epilogue: P = A op(B) over the T unpadded token rows, then
+    launch_fused_pad_reshape_transpose_rope_kvcache[_llama2](P, ...) without
+    storing P."""
+    _dev(A, B, q_lens, kv_lens, unpad_to_pad_idx, q, k, v)
+    for t, nm in ((q_lens, "q_lens"), (kv_lens, "kv_lens"), (unpad_to_pad_idx, "unpad_to_pad_idx")):
+        _u32(t, nm)
+    for t in (B, q, k, v):
+        _same(A, t, "linear_pad_rope_kvcache_prefill")
+    tokens = A.shape[0]
+    b, hq, qc, hd = q.shape
+    hkv, s = k.shape[1], k.shape[2]
+    n = (hq + 2 * hkv) * hd
+    _require(tuple(B.shape) == ((n, A.shape[1]) if trans_B else (A.shape[1], n)), "Incorrect weight size")
+    _require(tuple(k.shape) == (b, hkv, s, hd) and tuple(v.shape) == (b, hkv, s, hd), "Incorrect k v cache size")
+    _require(q_lens.shape[0] == b and kv_lens.shape[0] == b, "Incorrect batch size of sequence length")
+    _require(unpad_to_pad_idx.numel() >= tokens, "unpad_to_pad_idx too small")
+    tab = rope_table(hd, q.device) if use_table else None
+    capi.call("l2k_linear_pad_rope_kvcache_prefill", int(bool(trans_B)), A.data_ptr(), A.stride(0), B.data_ptr(),
+              B.stride(0), A.shape[1], q_lens.data_ptr(), kv_lens.data_ptr(), unpad_to_pad_idx.data_ptr(),
+              q.data_ptr(), k.data_ptr(), v.data_ptr(), tokens, b, hq, hkv, hd, qc, s,
+              tab.data_ptr() if tab is not None else None, ROPE_TABLE_POSITIONS if tab is not None else 0,
+              int(pairing), _code(q), _stream())
+
+
 def launch_fused_transpose_unpad(num_input_tokens, qkv, unpad_to_pad_idx, unpad_qkv):
     """include/kernel/fused_transpose_unpad.h:6-11 (qkv (B, H, Qc, hd) -> unpad_qkv (T, H * hd))."""
     _dev(qkv, unpad_to_pad_idx, unpad_qkv)

@@ -65,6 +65,15 @@ def test_status_strings():
     ("l2k_decode_attention", (None, None, None, None, None, None, None, 2, 4, 2, 64, 128, 0, None), 1),
     ("l2k_decode_attention", (None, None, None, None, None, None, None, 2, 4, 3, 64, 128, 0, None), 1),
     ("l2k_decode_attention", (None, None, None, None, None, None, None, 2, 4, 2, 64, 0, 0, None), 1),
+    ("l2k_linear_swiglu", (0, 16, 8, 64, None, 64, None, 16, None, 8, 2, None), 1),  # null pointers
+    ("l2k_linear_swiglu", (0, 16, 8, 64, 16, 64, 16, 8, 16, 8, 2, None), 1),        # ldb < 2 inter
+    ("l2k_linear_swiglu", (0, 16, 8, 64, 16, 64, 16, 16, 16, 8, 0, None), 2),       # f32
+    ("l2k_linear_rope_kvcache_decode", (0, None, 64, None, 512, 64, None, None, None, None, None, 2, 2, 1, 128,
+                                        16, None, 0, 1, 2, None), 1),                  # null pointers
+    ("l2k_linear_rope_kvcache_decode", (0, 16, 64, 16, 512, 64, 16, 16, 16, 16, 16, 2, 2, 1, 128,
+                                        16, None, 0, 7, 2, None), 1),                  # pairing
+    ("l2k_linear_pad_rope_kvcache_prefill", (0, 16, 64, 16, 512, 64, 16, 16, 16, 16, 16, 16, 5, 2, 2, 1, 128,
+                                             0, 16, None, 0, 1, 2, None), 1),          # q_cache_len 0
 ])
 def test_bad_arguments_are_rejected(call, args, status):
     with pytest.raises(capi.L2KError) as e:

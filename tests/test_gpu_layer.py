@@ -125,3 +125,47 @@ def test_two_prefill_layers_against_oracle(dtype, tol):
         xr, pend = ref["x"], ref["down"]
     assert _row_rel_err(host(x), xr) <= tol
     assert _row_rel_err(host(pending), pend) <= tol
+
+
+@pytest.mark.parametrize("pairing", [0, 1])
+def test_fused_epilogues_bit_identical_to_separate_launches(pairing):
+    """A bf16 layer whose QKV projection carries the RoPE + K/V append and
+    whose gate/up projection carries the SwiGLU (7 decode launches, 9
+    prefill) against the same layer with the separate launches (9 and 11):
+    a decode step of 12 sequences, then a prefill pass of 104 tokens, every
+    output and both caches bit for bit."""
+    b, d, heads, kvh, f, s, qc = 12, 512, 4, 2, 1024, 256, 64
+    dev = torch.device("cuda")
+    runs = []
+    for fuse in (False, True):
+        L = DecoderLayer(d, heads, kvh, f, s, b, dtype=torch.bfloat16, seed=3, pairing=pairing,
+                         fuse_epilogues=fuse)
+        assert L.launches_per_step() == (7 if fuse else 9)
+        g = torch.Generator(device=dev)
+        g.manual_seed(4)
+        x = torch.randn(b, d, generator=g, device=dev).to(torch.bfloat16)
+        pending = torch.randn(b, d, generator=g, device=dev).to(torch.bfloat16)
+        lens = torch.randint(1, s, (b,), generator=torch.Generator().manual_seed(5))
+        kv_lens = lens.to(torch.uint32).cuda()
+        max_kv = torch.tensor([int(lens.max())], dtype=torch.uint32, device=dev)
+        is_done = torch.zeros(b, dtype=torch.uint8, device=dev)
+        is_done[2] = 1
+        down = L.decode(x, pending, kv_lens, max_kv, is_done)
+        out = [host(x), host(down), host(L.qk), host(L.act)]
+
+        # prefill: two prompts (64 and 40 new tokens after 0 and 10 cached) of the first two sequences
+        q_lens = torch.tensor([64, 40] + [0] * (b - 2), dtype=torch.uint32, device=dev)
+        kv_p = torch.tensor([64, 50] + [0] * (b - 2), dtype=torch.uint32, device=dev)
+        t = 104
+        unpad = torch.zeros(b, qc, dtype=torch.uint32, device=dev)
+        offsets = torch.zeros(b, dtype=torch.uint32, device=dev)
+        ops.launch_build_padding_index_maps(t, q_lens, unpad, offsets)
+        xp = torch.randn(t, d, generator=g, device=dev).to(torch.bfloat16)
+        assert L.launches_per_prefill(t) == (9 if fuse else 11)
+        down_p = L.prefill(xp, None, q_lens, kv_p, 64, 64, unpad)
+        torch.cuda.synchronize()
+        out += [host(xp), host(down_p), host(L.k_cache), host(L.v_cache)]
+        runs.append(out)
+    names = ["x", "down", "scores", "swiglu", "prefill x", "prefill down", "K cache", "V cache"]
+    for name, a, c in zip(names, *runs):
+        assert bits_equal(a, c), name
