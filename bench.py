@@ -198,10 +198,11 @@ def run_ours(args, rank, world, local_rank):
         if world > 1:
             dist.barrier()
 
-    # Two graphs of the same step: `chain.graph` (timed per step) and a copy
-    # whose dominant kernel (the fused step, or the fused scores) is
-    # bracketed by external event-record nodes, replayed in a separate loop
-    # so that the event nodes do not add to the step time.
+    # The step as the timed loop runs it (`chain.replay`: the one-kernel fused
+    # step launched directly, the operator sequence as a CUDA graph), and a
+    # graph copy whose dominant kernel (the fused step, or the fused scores)
+    # is bracketed by external event-record nodes, replayed in a separate
+    # loop so that the event nodes do not add to the step time.
     kev = (torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
     kernel_graph = capture_with_kernel_events(chain, kev)
     chain.capture()
@@ -209,18 +210,18 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
 
-    def one_step(graph, i=None):
+    def one_step(run, i=None):
         chain.reset_lengths()
         flush()
         if i is not None:
             ev[i][0].record(stream)
-        graph.replay()
+        run()
         if i is not None:
             ev[i][1].record(stream)
 
     for _ in range(max(args.warmup, 3)):
-        one_step(chain.graph)
-        one_step(kernel_graph)
+        one_step(chain.replay)
+        one_step(kernel_graph.replay)
     torch.cuda.synchronize()
 
     clocks = ClockSampler(local_rank)
@@ -229,10 +230,10 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     clocks.start()
     for i in range(args.steps):
-        one_step(chain.graph, i)
+        one_step(chain.replay, i)
     torch.cuda.synchronize()
     for i in range(args.steps):
-        one_step(kernel_graph)
+        one_step(kernel_graph.replay)
         kev[1].synchronize()
         kernel_ms.append(kev[0].elapsed_time(kev[1]))
     torch.cuda.synchronize()
@@ -298,6 +299,8 @@ def run_ours(args, rank, world, local_rank):
                        "hidden": w.hidden, "kv_cache_len": w.kv_cache_len, "batch_per_gpu": w.batch,
                        "prefill_len": w.prefill_len, "attention_output": bool(args.attention),
                        "parallelism": f"sequence-batch shards x{world}",
+                       "launch": ("one kernel per step, launched directly" if chain.fused
+                                  else f"{chain.kernels_per_step()} kernels per step, one CUDA graph replay"),
                        "l2": (("flushed between timed steps (2 x L2 written" +
                                (")" if drain_buf is None else ", then 2 x L2 read to evict it)")) if flush_each else
                               f"not flushed: inputs larger than L2 ({chain_bytes / 1e9:.2f} GB per step, "

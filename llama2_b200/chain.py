@@ -20,7 +20,8 @@ on this path). A decode step runs as ONE launch (ops.decode_step, the fused
 decode-step kernel) whenever its shapes are supported, else as the operator
 sequence above. All buffers live on one device; ``step()`` only enqueues
 work on the current stream, and ``capture()`` records the step as a CUDA
-graph so a step costs one graph launch. ``step_e2e()`` is the host-facing
+graph so a step costs one graph launch; ``replay()`` launches the one-kernel
+step directly and replays the graph otherwise. ``step_e2e()`` is the host-facing
 form: copy this step's inputs from pinned host memory, run, copy the results
 back.
 """
@@ -125,6 +126,7 @@ class Chain:
             self.workspace = ops.decode_step_workspace(self.device)
             self.fused = ops.decode_step_supported(**self._step_tensors())
         self.graph = None
+        self._launch = None  # the one-kernel step, launched directly (no graph)
         self._pinned = None
 
     def _step_tensors(self) -> dict:
@@ -223,6 +225,17 @@ class Chain:
         return g
 
     def replay(self):
+        """Enqueue one step: the one-kernel fused step is launched directly
+        (a CUDA graph adds its launch cost and saves nothing for one kernel);
+        the operator sequence replays its graph."""
+        if self.fused:
+            if self._launch is None:
+                w = self.w
+                attn = (self.attn_out.view(w.batch, w.heads, 1, w.head_dim) if self.attention_output else None)
+                self._launch = ops.decode_step_launcher(**self._step_tensors(), workspace=self.workspace,
+                                                        attn_out=attn)
+            self._launch()
+            return
         if self.graph is None:
             self.capture()
         self.graph.replay()
@@ -249,8 +262,8 @@ class Chain:
         return hin.buf.numel(), small + rows * self._m_written * qk.element_size()
 
     def step_e2e(self):
-        """One copy of the step's inputs to the device, the step (graph
-        replay), then its results back to pinned host memory: one copy of the
+        """One copy of the step's inputs to the device, the step (replay()),
+        then its results back to pinned host memory: one copy of the
         lengths maxima, normed rows and SwiGLU output, and one 2-D copy of the
         written part (keys [0, M)) of every score row."""
         from cuda.bindings import runtime as cudart

@@ -16,8 +16,8 @@
 // BN = 128). One thread issues the loads, refilling a stage as soon as the
 // MMAs that read it complete; another issues four 128 x BN x 16 MMAs per
 // block. The tensor maps bound rows at M, columns at N and k at K, so partial
-// tiles read zeros. The four warps then read their 32 TMEM lanes (rows) and
-// store the rows' BN columns. Products of one row tile (M <= 128: decode
+// tiles read zeros. Eight warps then read the accumulator, two per TMEM lane
+// quadrant (32 rows), each taking half of the rows' 32-column chunks. Products of one row tile (M <= 128: decode
 // batches, bound by reading B) split K over a thread-block cluster of up to
 // 8 CTAs that reduce their fp32 rows into rank 0 over distributed shared
 // memory.
@@ -63,7 +63,8 @@ namespace
 {
 
 constexpr int BM = 128, BK = 64;
-constexpr int kThreads = 128;
+constexpr int kEpiParts = 2;             // warps per TMEM lane quadrant in the epilogue
+constexpr int kThreads = 128 * kEpiParts;
 constexpr uint32_t kABox = BM * 128; // 128 rows x 64 k
 
 // Tile configuration: BN columns of C per CTA, STAGES-deep ring.
@@ -272,16 +273,18 @@ __device__ __forceinline__ void acc32(uint32_t taddr, int c0, uint32_t (&r)[32],
 // The epilogue of one tile for this thread's row: BN accumulator columns at
 // taddr (this warp's lane quadrant included); col0 = the tile's first column
 // of op(B) (EPI_SWIGLU: of the gate half, also the first output column).
+// The row's 32-column chunks are dealt to nparts warps of the same lane
+// quadrant: this warp takes chunks part, part + nparts, ...
 template <typename T, int BN, bool SPLIT, int EPI>
 __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t taddr, int64_t row, bool store,
                                               bool wide, int64_t col0, const float *red, int64_t red_stride,
-                                              int split, const RopeTok &tok)
+                                              int split, const RopeTok &tok, int part, int nparts)
 {
     if constexpr (EPI == EPI_STORE)
     {
         T *out = static_cast<T *>(a.c) + row * a.ldc;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32)
+        for (int c0 = 32 * part; c0 < BN; c0 += 32 * nparts)
         {
             uint32_t r[32];
             acc32<SPLIT>(taddr, c0, r, store, red, red_stride, split);
@@ -299,7 +302,7 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
         // accumulator columns [0, BN/2): gate; [BN/2, BN): up
         T *out = static_cast<T *>(a.c) + row * a.ldc;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN / 2; c0 += 32)
+        for (int c0 = 32 * part; c0 < BN / 2; c0 += 32 * nparts)
         {
             uint32_t g[32], u[32];
             acc32<SPLIT>(taddr, c0, g, store, red, red_stride, split);
@@ -315,7 +318,9 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
     }
     else
     {
-        // whole heads: accumulator columns [j hd, (j + 1) hd) hold head col0 / hd + j
+        // whole heads: accumulator columns [j hd, (j + 1) hd) hold head col0 / hd + j;
+        // item counts the chunks (or chunk pairs) of the tile in order
+        int item = 0;
         const RopeEpi &R = a.rope;
         const int hd = (int)R.hd, half = hd / 2;
         const int64_t total_heads = R.hq + 2 * R.hkv;
@@ -360,6 +365,8 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
 #pragma unroll 1
                 for (int c0 = 0; c0 < hd; c0 += 32)
                 {
+                    if (item++ % nparts != part)
+                        continue;
                     uint32_t r[32];
                     acc32<SPLIT>(taddr, hc + c0, r, store, red, red_stride, split);
                     if (!dst)
@@ -377,6 +384,8 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
 #pragma unroll 1
                 for (int c0 = 0; c0 < hd; c0 += 32)
                 {
+                    if (item++ % nparts != part)
+                        continue;
                     uint32_t r[32];
                     acc32<SPLIT>(taddr, hc + c0, r, store, red, red_stride, split);
                     if (!dst)
@@ -404,6 +413,8 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
 #pragma unroll 1
                 for (int c0 = 0; c0 < half; c0 += 32)
                 {
+                    if (item++ % nparts != part)
+                        continue;
                     uint32_t r0[32], r1[32];
                     acc32<SPLIT>(taddr, hc + c0, r0, store, red, red_stride, split);
                     acc32<SPLIT>(taddr, hc + half + c0, r1, store, red, red_stride, split);
@@ -563,11 +574,13 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
     }
     __syncwarp();
 
-    // -------- epilogue: warp w holds rows row0 + 32 w + lane --------
-    const int64_t row = row0 + 32 * warp + lane;
+    // -------- epilogue: warps w and w + 4 hold rows row0 + 32 w + lane (TMEM
+    // lane quadrant w), each half of the row's column chunks --------
+    const int quad = warp & 3, part = warp >> 2;
+    const int64_t row = row0 + 32 * quad + lane;
     const bool store = row < a.m;
     const bool wide = a.wide != 0;
-    const int lrow = 32 * warp + lane;          // row within the tile
+    const int lrow = 32 * quad + lane;          // row within the tile
     float *red = reinterpret_cast<float *>(smem); // SPLIT, rank 0: [split - 1][m][BN] peer rows (in the idle ring)
     const int m_tile = (int)min((int64_t)BM, a.m - row0);
     // EPI_ROPE: this row's token, read before the MMAs are waited for
@@ -591,10 +604,10 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
             if (rank != 0)
             {
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 32)
+                for (int c0 = 32 * part; c0 < BN; c0 += 32 * kEpiParts)
                 {
                     uint32_t r[32];
-                    tmem_ld32_async(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, r);
+                    tmem_ld32_async(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)c0, r);
                     tmem_wait_ld();
                     if (lrow < m_tile && !*abort_flag)
                     {
@@ -616,10 +629,11 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
             }
         }
         if (!*abort_flag && (!SPLIT || rank == 0))
-            tile_epilogue<T, BN, SPLIT, EPI>(a, tmem + ((uint32_t)(32 * warp) << 16), row, store, wide, col0,
-                                             red + (int64_t)lrow * BN, (int64_t)m_tile * BN, split, tok);
+            tile_epilogue<T, BN, SPLIT, EPI>(a, tmem + ((uint32_t)(32 * quad) << 16), row, store, wide, col0,
+                                             red + (int64_t)lrow * BN, (int64_t)m_tile * BN, split, tok, part,
+                                             kEpiParts);
     }
-    else if (EPI == EPI_STORE && store)
+    else if (EPI == EPI_STORE && store && part == 0)
     {
         T *out = static_cast<T *>(a.c) + row * a.ldc;
         for (int64_t col = col0; col < min((int64_t)col0 + BN, a.n); ++col)
@@ -648,13 +662,13 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
 // one CTA per SM walks the 128 x 256 tiles blockIdx.x, blockIdx.x +
 // gridDim.x, ...; warp 0 streams A and B tiles through a 4-stage ring of
 // 48 KB across tile boundaries, warp 1 issues the MMAs of a tile into one of
-// two 256-column TMEM accumulators, and warps 2-5 (one per TMEM lane
+// two 256-column TMEM accumulators, and warps 2-9 (two per TMEM lane
 // quadrant) run the epilogue of the previous tile from the other
 // accumulator, so the epilogue (a store, SwiGLU or RoPE) overlaps the next
 // tile's main loop. Accumulator hand-over: acc_full[b] (the tile's MMAs
-// completed, tcgen05.commit) and acc_empty[b] (the four epilogue warps have
-// read it).
-constexpr int kPThreads = 192;
+// completed, tcgen05.commit) and acc_empty[b] (the eight epilogue warps
+// have read it).
+constexpr int kPThreads = 64 + 128 * kEpiParts; // producer warp, MMA warp, epilogue warps
 constexpr int kPStages = 4;
 constexpr int kPBN = 256;
 constexpr uint32_t kPStageBytes = kABox + kPBN * 128;
@@ -697,7 +711,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         for (int b = 0; b < 2; ++b)
         {
             mbar_init(bar_acc_full + 8 * b, 1);
-            mbar_init(bar_acc_empty + 8 * b, 4);
+            mbar_init(bar_acc_empty + 8 * b, 4 * kEpiParts);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -805,8 +819,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
     else
     {
-        // epilogue warps 2..5: TMEM lane quadrant warp % 4 holds rows 32 (warp % 4) + lane of a tile
-        const int quad = warp & 3;
+        // epilogue warps 2..: TMEM lane quadrant warp % 4 holds rows 32 (warp % 4) + lane of a tile;
+        // the kEpiParts warps of a quadrant share its column chunks
+        const int quad = warp & 3, part = (warp - 2) >> 2;
         const bool wide = a.wide != 0;
         int64_t lt = 0;
         for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++lt)
@@ -826,7 +841,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
             tc_fence_after();
             __syncwarp();
             tile_epilogue<T, BN, false, EPI>(a, tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * quad) << 16), row,
-                                             store, wide, ocol0, nullptr, 0, 1, tok);
+                                             store, wide, ocol0, nullptr, 0, 1, tok, part, kEpiParts);
             tc_fence_before();
             __syncwarp();
             if (lane == 0)

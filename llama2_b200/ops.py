@@ -525,6 +525,35 @@ def decode_step_attention(*, q_lens, kv_lens, max_lens, input_ids, embed_table, 
     capi.call("l2k_decode_step_attention", ctypes.byref(args), attn_out.data_ptr(), workspace.data_ptr(), _stream())
 
 
+def decode_step_launcher(*, workspace, attn_out=None, **kw):
+    """decode_step (or, with attn_out, decode_step_attention) with its
+    arguments checked and packed once: returns a function that enqueues the
+    step on the current stream. For a caller that repeats the step over the
+    same tensors: the step is one kernel, so a direct launch costs less than
+    replaying it from a CUDA graph."""
+    kw.setdefault("use_table", True)
+    args = _decode_step_args(**kw)
+    _dev(workspace)
+    ws = workspace.data_ptr()
+    lib = capi.lib()
+    if attn_out is None:
+        name, fn, extra = "l2k_decode_step", lib.l2k_decode_step, ()
+    else:
+        _dev(attn_out)
+        _same(kw["qk"], attn_out, "decode_step_attention")
+        _require(attn_out.numel() == kw["q"].numel(), "attn_out must hold (batch, Hq, 1, head_dim)")
+        name, fn, extra = "l2k_decode_step_attention", lib.l2k_decode_step_attention, (attn_out.data_ptr(),)
+    ref = ctypes.byref(args)
+
+    def launch():
+        status = fn(ref, *extra, ws, _stream())
+        if status != 0:
+            raise capi.L2KError(name, status, lib.l2k_last_error_message().decode())
+
+    launch.args = args  # keeps the packed arguments alive with the launcher
+    return launch
+
+
 def decode_step_no_alloc(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv,
                          is_done, q, k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table=True):
     """decode_step with the library's own static scratch as workspace
