@@ -138,7 +138,7 @@ __device__ __forceinline__ void swiglu_range(const StepArgs &a, int64_t n)
         Vec16<T> o;
 #pragma unroll
         for (int k = 0; k < N; ++k)
-            o.v[k] = from_f<T>(silu_mul(to_f(gv.v[k]), to_f(uv.v[k])));
+            o.v[k] = from_f<T>(silu_mul<T>(to_f(gv.v[k]), to_f(uv.v[k])));
         stg(out + t * a.hidden + c * N, as_u4(o));
     }
 }

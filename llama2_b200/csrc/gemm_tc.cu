@@ -312,7 +312,7 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
             float o[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-                o[j] = silu_mul(round_t<T>(g[j]), round_t<T>(u[j]));
+                o[j] = silu_mul<T>(round_t<T>(g[j]), round_t<T>(u[j]));
             store_run<T>(out, col0 + c0, a.n, wide, o);
         }
     }

@@ -1,6 +1,6 @@
 """Timings of single operators and of the decoder layer on one GPU.
 
-    python -m llama2_b200.microbench {gemm,attention,paged,pv,unpad,rope,layer} [--iters N]
+    python -m llama2_b200.microbench {gemm,attention,paged,pv,swiglu,unpad,rope,layer} [--iters N]
 
 Each prints one line per shape. Kernels are timed with CUDA events on the
 current stream; ``gemm`` times back-to-back launches (compute-bound, L2
@@ -136,6 +136,16 @@ def bench_pv(iters):
           f"{2 * b * h * qc * s * hd / ms / 1e9:.1f} TF/s")
 
 
+def bench_swiglu(iters):
+    for (t, dt) in ((16384, torch.bfloat16), (16384, torch.float32), (64, torch.bfloat16)):
+        f = 11008
+        inp = torch.randn(t, 2 * f, device="cuda").to(dt)
+        out = torch.empty(t, f, device="cuda", dtype=dt)
+        ms = time_ms(lambda: ops.launch_swiglu(inp, out), iters)
+        nbytes = (inp.numel() + out.numel()) * inp.element_size()
+        print(f"swiglu {dt} {t} x {f}: {ms * 1e3:.1f} us {nbytes / ms / 1e6:.1f} GB/s")
+
+
 def bench_unpad(iters):
     b, h, qc, hd = 8, 32, 2048, 128
     qkv = torch.randn(b, h, qc, hd, device="cuda", dtype=torch.bfloat16)
@@ -201,7 +211,7 @@ def bench_layer(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "paged", "pv", "unpad", "rope", "layer"])
+    ap.add_argument("what", choices=["gemm", "attention", "paged", "pv", "swiglu", "unpad", "rope", "layer"])
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
     torch.manual_seed(0)
