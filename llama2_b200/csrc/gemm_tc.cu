@@ -3,24 +3,30 @@
 //   C[m, n] = sum_k A[m, k] * B'[k, n],  B' = B (K x N) or B^T (B stored N x K),
 // fp32 accumulation in tensor memory, one rounding to bf16/f16 at the end.
 //
-// One CTA computes a 128 x BN tile of C (BN = 256, or 128 for products of at
-// most 128 rows), walking K in blocks of 64. Per block TMA brings (128-byte
-// swizzle)
+// A CTA computes 128 x BN tiles of C, walking K in blocks of 64. Per block
+// TMA brings (128-byte swizzle)
 //   * the A tile, 128 rows x 64 k: the K-major A operand;
 //   * the B tile: with trans_B (B stored N x K) BN rows x 64 k, the K-major
 //     B operand; without it (B stored K x N, e.g. a weight [in, out]) 64 k
 //     rows x BN columns as 64-column boxes, the MN-major B operand (SBO 1024
-//     bytes between 8-row k groups, LBO 8 KB between the 64-column chunks);
-// through a ring (2 stages of 48 KB at BN = 256, two CTAs per SM so one
-// CTA's epilogue overlaps the other's main loop; 4 stages of 32 KB at
-// BN = 128). One thread issues the loads, refilling a stage as soon as the
+//     bytes between 8-row k groups, LBO 8 KB between the 64-column chunks).
+// One thread issues the loads into a ring, refilling a stage as soon as the
 // MMAs that read it complete; another issues four 128 x BN x 16 MMAs per
-// block. The tensor maps bound rows at M, columns at N and k at K, so partial
-// tiles read zeros. Eight warps then read the accumulator, two per TMEM lane
-// quadrant (32 rows), each taking half of the rows' 32-column chunks. Products of one row tile (M <= 128: decode
-// batches, bound by reading B) split K over a thread-block cluster of up to
-// 8 CTAs that reduce their fp32 rows into rank 0 over distributed shared
-// memory.
+// block into TMEM. The tensor maps bound rows at M, columns at N and k at K,
+// so partial tiles read zeros. Two warps per TMEM lane quadrant (32 rows)
+// read the accumulator, each taking half of the rows' 32-column chunks.
+// Three shapes:
+//   * more than 128 rows (prefill): the persistent kernel below, one CTA per
+//     SM over 128 x 256 tiles, a 4-stage ring of 48 KB, two TMEM
+//     accumulators so the epilogue warps drain one tile while the next one's
+//     MMAs run;
+//   * one row tile (M <= 128: decode batches, bound by reading B) with at
+//     most one 128-column tile per SM: 128 x 128 tiles with K split over a
+//     thread-block cluster of up to 8 CTAs that reduce their fp32 rows into
+//     rank 0 over distributed shared memory (3 stages of 32 KB, two CTAs per
+//     SM), or a 4-stage ring without the split;
+//   * one row tile with more 128-column tiles than SMs: 128 x 256 tiles in a
+//     4-stage ring of 48 KB, one CTA per SM, one wave.
 // Every mbarrier wait is bounded; on expiry the kernel records an error code
 // (l2k_device_error) and leaves after its copies and MMAs have drained.
 //
