@@ -19,10 +19,11 @@ include/kernel/fused_add_residual_rmsnorm.h:6-19):
 The lengths are updated once per model step (launch_update_q_kv_lens) before
 the first layer; each layer reads the updated kv_lens and the device max.
 Weights are [in, out] row-major (the MN-major B operand of the tensor-core
-GEMM). Nine launches per layer; ``capture_decode`` records a layer step as a
-CUDA graph. ``prefill`` runs the same layer over the new tokens of a batch of
-prompts (eleven launches: the scores, P.V and the unpad replace the fused
-decode attention).
+GEMM). Nine launches per layer as listed (seven with the fused epilogues
+below); ``capture_decode`` records a layer step as a CUDA graph. ``prefill``
+runs the same layer over the new tokens of a batch of prompts (eleven
+launches, nine fused: the scores, P.V and the unpad replace the fused decode
+attention).
 
 With 16-bit weights and more than 8 rows (where launch_linear runs on the
 tensor cores) the QKV projection takes the RoPE + K/V append into its
