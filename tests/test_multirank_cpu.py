@@ -65,3 +65,25 @@ def test_job_throughput_counts_every_rank():
     # 4 ranks x 64 tokens x 10 steps over a slowest-rank time of 2 ms
     assert bench.job_tokens_per_s(64, 4, 10, 2.0) == 64 * 4 * 10 / 2e-3
     assert bench.max_over_ranks([3.0, 1.0], 1, "cpu") == [3.0, 1.0]
+
+
+def test_reference_arm_json_line():
+    """`bench.py --impl reference` (the reference's CPU path on host cores)
+    prints one JSON line with the keys the bench contract names."""
+    import json
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", "tiny", "--steps", "1",
+                          "--warmup", "1"], cwd=root, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    res = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in res, key
+    assert res["impl"] == "reference" and res["value"] > 0 and res["config"]["workload"] == "tiny"
+    assert {"value", "unit", "cores", "kind", "sample"} <= set(res["cpu_baseline"])
+    assert res["e2e"]["h2d_bytes_per_step"] == 0 and res["e2e"]["d2h_bytes_per_step"] == 0
