@@ -87,3 +87,22 @@ def test_reference_arm_json_line():
     assert res["impl"] == "reference" and res["value"] > 0 and res["config"]["workload"] == "tiny"
     assert {"value", "unit", "cores", "kind", "sample"} <= set(res["cpu_baseline"])
     assert res["e2e"]["h2d_bytes_per_step"] == 0 and res["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_decode_algorithmic_bytes_by_operator():
+    """The bytes behind every decode roofline figure, recounted operator by
+    operator (each tensor read or written once) for the 7B batch-64 bf16 step
+    at seeded lengths: the same total as workloads.algorithmic_bytes."""
+    from llama2_b200.workloads import algorithmic_bytes
+
+    w = WORKLOADS["7b-b64-bf16"]
+    s, d, f, h, b = 2, w.dim, w.hidden, w.heads, w.batch
+    kv = np.random.default_rng(3).integers(1, w.kv_cache_len, b) + 1
+    embedding = b * d * s + b * d * s                  # gathered rows read, x written
+    rmsnorm = b * d * s + b * d * s + d * s            # x read, normed written, weight read
+    rope = b * 3 * d * s + b * d * s + 2 * b * d * s   # qkv read; q, K row, V row written
+    scores = b * d * s + int(kv.sum()) * d * s + b * h * int(kv.max()) * s  # q, K rows 0..pos, score rows
+    swiglu = b * 2 * f * s + b * f * s                 # gate/up read, output written
+    assert algorithmic_bytes(w, kv) == embedding + rmsnorm + rope + scores + swiglu
+    pv = int(kv.sum()) * d * s + b * d * s             # V rows 0..pos read, attention output written
+    assert algorithmic_bytes(w, kv, attention_output=True) == embedding + rmsnorm + rope + scores + swiglu + pv
