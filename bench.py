@@ -4,12 +4,25 @@
 
 A step is one pass of the chain (update lens -> embedding -> RMSNorm -> RoPE +
 KV append -> fused scores -> SwiGLU) over one batch of synthetic input
-(llama2_b200.workloads). The default workload is 7b-b1: Llama-2-7B dims,
-batch 1 decode, fp32, KV cache 4096 — the first 7B-dims configuration of the
-reference path's benchmark set. Under torchrun each rank runs its own batch
-on its own GPU (sharding by sequence batch; no collective on the data path),
-so scaling is weak; time is the max over ranks of the summed per-step device
-time (CUDA events), and value = tokens of all ranks / that time.
+(llama2_b200.workloads). The default workload is 7b-b64: Llama-2-7B dims,
+batch 64 decode, fp32 (the reference's precision), KV cache [64, 32, 4096,
+128] — the largest single-GPU 7B-dims decode configuration, whose 2.2 GB
+step is where the HBM roofline fraction means something (a batch-1 step
+moves 9 MB, 1.4 us at the copy peak, under the launch latency).
+
+Under torchrun each rank runs on its own GPU with no collective on the data
+path; time is the max over ranks of the summed per-step device time (CUDA
+events), and value = tokens of all ranks / that time. Two ways to split:
+
+  default        weak scaling: every rank holds its own batch of the
+                 workload's size (its own activations and cache, the same
+                 multiset of sequence lengths in a rank-permuted order, so
+                 the ranks' work is equal);
+  --shard ORDER  strong scaling: one global seeded batch of the workload's
+                 size is split by sequence over the ranks (ORDER contiguous:
+                 rank r takes sequences [r*B/N, (r+1)*B/N); balanced: sorted
+                 by length and dealt in snake order, equal counts and nearly
+                 equal keys per rank). Per-rank step times are reported.
 
 Between timed steps the sequence lengths are restored and the L2 cache is
 flushed: a 2 x L2-sized buffer is written, then another one read, so that
@@ -40,7 +53,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from llama2_b200.workloads import WORKLOADS, algorithmic_bytes, host_cache_ok, host_inputs, with_batch  # noqa: E402
+from llama2_b200.workloads import (WORKLOADS, algorithmic_bytes, host_cache_ok, host_inputs,  # noqa: E402
+                                   shard_inputs, shard_rows, with_batch)
 
 FALLBACK_HBM_GBS = 6650.0
 
@@ -50,7 +64,10 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", default="7b-b1", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="7b-b64", choices=sorted(WORKLOADS))
+    ap.add_argument("--shard", default="off", choices=["off", "contiguous", "balanced"],
+                    help="split ONE global batch of the workload over the ranks (strong scaling) instead of "
+                         "giving every rank a batch of its own (weak scaling)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -145,24 +162,65 @@ class ClockSampler:
 # CPU baselines (oracle / reference helpers) — only the CPU legs touch oracle/
 # ---------------------------------------------------------------------------
 def cpu_chain_rate(w, inputs, seconds, impl, attention_output=False):
-    """tokens/s of the CPU chain on a bounded sample: whole steps until `seconds`."""
+    """tokens/s of the CPU chain on a bounded sample: chain steps over the
+    first sequences of the batch (CpuChain.sample_batch) until `seconds`."""
     from oracle import cpu_chain
     runner = cpu_chain.CpuChain(w, inputs, impl=impl, attention_output=attention_output)
-    steps, t0 = 0, time.perf_counter()
+    steps, tokens, t0 = 0, 0, time.perf_counter()
     while True:
-        runner.step()
+        tokens += runner.step()
         steps += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    return {"value": steps * w.tokens / el, "unit": "tokens/s", "cores": runner.threads, "kind": runner.kind,
-            "sample": f"{steps} full chain step(s) of {w.name} (batch {w.batch}) in {el:.1f} s on "
-                      f"{runner.threads} thread(s)"}
+    nseq = len(runner.sample_batch())
+    return {"value": tokens / el, "unit": "tokens/s", "cores": runner.threads, "kind": runner.kind,
+            "cpu_model": host_cpu()["model"],
+            "sample": f"{steps} chain step(s) over {nseq} of the {w.batch} sequence(s) of {w.name} "
+                      f"({tokens} tokens) in {el:.1f} s on {runner.threads} thread(s)"}
 
 
 # ---------------------------------------------------------------------------
 # Our arm
 # ---------------------------------------------------------------------------
+def bench_config(w_job, args, n_gpus):
+    """The workload as both arms describe it (the same dict in the line of
+    `--impl ours` and of `--impl reference`)."""
+    shard = args.shard != "off"
+    per_gpu = w_job.batch // n_gpus if shard else w_job.batch
+    flush = {"always": "flushed between timed GPU steps (2 x L2 written, then 2 x L2 read to evict it)",
+             "write": "flushed between timed GPU steps (2 x L2 written)",
+             "auto": "flushed between timed GPU steps unless a step moves more than 4 x L2 "
+                     "(then its inputs alone exceed L2)"}[args.l2_flush]
+    return {"workload": w_job.name, "dim": w_job.dim, "heads": w_job.heads, "head_dim": w_job.head_dim,
+            "hidden": w_job.hidden, "kv_cache_len": w_job.kv_cache_len, "dtype": w_job.dtype,
+            "global_batch": per_gpu * n_gpus, "batch_per_gpu": per_gpu, "prefill_len": w_job.prefill_len,
+            "attention_output": bool(args.attention),
+            "parallelism": (f"sequence-batch shards x{n_gpus}: one global batch split {args.shard} by sequence"
+                            if shard else f"sequence-batch shards x{n_gpus}: a batch of its own per GPU, same "
+                                          f"multiset of lengths on every rank"),
+            "positions": f"uniform in [{w_job.pos_lo}, {w_job.pos_hi}], seed 0" if w_job.decode
+                         else "fresh prefill",
+            "l2": flush}
+
+
+def rank_inputs(args, rank, world):
+    """(per-rank workload, per-rank host inputs, the job's workload)."""
+    w_job = WORKLOADS[args.workload]
+    if args.batch:
+        w_job = with_batch(w_job, args.batch)
+    if args.shard == "off":
+        return w_job, host_inputs(w_job, seed=0, rank=rank, kv_cache=host_cache_ok(w_job)), w_job
+    if not w_job.decode:
+        raise SystemExit("--shard splits the sequence batch of a decode workload")
+    glob = host_inputs(w_job, seed=0, kv_cache=host_cache_ok(w_job))
+    rows = shard_rows(glob["kv_lens"], world, rank, args.shard)
+    inputs = shard_inputs(w_job, glob, rows)
+    if "cache_seed" in inputs:
+        inputs["cache_seed"] = rank  # the rank's cache slice, drawn on its device
+    return with_batch(w_job, len(rows)), inputs, w_job
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -171,10 +229,7 @@ def run_ours(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    w = WORKLOADS[args.workload]
-    if args.batch:
-        w = with_batch(w, args.batch)
-    inputs = host_inputs(w, seed=0, rank=rank, kv_cache=host_cache_ok(w))
+    w, inputs, w_job = rank_inputs(args, rank, world)
     chain = Chain(w, inputs, device=dev, fused=not args.unfused, attention_output=args.attention)
 
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
@@ -243,7 +298,10 @@ def run_ours(args, rank, world, local_rank):
     total_ms = sum(step_ms)
 
     # End to end through the public API: H2D of the step's inputs from pinned
-    # memory, the chain, D2H of its results, every step.
+    # memory, the chain, D2H of its results, every step. Timed twice: by the
+    # host clock from the call to the results being on the host (the stream
+    # synchronized after each step, as a caller that reads the results does),
+    # and by CUDA events around the same work on the stream.
     chain.host_buffers(inputs)
     h2d, d2h = chain.e2e_bytes()
     ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -252,11 +310,16 @@ def run_ours(args, rank, world, local_rank):
         chain.step_e2e()
     torch.cuda.synchronize()
     barrier()
+    wall_s = 0.0
     for i in range(args.steps):
         flush()
+        stream.synchronize()
+        t0 = time.perf_counter()
         ev2[i][0].record(stream)
         chain.step_e2e()
         ev2[i][1].record(stream)
+        stream.synchronize()
+        wall_s += time.perf_counter() - t0
     torch.cuda.synchronize()
     barrier()
     e2e_ms = sum(a.elapsed_time(b) for a, b in ev2)
@@ -275,7 +338,9 @@ def run_ours(args, rank, world, local_rank):
         kernel_key = "score_rows_stream" if w.decode else "prefill_scores_tc"
         kernel_bytes = scores_bytes(w, kv_after)
 
-    total_ms, e2e_ms = max_over_ranks([total_ms, e2e_ms], world, dev)
+    per_rank_ms = gather_over_ranks(total_ms / args.steps, world, dev)
+    per_rank_clocks = gather_objects(clocks.summary(), world)
+    total_ms, e2e_ms, wall_ms = max_over_ranks([total_ms, e2e_ms, wall_s * 1e3], world, dev)
 
     result = None
     if rank == 0:
@@ -291,20 +356,14 @@ def run_ours(args, rank, world, local_rank):
             "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if args.shard != "off" else "weak",
             "vs_baseline": None,
             "dtype": {"f32": "fp32", "bf16": "bf16", "f16": "fp16"}[w.dtype],
             "data": "synthetic (seeded; N(0,1) activations and KV cache, N(0,0.02) embeddings)",
-            "config": {"workload": w.name, "dim": w.dim, "heads": w.heads, "head_dim": w.head_dim,
-                       "hidden": w.hidden, "kv_cache_len": w.kv_cache_len, "batch_per_gpu": w.batch,
-                       "prefill_len": w.prefill_len, "attention_output": bool(args.attention),
-                       "parallelism": f"sequence-batch shards x{world}",
-                       "launch": ("one kernel per step, launched directly" if chain.fused
-                                  else f"{chain.kernels_per_step()} kernels per step, one CUDA graph replay"),
-                       "l2": (("flushed between timed steps (2 x L2 written" +
-                               (")" if drain_buf is None else ", then 2 x L2 read to evict it)")) if flush_each else
-                              f"not flushed: inputs larger than L2 ({chain_bytes / 1e9:.2f} GB per step, "
-                              f"> 4 x L2)")},
+            "config": bench_config(w_job, args, world),
+            "launch": ("one kernel per step, launched directly" if chain.fused
+                       else f"{chain.kernels_per_step()} kernels per step, one CUDA graph replay"),
+            "l2_flushed": bool(flush_each),
             "chain_hbm": {"algorithmic_bytes_per_step": chain_bytes,
                           "achieved_gbs": chain_bytes / (total_ms / args.steps * 1e-3) / 1e9,
                           "frac_of_peak": chain_bytes / (total_ms / args.steps * 1e-3) / 1e9 / peak},
@@ -312,17 +371,46 @@ def run_ours(args, rank, world, local_rank):
                          "bound": "hbm", "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": achieved / peak if achieved else None,
                          "algorithmic_bytes_per_launch": kernel_bytes, "mean_launch_ms": kmean,
-                         "traffic": profiled_traffic(kernel_key, w.name)},
-            "e2e": {"value": job_tokens_per_s(w.tokens, world, args.steps, e2e_ms), "unit": "tokens/s",
+                         "traffic": profiled_traffic(kernel_key, w.name if args.shard == "off" else None)},
+            "e2e": {"value": job_tokens_per_s(w.tokens, world, args.steps, wall_ms), "unit": "tokens/s",
+                    "timing": "host clock from the call to the results on the host, per step",
+                    "event_value": job_tokens_per_s(w.tokens, world, args.steps, e2e_ms),
                     "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": chain.kernels_per_step() * args.steps,
             "clocks": clocks.summary(),
         }
+        if world > 1:
+            result["per_rank"] = {"ms_per_step": per_rank_ms,
+                                  "sequences": [w.batch] * world,
+                                  "sm_mhz": [c["sm_mhz"] for c in per_rank_clocks],
+                                  "reasons": sorted({r for c in per_rank_clocks for r in c["reasons"]})}
         if not args.no_cpu_baseline and world == 1:
             result["cpu_baseline"] = cpu_chain_rate(w, inputs, args.cpu_sample_seconds, impl="port",
                                                     attention_output=args.attention)
     return result
+
+
+def gather_over_ranks(value, world, device):
+    """Every rank's float, in rank order (every rank calls it)."""
+    if world == 1:
+        return [value]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
+def gather_objects(obj, world):
+    """Every rank's picklable object, in rank order (every rank calls it)."""
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
 
 
 def max_over_ranks(values, world, device):
@@ -394,37 +482,71 @@ def profiled_traffic(kernel_key, workload):
 # ---------------------------------------------------------------------------
 # Reference arm: the reference's CPU implementation on the host cores
 # ---------------------------------------------------------------------------
+def host_cpu():
+    """The host's CPU model (from /proc/cpuinfo) and the logical CPUs this
+    process may run on."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        usable = len(os.sched_getaffinity(0))
+    except AttributeError:
+        usable = os.cpu_count()
+    return {"model": model or "unknown", "logical_cpus": os.cpu_count(), "usable_cpus": usable}
+
+
 def run_reference(args):
     from oracle import cpu_chain
 
-    w = WORKLOADS[args.workload]
-    inputs = host_inputs(w, seed=0, kv_cache=host_cache_ok(w))
+    w_job = WORKLOADS[args.workload]
+    if args.batch:
+        w_job = with_batch(w_job, args.batch)
+    inputs = host_inputs(w_job, seed=0, kv_cache=host_cache_ok(w_job))
     impl = "ref" if cpu_chain.ref_available() else "port"
-    runner = cpu_chain.CpuChain(w, inputs, impl=impl, threads=os.cpu_count(), attention_output=args.attention)
+    cpu = host_cpu()
+    threads = cpu["usable_cpus"]
+    # A decode step samples up to 16 sequences: 16 x heads (sequence, head)
+    # score rows keep every host thread busy in the dominant part.
+    runner = cpu_chain.CpuChain(w_job, inputs, impl=impl, threads=threads, attention_output=args.attention,
+                                max_sequences=16)
     sample = runner.sample_batch()
     # Prefill: the scores of every 16th query row are computed and their time is
     # scaled by 16 (a full 2048-row step of the CPU helpers takes many seconds).
-    stride = 1 if w.decode else 16
+    stride = 1 if w_job.decode else 16
     for _ in range(max(args.warmup, 1)):
         runner.step(sample, row_stride=stride)
     el = 0.0
     for _ in range(args.steps):
         runner.step(sample, row_stride=stride)
         el += runner.last_times["other"] + runner.last_times["scores"] * stride
-    tokens = len(sample) * (w.prefill_len or 1) * args.steps
+    tokens = len(sample) * (w_job.prefill_len or 1) * args.steps
     value = tokens / el
+    rows = len(sample) * w_job.heads
     return {
         "impl": "reference",
         "metric": "layer-kernel tokens/s at Llama-2-7B dims",
         "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": {"f32": "fp32", "bf16": "bf16", "f16": "fp16"}[w.dtype],
-        "data": "synthetic (seeded)",
-        "config": {"workload": w.name, "batch_per_step_sample": len(sample), "attention_output": bool(args.attention)},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": runner.threads, "kind": runner.kind,
-                         "sample": f"{len(sample)} of {w.batch} sequence(s) per step, {args.steps} steps" +
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong" if args.shard != "off" else "weak", "vs_baseline": None,
+        "dtype": {"f32": "fp32", "bf16": "bf16", "f16": "fp16"}[w_job.dtype],
+        "data": "synthetic (seeded; N(0,1) activations and KV cache, N(0,0.02) embeddings)",
+        "config": bench_config(w_job, args, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": runner.kind,
+                         "cpu_model": cpu["model"], "logical_cpus": cpu["logical_cpus"],
+                         "sample": f"{len(sample)} of {w_job.batch} sequence(s) per step, {args.steps} steps; "
+                                   f"{rows} (sequence, head) RoPE and score rows per step spread over "
+                                   f"{threads} thread(s), embedding/RMSNorm/SwiGLU over "
+                                   f"{min(threads, len(sample) * (w_job.prefill_len or 1))} row block(s)" +
                                    (f"; scores of every {stride}th query row, their time x{stride}" if stride > 1
-                                    else "")},
+                                    else "") +
+                                   ("" if impl == "ref" else "; the reference helpers are not built here: the C "
+                                                             "restatement ran")},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

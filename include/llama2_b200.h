@@ -478,11 +478,19 @@ int l2k_decode_step_attention_no_alloc(const l2k_decode_step_args *args, void *a
  * the tensors it already has and owns no device allocator). The workspace is
  * a 256-byte scratch array inside this library, one per device; nothing is
  * allocated. (No counterpart in the reference, which has no fused step.)
+ *  - The stream must belong to the current device (a stream of another
+ *    device returns L2K_ERR_INVALID_ARGUMENT); the scratch used is that
+ *    device's.
  *  - The first call on a device looks the scratch up (cudaGetSymbolAddress,
- *    with that device current); make it before any stream capture.
- *  - The scratch is zero when the library loads and every completed call
- *    leaves it zero; a call that did not complete (a CUDA error) can leave it
- *    nonzero, and the library must then be reloaded.
+ *    with that device current); make it before any stream capture. A call
+ *    that finds a different driver context current than at the lookup (after
+ *    cudaDeviceReset, or with a non-primary context made current) looks it
+ *    up again in that context.
+ *  - The scratch is zero when its context loads the library's kernels, and
+ *    every call whose kernel runs to its end leaves it zero — also one whose
+ *    bounded waits expired (l2k_device_error != 0): every CTA still takes its
+ *    ticket. Only a call whose context is lost (a sticky CUDA error) can
+ *    leave it nonzero; the new context a reset creates starts from zero.
  *  - Calls on one device share the scratch: two steps that may run at the
  *    same time (different streams) race and give wrong lengths. Use
  *    l2k_decode_step with separate workspaces for that.

@@ -254,26 +254,40 @@ class Chain:
         self._pinned = (hin, hout)
         return hin, hout
 
+    def _one_copy(self) -> bool:
+        """Whether the results come back in ONE device-to-host copy (the small
+        outputs and every score row whole) rather than two (the small outputs,
+        then a 2-D copy of the written keys [0, M) of every row): one copy
+        when the written part is at least half of each row, where the unwritten
+        tail costs less than a second copy's latency."""
+        return 2 * self._m_written >= self.qk.shape[3]
+
     def e2e_bytes(self):
         hin, hout = self._pinned
         qk = self.qk
         small = hout.offsets["qk"]
         rows = qk.shape[0] * qk.shape[1] * qk.shape[2]
-        return hin.buf.numel(), small + rows * self._m_written * qk.element_size()
+        cols = qk.shape[3] if self._one_copy() else self._m_written
+        return hin.buf.numel(), small + rows * cols * qk.element_size()
 
     def step_e2e(self):
         """One copy of the step's inputs to the device, the step (replay()),
-        then its results back to pinned host memory: one copy of the
-        lengths maxima, normed rows and SwiGLU output, and one 2-D copy of the
-        written part (keys [0, M)) of every score row."""
+        then its results back to pinned host memory: either one copy of the
+        lengths maxima, normed rows, SwiGLU output and the whole score rows,
+        or one copy of the small results and one 2-D copy of the written part
+        (keys [0, M)) of every score row, whichever moves less (_one_copy)."""
         from cuda.bindings import runtime as cudart
 
         hin, hout = self._pinned
         self.inputs.buf.copy_(hin.buf, non_blocking=True)
         self.replay()
         small = hout.offsets["qk"]
-        hout.buf[:small].copy_(self.outputs.buf[:small], non_blocking=True)
         qk, hqk = self.qk, hout["qk"]
+        if self._one_copy():
+            n = small + qk.numel() * qk.element_size()
+            hout.buf[:n].copy_(self.outputs.buf[:n], non_blocking=True)
+            return
+        hout.buf[:small].copy_(self.outputs.buf[:small], non_blocking=True)
         es = qk.element_size()
         rows = qk.shape[0] * qk.shape[1] * qk.shape[2]
         if self._m_written and rows:

@@ -369,10 +369,14 @@ extern "C" int l2k_decode_step_attention(const l2k_decode_step_args *args, void 
 // l2k_decode_step_no_alloc: the same launch with its workspace in a
 // file-scope device array instead of caller memory. The array is 256 bytes
 // (the step needs l2k_decode_step_workspace_bytes() of them); each device
-// has its own copy, zero when the module loads, and every completed step
-// leaves it zero again. Its address is looked up once per device with
-// cudaGetSymbolAddress (the first call on a device, with that device
-// current) and cached; nothing is allocated.
+// has its own copy, zero when the module loads, and every step that runs to
+// its end (including one whose bounded waits expired) leaves it zero again.
+// Its address is looked up with cudaGetSymbolAddress on the first call on a
+// device, with that device current, and cached together with the device's
+// current driver context; a call that finds another context current (after
+// cudaDeviceReset, or under a driver context the caller made current) looks
+// it up again, so the cached address never outlives the context it belongs
+// to. Nothing is allocated.
 // ---------------------------------------------------------------------------
 namespace l2k
 {
@@ -382,40 +386,73 @@ static __device__ __align__(256) uint32_t g_step_scratch[kStepScratchBytes / 4];
 
 namespace
 {
+struct ScratchSlot
+{
+    void *ctx = nullptr;     // the driver context the address was looked up in
+    uint32_t *ptr = nullptr; // g_step_scratch's device address in that context
+};
 std::mutex g_scratch_mutex;
-uint32_t *g_scratch_ptr[kMaxScratchDevices] = {};
-} // namespace
-} // namespace l2k
+ScratchSlot g_scratch[kMaxScratchDevices];
 
-namespace l2k
+// cuCtxGetCurrent from the driver, found at run time (the library links the
+// CUDA runtime statically and does not link the driver library itself).
+using CtxGetCurrentFn = int (*)(void **);
+CtxGetCurrentFn ctx_get_current()
 {
-namespace
-{
-// The static scratch of the current device (looked up on its first use).
-int static_scratch(uint32_t **out)
+    static CtxGetCurrentFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<CtxGetCurrentFn>(p);
+    }();
+    return fn;
+}
+
+// The static scratch of the device `stream` belongs to, which must be the
+// current device (cudaGetSymbolAddress answers for the current context).
+int static_scratch(const char *who, cudaStream_t stream, uint32_t **out)
 {
     if (l2k_decode_step_workspace_bytes() > kStepScratchBytes)
-        return set_error(L2K_ERR_UNSUPPORTED_SHAPE,
-                         "l2k_decode_step_no_alloc: the step needs %lld bytes of scratch, the static scratch holds %d",
-                         (long long)l2k_decode_step_workspace_bytes(), kStepScratchBytes);
+        return set_error(L2K_ERR_UNSUPPORTED_SHAPE, "%s: the step needs %lld bytes of scratch, the static scratch "
+                         "holds %d", who, (long long)l2k_decode_step_workspace_bytes(), kStepScratchBytes);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess)
-        return set_error(L2K_ERR_CUDA, "l2k_decode_step_no_alloc: cudaGetDevice: %s", cudaGetErrorString(e));
+        return set_error(L2K_ERR_CUDA, "%s: cudaGetDevice: %s", who, cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxScratchDevices)
-        return set_error(L2K_ERR_UNSUPPORTED_SHAPE, "l2k_decode_step_no_alloc: device %d >= %d", dev,
-                         kMaxScratchDevices);
+        return set_error(L2K_ERR_UNSUPPORTED_SHAPE, "%s: device %d >= %d", who, dev, kMaxScratchDevices);
+    if (stream != nullptr && stream != cudaStreamLegacy && stream != cudaStreamPerThread)
+    {
+        int sdev = -1;
+        e = cudaStreamGetDevice(stream, &sdev);
+        if (e != cudaSuccess)
+            return set_error(L2K_ERR_CUDA, "%s: cudaStreamGetDevice: %s", who, cudaGetErrorString(e));
+        if (sdev != dev)
+            return set_error(L2K_ERR_INVALID_ARGUMENT, "%s: the stream belongs to device %d but device %d is "
+                             "current; make the stream's device current first", who, sdev, dev);
+    }
+    // The context the lookup is valid for: the current one. A null context
+    // means the runtime has not made one current yet; the lookup below does.
+    void *ctx = nullptr;
+    if (CtxGetCurrentFn get = ctx_get_current())
+        get(&ctx);
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_ptr[dev])
+    ScratchSlot &slot = g_scratch[dev];
+    if (!slot.ptr || !ctx || slot.ctx != ctx)
     {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_step_scratch);
         if (e != cudaSuccess)
-            return set_error(L2K_ERR_CUDA, "l2k_decode_step_no_alloc: cudaGetSymbolAddress: %s",
-                             cudaGetErrorString(e));
-        g_scratch_ptr[dev] = static_cast<uint32_t *>(p);
+            return set_error(L2K_ERR_CUDA, "%s: cudaGetSymbolAddress: %s", who, cudaGetErrorString(e));
+        if (!ctx)
+            if (CtxGetCurrentFn get = ctx_get_current())
+                get(&ctx); // the lookup made the primary context current
+        slot.ptr = static_cast<uint32_t *>(p);
+        slot.ctx = ctx;
     }
-    *out = g_scratch_ptr[dev];
+    *out = slot.ptr;
     return L2K_OK;
 }
 } // namespace
@@ -424,7 +461,7 @@ int static_scratch(uint32_t **out)
 extern "C" int l2k_decode_step_no_alloc(const l2k_decode_step_args *args, l2k_stream_t stream)
 {
     uint32_t *scratch = nullptr;
-    if (int st = l2k::static_scratch(&scratch))
+    if (int st = l2k::static_scratch("l2k_decode_step_no_alloc", (cudaStream_t)stream, &scratch))
         return st;
     return l2k::step_entry(args, nullptr, scratch, stream, true);
 }
@@ -434,7 +471,7 @@ extern "C" int l2k_decode_step_attention_no_alloc(const l2k_decode_step_args *ar
 {
     L2K_REQUIRE(attn_out != nullptr, "l2k_decode_step_attention_no_alloc: null attn_out");
     uint32_t *scratch = nullptr;
-    if (int st = l2k::static_scratch(&scratch))
+    if (int st = l2k::static_scratch("l2k_decode_step_attention_no_alloc", (cudaStream_t)stream, &scratch))
         return st;
     return l2k::step_entry(args, attn_out, scratch, stream, true);
 }

@@ -564,6 +564,20 @@ def decode_step_no_alloc(*, q_lens, kv_lens, max_lens, input_ids, embed_table, n
     capi.call("l2k_decode_step_no_alloc", ctypes.byref(args), _stream())
 
 
+def decode_step_attention_no_alloc(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed,
+                                   qkv, is_done, q, k_cache, v_cache, qk, gate_up, ffn_out, attn_out, pairing,
+                                   use_table=True):
+    """decode_step_attention on the library's static scratch
+    (l2k_decode_step_attention_no_alloc); steps on one device must not
+    overlap."""
+    args = _decode_step_args(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done,
+                             q, k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table)
+    _dev(attn_out)
+    _same(qk, attn_out, "decode_step_attention_no_alloc")
+    _require(attn_out.numel() == q.numel(), "attn_out must hold (batch, Hq, 1, head_dim)")
+    capi.call("l2k_decode_step_attention_no_alloc", ctypes.byref(args), attn_out.data_ptr(), _stream())
+
+
 def decode_step_supported(**kw) -> bool:
     """Whether decode_step takes these tensors (shape and alignment support)."""
     kw.pop("workspace", None)

@@ -71,6 +71,12 @@ def host_inputs(w: Workload, seed: int = 0, rank: int = 0, kv_cache: bool = True
     Decode: positions p ~ U[pos_lo, pos_hi]; kv_lens holds p (the length
     before this step's token), and the length update makes it p + 1.
     Prefill: a fresh prefill (kv_lens = 0 before the update, q_lens = prefill_len).
+
+    Every rank draws its own activations, ids and cache from the seed
+    sequence [seed, rank]. The positions of rank r > 0 are a rank-seeded
+    permutation of rank 0's draw (`rank_positions`), so the ranks of a
+    weak-scaling job hold different sequences with the same multiset of
+    lengths: equal work per rank, as with statistically identical shards.
     """
     rng = np.random.default_rng([seed, rank])
     d, h, hd, f, s = w.dim, w.heads, w.head_dim, w.hidden, w.kv_cache_len
@@ -86,6 +92,8 @@ def host_inputs(w: Workload, seed: int = 0, rank: int = 0, kv_cache: bool = True
     if w.decode:
         out["q_lens"] = np.ones(w.batch, np.uint32)
         out["kv_lens"] = rng.integers(w.pos_lo, w.pos_hi + 1, w.batch, dtype=np.uint32)
+        if rank:
+            out["kv_lens"] = rank_positions(w, seed, rank)
     else:
         out["q_lens"] = np.full(w.batch, w.prefill_len, np.uint32)
         out["kv_lens"] = np.zeros(w.batch, np.uint32)
@@ -94,6 +102,60 @@ def host_inputs(w: Workload, seed: int = 0, rank: int = 0, kv_cache: bool = True
         out["v_cache"] = rng.standard_normal((w.batch, h, s, hd), dtype=np.float32)
     else:
         out["cache_seed"] = seed * 1000003 + rank
+    return out
+
+
+def rank_positions(w: Workload, seed: int, rank: int) -> np.ndarray:
+    """Rank 0's seeded positions (the same draw host_inputs makes for rank 0,
+    replayed from its seed sequence), permuted by a generator seeded with
+    [seed, rank, 1]. Every rank of a weak-scaling job thus holds the same
+    multiset of sequence lengths in a different order."""
+    rng = np.random.default_rng([seed, 0])
+    d, f, t = w.dim, w.hidden, w.tokens
+    # replay rank 0's draws up to its positions (same order and sizes as host_inputs)
+    rng.standard_normal((w.vocab, d), dtype=np.float32)
+    rng.uniform(0.5, 1.5, d)
+    rng.integers(0, w.vocab, t, dtype=np.uint32)
+    rng.standard_normal((t, 3 * d), dtype=np.float32)
+    rng.standard_normal((t, 2 * f), dtype=np.float32)
+    base = rng.integers(w.pos_lo, w.pos_hi + 1, w.batch, dtype=np.uint32)
+    return base[np.random.default_rng([seed, rank, 1]).permutation(w.batch)]
+
+
+def shard_rows(positions, world: int, rank: int, order: str = "contiguous") -> np.ndarray:
+    """Sequence indices of one global batch that rank `rank` of `world` owns.
+
+    contiguous: the slice [rank*B/world, (rank+1)*B/world) — the rank's part
+    of the (batch, kv_head, kv_cache_len, head_dim) cache cut along batch.
+    balanced: sequences sorted by length (longest first) and dealt to the
+    ranks in snake order (0..N-1, N-1..0, ...): every rank gets B/world
+    sequences and nearly the same number of keys, so the slowest rank (which
+    sets the job's time) is not held up by a run of long sequences."""
+    b = len(positions)
+    if b % world:
+        raise ValueError(f"global batch {b} does not split evenly over {world} ranks")
+    if order == "contiguous":
+        per = b // world
+        return np.arange(rank * per, (rank + 1) * per)
+    if order != "balanced":
+        raise ValueError(f"unknown shard order {order!r}")
+    idx = np.argsort(-np.asarray(positions, np.int64), kind="stable")
+    lanes = np.concatenate([np.arange(world), np.arange(world)[::-1]])
+    owner = lanes[np.arange(b) % (2 * world)]
+    return np.sort(idx[owner == rank])
+
+
+def shard_inputs(w: Workload, inputs: dict, rows) -> dict:
+    """The per-step inputs of the sequences `rows` of a global batch (decode)."""
+    rows = np.asarray(rows, np.int64)
+    out = {k: v for k, v in inputs.items() if k in ("embed_table", "norm_weight")}
+    for k in ("ids", "qkv", "gate_up", "is_done", "q_lens", "kv_lens"):
+        out[k] = np.ascontiguousarray(inputs[k][rows])
+    for k in ("k_cache", "v_cache"):
+        if k in inputs:
+            out[k] = np.ascontiguousarray(inputs[k][rows])
+    if "cache_seed" in inputs:
+        out["cache_seed"] = inputs["cache_seed"]
     return out
 
 

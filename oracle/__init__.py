@@ -69,8 +69,15 @@ def ref_available() -> bool:
     return ref_lib() is not None
 
 
-def build_ref(ref_root: str = "/root/reference") -> bool:
+def reference_root() -> str:
+    """Where the reference sources are: $L2K_REFERENCE_ROOT when set, else a
+    checkout named "reference" beside this repository."""
+    return os.environ.get("L2K_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference")
+
+
+def build_ref(ref_root: str | None = None) -> bool:
     """Compile the reference helpers when the reference sources are present."""
+    ref_root = ref_root or reference_root()
     if not os.path.isdir(ref_root):
         return False
     subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF_ROOT={ref_root}"], check=True)
@@ -117,6 +124,16 @@ class port:
         port_lib().orc_rope_cos_sin(_u32(i), _u32(head_dim), _u32(pos), _u32(seq_len), ctypes.byref(c),
                                     ctypes.byref(s))
         return c.value, s.value
+
+    @staticmethod
+    def rotate_one_head(pairing, head, pos, seq_len):
+        """One head (head_dim floats) rotated at `pos` with the length `seq_len`
+        the angle's scale uses: the per-head step of rope_kvcache_decode."""
+        head = f32(head)
+        out = np.empty_like(head)
+        port_lib().orc_rotate_one_head(_int(pairing), _ptr(head), _i64(head.shape[0]), _u32(pos), _u32(seq_len),
+                                       _ptr(out))
+        return out
 
     @staticmethod
     def rope_kvcache_decode(pairing, inp, is_done, kv_lens, q, k, v):

@@ -29,8 +29,9 @@ def ref_available() -> bool:
 
 class CpuChain:
     def __init__(self, w, inputs: dict, impl: str = "port", threads: int = 1, seed: int = 0,
-                 attention_output: bool = False):
+                 attention_output: bool = False, max_sequences: int = 8):
         self.w = w
+        self.max_sequences = max(1, int(max_sequences))
         self.attention_output = attention_output
         self.impl = impl
         self.kind = "reference" if impl == "ref" else "port"
@@ -52,9 +53,10 @@ class CpuChain:
         self._sample = sample
 
     def sample_batch(self):
-        """Sequences processed per step: all of a decode batch up to 8, one prefill sequence."""
+        """Sequences processed per step: the first max_sequences of a decode
+        batch (8 by default), one prefill sequence."""
         w = self.w
-        return list(range(min(w.batch, 8))) if w.decode else [0]
+        return list(range(min(w.batch, self.max_sequences))) if w.decode else [0]
 
     def _map(self, fn, items):
         if self.pool is None:

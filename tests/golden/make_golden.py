@@ -9,7 +9,7 @@ reference's test sources in place (``make -C oracle ref``) and called through
 
 Run from the repository root, where the reference sources are present:
 
-    python tests/golden/make_golden.py [--ref-root /root/reference]
+    python tests/golden/make_golden.py [--ref-root DIR]   (default: $L2K_REFERENCE_ROOT, else ../reference)
 
 The fixtures are committed; nothing at test time needs the reference.
 """
@@ -471,7 +471,7 @@ def gen_attention_qkv(lib):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-root", default="/root/reference")
+    ap.add_argument("--ref-root", default=None, help="the reference sources (default: oracle.reference_root())")
     args = ap.parse_args()
     oracle.build_ref(args.ref_root)
     lib = oracle.ref_lib()

@@ -140,7 +140,9 @@ def test_end_to_end_step_reads_back_results(name, batch):
     ref = ochain.decode_step(w, inp)
     assert max_rel_err(host(hout["qk"])[..., :m], ref["qk"][..., :m]) <= REL[w.dtype]
     h2d, d2h = ch.e2e_bytes()
-    assert h2d == hin.buf.numel() and d2h < hout.buf.numel()
+    assert h2d == hin.buf.numel()
+    # one copy of everything when keys [0, M) are at least half of each row, else the written part only
+    assert (d2h == hout.buf.numel()) == (2 * m >= w.kv_cache_len) and d2h <= hout.buf.numel()
 
 
 # ---------------------------------------------------------------------------

@@ -1,12 +1,15 @@
 """The multi-rank host logic of bench.py on CPU: two gloo ranks (world 2).
 
-Each rank owns its own sequence-batch shard (seeded by rank, no exchange on
-the data path); the job's time is the maximum over ranks, and its throughput
-is every rank's tokens over that time."""
+Weak scaling: each rank owns a batch of its own (seeded by rank, no exchange
+on the data path) with the same multiset of sequence lengths. Strong scaling
+(--shard): one global batch split by sequence over the ranks. The job's time
+is the maximum over ranks, and its throughput is every rank's tokens over
+that time."""
 import os
 import socket
 
 import numpy as np
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -33,7 +36,14 @@ def _worker(rank, world, port, out):
         d = torch.tensor([digest], dtype=torch.float64)
         all_d = [torch.zeros(1, dtype=torch.float64) for _ in range(world)]
         dist.all_gather(all_d, d)
-        out.put((rank, got, [x.item() for x in all_d]))
+        per_rank = bench.gather_over_ranks(float(rank + 1), world, "cpu")
+        objs = bench.gather_objects({"rank": rank}, world)
+        # strong scaling: this rank's rows of one global batch, as bench.rank_inputs picks them
+        args = bench.argparse.Namespace(workload="tiny", batch=8, shard="balanced")
+        w_rank, inp_rank, w_job = bench.rank_inputs(args, rank, world)
+        rows = bench.shard_rows(host_inputs(w_job, seed=0, kv_cache=False)["kv_lens"], world, rank, "balanced")
+        out.put((rank, got, [x.item() for x in all_d], per_rank, objs, rows.tolist(), w_rank.batch,
+                 inp_rank["kv_lens"].tolist()))
     finally:
         dist.destroy_process_group()
 
@@ -49,9 +59,15 @@ def test_two_gloo_ranks():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, got, digests in res:
+    glob = host_inputs(with_batch(WORKLOADS["tiny"], 8), seed=0, kv_cache=False)["kv_lens"]
+    all_rows = []
+    for rank, got, digests, per_rank, objs, rows, batch, kv in res:
         assert got == [2.0, 10.0]
         assert digests[0] != digests[1]  # each rank has its own shard
+        assert per_rank == [1.0, 2.0] and objs == [{"rank": 0}, {"rank": 1}]
+        assert batch == 4 and kv == glob[rows].tolist()
+        all_rows += rows
+    assert sorted(all_rows) == list(range(8))  # every sequence of the global batch on exactly one rank
 
 
 def test_shards_are_deterministic_per_rank():
@@ -85,7 +101,9 @@ def test_reference_arm_json_line():
                 "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert key in res, key
     assert res["impl"] == "reference" and res["value"] > 0 and res["config"]["workload"] == "tiny"
-    assert {"value", "unit", "cores", "kind", "sample"} <= set(res["cpu_baseline"])
+    args = bench.argparse.Namespace(workload="tiny", batch=0, shard="off", attention=False, l2_flush="always")
+    assert res["config"] == bench.bench_config(WORKLOADS["tiny"], args, 1)
+    assert {"value", "unit", "cores", "kind", "sample", "cpu_model"} <= set(res["cpu_baseline"])
     assert res["e2e"]["h2d_bytes_per_step"] == 0 and res["e2e"]["d2h_bytes_per_step"] == 0
 
 
@@ -106,3 +124,42 @@ def test_decode_algorithmic_bytes_by_operator():
     assert algorithmic_bytes(w, kv) == embedding + rmsnorm + rope + scores + swiglu
     pv = int(kv.sum()) * d * s + b * d * s             # V rows 0..pos read, attention output written
     assert algorithmic_bytes(w, kv, attention_output=True) == embedding + rmsnorm + rope + scores + swiglu + pv
+
+
+def test_weak_scaling_ranks_hold_the_same_lengths():
+    """Every rank's positions are a permutation of rank 0's: equal work per
+    rank, different sequences."""
+    w = with_batch(WORKLOADS["tiny"], 16)
+    base = host_inputs(w, seed=0, rank=0, kv_cache=False)["kv_lens"]
+    for rank in (1, 2, 7):
+        kv = host_inputs(w, seed=0, rank=rank, kv_cache=False)["kv_lens"]
+        assert sorted(kv.tolist()) == sorted(base.tolist()) and not np.array_equal(kv, base)
+
+
+@pytest.mark.parametrize("order", ["contiguous", "balanced"])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_shard_rows_partition_the_global_batch(order, world):
+    from llama2_b200.workloads import shard_rows
+    w = WORKLOADS["13b-b256"]
+    kv = np.random.default_rng(5).integers(w.pos_lo, w.pos_hi + 1, w.batch, dtype=np.uint32)
+    parts = [shard_rows(kv, world, r, order) for r in range(world)]
+    assert all(len(p) == 256 // world for p in parts)
+    assert sorted(np.concatenate(parts).tolist()) == list(range(256))
+    if order == "contiguous":
+        assert all(np.array_equal(p, np.arange(r * len(p), (r + 1) * len(p))) for r, p in enumerate(parts))
+    else:
+        keys = [int(kv[p].astype(np.int64).sum()) for p in parts]
+        assert max(keys) <= 1.01 * (sum(keys) / world)  # snake dealing keeps the ranks' keys within 1 %
+    with pytest.raises(ValueError):
+        shard_rows(kv[:255], 2, 0, order)
+
+
+def test_both_arms_describe_the_same_config():
+    """The reference arm's config is the dict the GPU arm prints for the same
+    arguments (so the two lines compare)."""
+    args = bench.argparse.Namespace(workload="7b-b64", batch=0, shard="off", attention=False, l2_flush="always")
+    a = bench.bench_config(WORKLOADS["7b-b64"], args, 1)
+    assert a["workload"] == "7b-b64" and a["global_batch"] == 64 and a["batch_per_gpu"] == 64
+    args.shard = "contiguous"
+    b = bench.bench_config(WORKLOADS["13b-b256"], args, 8)
+    assert b["global_batch"] == 256 and b["batch_per_gpu"] == 32 and "split contiguous" in b["parallelism"]
