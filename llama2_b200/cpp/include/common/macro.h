@@ -28,3 +28,26 @@
             std::exit(EXIT_FAILURE);                                                                  \
         }                                                                                             \
     } while (0)
+
+// For callers that hold a cuBLAS handle (the reference's include/common/macro.h:42-50 offers the same check);
+// expands only where cublas_v2.h is included. The operators of this library do not call cuBLAS.
+#define CUBLAS_CHECK(call)                                                                            \
+    do                                                                                                \
+    {                                                                                                 \
+        cublasStatus_t st_ = (call);                                                                  \
+        if (st_ != CUBLAS_STATUS_SUCCESS)                                                             \
+        {                                                                                             \
+            std::fprintf(stderr, "cuBLAS error: %s at %s:%d\n", cublasGetStatusString(st_), __FILE__, __LINE__); \
+            std::exit(EXIT_FAILURE);                                                                  \
+        }                                                                                             \
+    } while (0)
+
+#define MALLOC_CHECK(ptr)                                                                             \
+    do                                                                                                \
+    {                                                                                                 \
+        if ((ptr) == nullptr)                                                                         \
+        {                                                                                             \
+            std::fprintf(stderr, "Host memory allocation failed at %s:%d\n", __FILE__, __LINE__);     \
+            std::exit(EXIT_FAILURE);                                                                  \
+        }                                                                                             \
+    } while (0)
