@@ -458,6 +458,47 @@ int l2k_decode_attention_paged(const void *q, const void *k_pages, const void *v
                                int64_t kv_head_num, int64_t head_dim, int dtype, l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Paged K/V caches (prefill), same pool layout and block table as above.
+ * No counterpart in the reference; each replaces the contiguous operator
+ * named beside it, whose reference counterpart it keeps:
+ *
+ * l2k_fused_pad_reshape_transpose_rope_kvcache_paged: the prefill RoPE +
+ *   append of l2k_fused_pad_reshape_transpose_rope_kvcache[_llama2]
+ *   (src/kernel/fused_pad_reshape_transpose_rope_kvcache*.cu:11-126; pairing
+ *   selects which) with K/V row pos = kv_len - q_len + t written to page
+ *   block_table[b][pos / page_rows], row pos % page_rows.
+ * l2k_prefill_attention_scores_paged: l2k_prefill_attention_scores over a
+ *   paged K cache; 16-bit data, head_dim 128 (page_rows 64: a 128-key tile of
+ *   the tensor-core kernel is two pages). qk is (B, Hq, q_cache_len,
+ *   max_pages * 64). Other shapes return L2K_ERR_UNSUPPORTED_SHAPE.
+ * l2k_attention_qkv_paged: l2k_attention_qkv over a paged V cache, same
+ *   shape coverage (one page is one 64-key block). kv_lens (device) are the
+ *   sequences' lengths: a block wholly past a sequence's length reads pool
+ *   page 0 (its probabilities are zero), so unset table entries past a
+ *   sequence's pages are never dereferenced. As with the contiguous operator,
+ *   rows after a sequence's length (here up to the end of its last page) are
+ *   read and multiplied by zero probabilities.
+ * ------------------------------------------------------------------------ */
+int l2k_fused_pad_reshape_transpose_rope_kvcache_paged(const void *input, const uint32_t *q_lens,
+                                                       const uint32_t *kv_lens, const uint32_t *unpad_to_pad_idx,
+                                                       void *q, void *k_pages, void *v_pages,
+                                                       const uint32_t *block_table, int64_t max_pages,
+                                                       int64_t num_pages, int64_t page_rows, int64_t num_tokens,
+                                                       int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                                       int64_t head_dim, int64_t q_cache_len, const float *rope_table,
+                                                       int64_t rope_table_positions, int pairing, int dtype,
+                                                       l2k_stream_t stream);
+int l2k_prefill_attention_scores_paged(const void *q, const void *k_pages, const uint32_t *block_table,
+                                       int64_t max_pages, int64_t num_pages, const uint32_t *q_lens,
+                                       const uint32_t *kv_lens, uint32_t max_q_len, uint32_t max_kv_len, void *qk,
+                                       int64_t batch, int64_t q_head_num, int64_t kv_head_num, int64_t q_cache_len,
+                                       int64_t head_dim, int dtype, l2k_stream_t stream);
+int l2k_attention_qkv_paged(const void *qk, const void *v_pages, const uint32_t *block_table, int64_t max_pages,
+                            int64_t num_pages, const uint32_t *kv_lens, void *qkv, int64_t batch, int64_t q_head_num,
+                            int64_t kv_head_num, int64_t q_cache_len, int64_t head_dim, int64_t m, int64_t n,
+                            int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * The fused decode step with the attention output: everything
  * l2k_decode_step computes, and in the same launch
  *   attn_out[b, h, 0, :] = sum_{j <= pos} qk[b, h, 0, j] * v_cache[b, h / (Hq/Hkv), j, :]

@@ -75,6 +75,11 @@ SIGNATURES = {
                                                     vp, i64, cint, cint, vp],
     "l2k_decode_attention_paged": [vp, vp, vp, vp, i64, i64, vp, vp, vp, vp, i64, i64, i64, i64, cint, vp],
     "l2k_prefill_attention_scores": [vp, vp, vp, vp, u32, u32, vp, i64, i64, i64, i64, i64, i64, cint, vp],
+    "l2k_fused_pad_reshape_transpose_rope_kvcache_paged": [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, i64,
+                                                           i64, i64, i64, i64, vp, i64, cint, cint, vp],
+    "l2k_prefill_attention_scores_paged": [vp, vp, vp, i64, i64, vp, vp, u32, u32, vp, i64, i64, i64, i64, i64, cint,
+                                           vp],
+    "l2k_attention_qkv_paged": [vp, vp, vp, i64, i64, vp, vp, i64, i64, i64, i64, i64, i64, i64, cint, vp],
     "l2k_decode_step_workspace_bytes": ([], i64),
     "l2k_decode_step_supported": [ctypes.POINTER(DecodeStepArgs)],
     "l2k_decode_step": [ctypes.POINTER(DecodeStepArgs), vp, vp],

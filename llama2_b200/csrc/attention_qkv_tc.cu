@@ -58,7 +58,8 @@ enum PvError
     ERR_PV_WAIT_LOAD = 0x301,
     ERR_PV_WAIT_MMA = 0x302,
     ERR_PV_WAIT_DONE = 0x303,
-    ERR_PV_SMEM_ALIGN = 0x304
+    ERR_PV_SMEM_ALIGN = 0x304,
+    ERR_PV_PAGE = 0x305 // a block-table entry past the page pool (page 0 was read instead)
 };
 
 struct PvArgs
@@ -68,6 +69,11 @@ struct PvArgs
     int64_t m;  // rows written per (seq, head)
     int n_kb;   // key blocks covering [0, n)
     int n_mt;   // row tiles per (seq, head)
+    // Paged V cache (null block_table: contiguous): V is (num_pages, Hkv, 64, 128);
+    // key block kb of sequence b is page block_table[b * max_pages + kb].
+    const uint32_t *block_table;
+    const uint32_t *kv_lens;
+    int64_t max_pages, num_pages;
 };
 
 // MN-major operand, 128-byte swizzle (version 1): LBO = 8 KB between the two
@@ -172,9 +178,26 @@ __global__ void __launch_bounds__(kThreads, 2)
     else if (n_kb > 0 && tid == 64)
     {
         // ---- V producer (warp 2, lane 0) ----
-        const int vz = (int)(b * a.Hkv + h / a.group);
+        const int64_t kvh = h / a.group;
+        const int vz = (int)(b * a.Hkv + kvh);
+        // Paged: a block wholly past the sequence's length (its table entry may
+        // be unset; its probabilities are zero) reads pool page 0 instead.
+        const int64_t kvl = a.block_table ? (int64_t)a.kv_lens[b] : 0;
         produce(kVStages, bar_vfull, bar_vfreed, kVStage, [&](int kb, int st, uint32_t bar) {
             const uint32_t dst = sbase + kOffV + st * kVStage;
+            if (a.block_table)
+            {
+                int64_t page = ((int64_t)kb * BK < kvl && kb < a.max_pages) ? a.block_table[b * a.max_pages + kb] : 0;
+                if (page >= a.num_pages)
+                {
+                    atomicCAS(&g_pv_error, 0, ERR_PV_PAGE);
+                    page = 0;
+                }
+                const int pz = (int)(page * a.Hkv + kvh);
+                tma_load_3d(dst, &tm_v, 0, 0, pz, bar);
+                tma_load_3d(dst + kVBox, &tm_v, BK, 0, pz, bar);
+                return;
+            }
             tma_load_3d(dst, &tm_v, 0, kb * BK, vz, bar);
             tma_load_3d(dst + kVBox, &tm_v, BK, kb * BK, vz, bar);
         });
@@ -267,16 +290,21 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 template <typename T>
 int launch_pv_tc(const void *qk, const void *v, void *qkv, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc,
-                 int64_t S, int64_t m, int64_t n, cudaStream_t stream)
+                 int64_t S, int64_t m, int64_t n, const uint32_t *block_table, const uint32_t *kv_lens,
+                 int64_t max_pages, int64_t num_pages, cudaStream_t stream)
 {
     const CUtensorMapDataType dt =
         std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUtensorMap mp, mv;
     if (!make_map(&mp, dt, qk, (uint64_t)n, (uint64_t)Qc, (uint64_t)(batch * Hq), (uint64_t)S * 2,
                   (uint64_t)(Qc * S * 2), BM, BK) ||
-        !make_map(&mv, dt, v, HD, (uint64_t)n, (uint64_t)(batch * Hkv), HD * 2, (uint64_t)(S * HD * 2), BK, BK))
+        !(block_table ? make_map(&mv, dt, v, HD, BK, (uint64_t)(num_pages * Hkv), HD * 2, (uint64_t)(BK * HD * 2), BK,
+                                 BK)
+                      : make_map(&mv, dt, v, HD, (uint64_t)n, (uint64_t)(batch * Hkv), HD * 2,
+                                 (uint64_t)(S * HD * 2), BK, BK)))
         return set_error(L2K_ERR_CUDA, "l2k_attention_qkv: tensor map encoding failed");
-    PvArgs a{qkv, Hq, Hq / Hkv, Hkv, Qc, m, (int)ceil_div(n, BK), (int)ceil_div(m, BM)};
+    PvArgs a{qkv,        Hq,      Hq / Hkv, Hkv,      Qc,       m, (int)ceil_div(n, BK), (int)ceil_div(m, BM),
+             block_table, kv_lens, max_pages, num_pages};
     auto kernel = attention_qkv_tc_kernel<T>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e == cudaSuccess) // two CTAs per SM need the whole shared-memory carveout
@@ -301,11 +329,14 @@ bool attention_qkv_tc_supported(int dtype, int64_t head_dim, int64_t S, int64_t 
 }
 
 int attention_qkv_tc(const void *qk, const void *v, void *qkv, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc,
-                     int64_t S, int64_t m, int64_t n, int dtype, cudaStream_t stream)
+                     int64_t S, int64_t m, int64_t n, int dtype, cudaStream_t stream, const uint32_t *block_table,
+                     const uint32_t *kv_lens, int64_t max_pages, int64_t num_pages)
 {
     if (dtype == L2K_BF16)
-        return launch_pv_tc<__nv_bfloat16>(qk, v, qkv, batch, Hq, Hkv, Qc, S, m, n, stream);
-    return launch_pv_tc<__half>(qk, v, qkv, batch, Hq, Hkv, Qc, S, m, n, stream);
+        return launch_pv_tc<__nv_bfloat16>(qk, v, qkv, batch, Hq, Hkv, Qc, S, m, n, block_table, kv_lens, max_pages,
+                                           num_pages, stream);
+    return launch_pv_tc<__half>(qk, v, qkv, batch, Hq, Hkv, Qc, S, m, n, block_table, kv_lens, max_pages, num_pages,
+                                stream);
 }
 
 int read_pv_error(bool clear)

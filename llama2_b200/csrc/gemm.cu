@@ -212,7 +212,9 @@ int gemm_tc(int trans_b, int64_t m, int64_t n, int64_t k, const void *a, int64_t
 bool attention_qkv_tc_supported(int dtype, int64_t head_dim, int64_t S, int64_t n, const void *qk, const void *v,
                                 const void *qkv, int64_t grid); // attention_qkv_tc.cu
 int attention_qkv_tc(const void *qk, const void *v, void *qkv, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc,
-                     int64_t S, int64_t m, int64_t n, int dtype, cudaStream_t stream);
+                     int64_t S, int64_t m, int64_t n, int dtype, cudaStream_t stream,
+                     const uint32_t *block_table = nullptr, const uint32_t *kv_lens = nullptr, int64_t max_pages = 0,
+                     int64_t num_pages = 0);
 
 } // namespace l2k
 
@@ -303,4 +305,32 @@ extern "C" int l2k_attention_qkv(const void *qk, const void *v, void *qkv, int64
     L2K_REQUIRE_SHAPE(ceil_div(m, BM) <= 65535, "l2k_attention_qkv: m too large");
     return attention_qkv_cuda_cores(qk, v, qkv, batch, q_head_num, kv_head_num, q_cache_len, kv_cache_len, head_dim,
                                     m, n, nullptr, dtype, stream);
+}
+
+// P.V over a paged V cache (16-bit, head_dim 128: one page is one 64-key
+// block of the tcgen05 kernel). qk is (batch, Hq, q_cache_len, max_pages * 64).
+extern "C" int l2k_attention_qkv_paged(const void *qk, const void *v_pages, const uint32_t *block_table,
+                                       int64_t max_pages, int64_t num_pages, const uint32_t *kv_lens, void *qkv,
+                                       int64_t batch, int64_t q_head_num, int64_t kv_head_num, int64_t q_cache_len,
+                                       int64_t head_dim, int64_t m, int64_t n, int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    const char *name = "l2k_attention_qkv_paged";
+    L2K_REQUIRE(dtype_ok(dtype), "%s: unsupported dtype %d", name, dtype);
+    L2K_REQUIRE(batch >= 0 && q_head_num >= 0 && kv_head_num >= 0 && head_dim >= 0 && m >= 0 && n >= 0 &&
+                    max_pages >= 0 && num_pages >= 0,
+                "%s: negative size", name);
+    const int64_t S = max_pages * 64;
+    L2K_REQUIRE(m <= q_cache_len && n <= S, "%s: m/n exceed the cache dims", name);
+    if (batch == 0 || q_head_num == 0 || m == 0 || head_dim == 0)
+        return L2K_OK;
+    L2K_REQUIRE(kv_head_num > 0 && q_head_num % kv_head_num == 0, "%s: q_head_num must be a multiple of kv_head_num",
+                name);
+    L2K_REQUIRE(qk && v_pages && qkv && block_table && kv_lens && num_pages > 0, "%s: null pointer or no pages", name);
+    L2K_REQUIRE_SHAPE(num_pages * kv_head_num < (int64_t(1) << 31), "%s: page pool too large", name);
+    L2K_REQUIRE_SHAPE(attention_qkv_tc_supported(dtype, head_dim, S, n, qk, v_pages, qkv,
+                                                 ceil_div(m, 128) * batch * q_head_num),
+                      "%s: the paged path takes 16-bit data with head_dim 128, 16-byte aligned, n >= 1", name);
+    return attention_qkv_tc(qk, v_pages, qkv, batch, q_head_num, kv_head_num, q_cache_len, S, m, n, dtype, stream,
+                            block_table, kv_lens, max_pages, num_pages);
 }

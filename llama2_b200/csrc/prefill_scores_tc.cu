@@ -80,8 +80,11 @@ enum DevError
     ERR_WAIT_K = 0x102,
     ERR_WAIT_MMA = 0x103,
     ERR_WAIT_TMEM = 0x104,
-    ERR_SMEM_ALIGN = 0x105
+    ERR_SMEM_ALIGN = 0x105,
+    ERR_PAGE = 0x106 // a block-table entry past the page pool (page 0 was read instead)
 };
+
+constexpr int kPageRows = 64; // rows of one page of a paged K cache: 16 KB of 128 x 16-bit rows
 
 struct TcArgs
 {
@@ -94,6 +97,10 @@ struct TcArgs
     int n_qt;      // query tiles per (seq, head)
     int n_kt;      // key tiles covering [0, M)
     float c;       // scale * log2(e)
+    // Paged K cache (null block_table: contiguous): K is (num_pages, Hkv, 64, 128);
+    // keys [64 j, 64 j + 64) of sequence b are page block_table[b * max_pages + j].
+    const uint32_t *block_table;
+    int64_t max_pages, num_pages;
 };
 
 // ---------------------------------------------------------------------------
@@ -207,10 +214,35 @@ __global__ void __launch_bounds__(kThreads, 2)
             const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
             const uint32_t idesc_full = instr_desc(fmt, BN), idesc_half = instr_desc(fmt, BN / 2);
             const int kz = (int)(b * a.Hkv + kvh);
+            // Paged: the tile's two 64-key pages. A page wholly past the
+            // sequence's length (its table entry may be unset) is replaced by
+            // the tile's first page: those keys are masked for every row.
+            auto page_z = [&](int kt, int half) -> int {
+                int64_t j = 2 * (int64_t)kt + half;
+                if (j * kPageRows >= kv_len || j >= a.max_pages)
+                    j = 2 * (int64_t)kt;
+                int64_t page = a.block_table[b * a.max_pages + j];
+                if (page >= a.num_pages)
+                {
+                    atomicCAS(&g_device_error, 0, ERR_PAGE);
+                    page = 0;
+                }
+                return (int)(page * a.Hkv + kvh);
+            };
             auto issue_k = [&](int t) {
                 const int kt = t % n_a, st = t % kKStages;
                 const uint32_t dst = sbase + kOffK + st * 2 * kKBox;
                 mbar_expect_tx(bar_kfull + 8 * st, 2 * kKBox);
+                if (a.block_table)
+                {
+                    const int z0 = page_z(kt, 0), z1 = page_z(kt, 1);
+                    for (int hf = 0; hf < 2; ++hf)
+                    {
+                        tma_load_3d(dst + hf * kKBox, &tm_k, hf * KH, 0, z0, bar_kfull + 8 * st);
+                        tma_load_3d(dst + hf * kKBox + kKBox / 2, &tm_k, hf * KH, 0, z1, bar_kfull + 8 * st);
+                    }
+                    return;
+                }
                 for (int hf = 0; hf < 2; ++hf)
                     tma_load_3d(dst + hf * kKBox, &tm_k, hf * KH, kt * BN, kz, bar_kfull + 8 * st);
             };
@@ -443,20 +475,23 @@ __global__ void __launch_bounds__(kThreads, 2)
 template <typename T>
 int launch_tc(const void *q, const void *k, const uint32_t *q_lens, const uint32_t *kv_lens, uint32_t max_q,
               uint32_t max_kv, void *qk, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc, int64_t S,
-              cudaStream_t stream)
+              const uint32_t *block_table, int64_t max_pages, int64_t num_pages, cudaStream_t stream)
 {
     const CUtensorMapDataType dt =
         std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int64_t M = std::min<int64_t>(max_kv, S);
     CUtensorMap mq, mk, mp;
     const int64_t m8 = std::max<int64_t>(M & ~int64_t(7), 8);
-    if (!make_map(&mq, dt, q, HD, Qc, batch * Hq, HD * 2, Qc * HD * 2, BM) ||
-        !make_map(&mk, dt, k, HD, S, batch * Hkv, HD * 2, S * HD * 2, BN) ||
+    const bool kmap = block_table ? make_map(&mk, dt, k, HD, kPageRows, num_pages * Hkv, HD * 2,
+                                             kPageRows * HD * 2, kPageRows)
+                                  : make_map(&mk, dt, k, HD, S, batch * Hkv, HD * 2, S * HD * 2, BN);
+    if (!make_map(&mq, dt, q, HD, Qc, batch * Hq, HD * 2, Qc * HD * 2, BM) || !kmap ||
         !make_map(&mp, dt, qk, m8, Qc, batch * Hq, S * 2, Qc * S * 2, BM))
         return set_error(L2K_ERR_CUDA, "l2k_prefill_attention_scores: tensor map encoding failed");
     // c = (1/sqrtf(128)) * log2(e): the oracle's fp32 scale, moved to base 2 for ex2.
     TcArgs a{q_lens, kv_lens, qk, Hq, Hq / Hkv, Hkv, Qc, S, M, M & ~int64_t(7), (int)ceil_div(max_q, BM),
-             (int)ceil_div(M, BN), (1.f / sqrtf((float)HD)) * 1.44269504088896340736f};
+             (int)ceil_div(M, BN), (1.f / sqrtf((float)HD)) * 1.44269504088896340736f, block_table, max_pages,
+             num_pages};
     auto kernel = prefill_scores_tc_kernel<T>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
     if (e != cudaSuccess)
@@ -479,11 +514,14 @@ bool prefill_tc_supported(int dtype, int64_t head_dim, int64_t S, int64_t Qc, co
 
 int prefill_scores_tc(const void *q, const void *k, const uint32_t *q_lens, const uint32_t *kv_lens, uint32_t max_q,
                       uint32_t max_kv, void *qk, int64_t batch, int64_t Hq, int64_t Hkv, int64_t Qc, int64_t S,
-                      int dtype, cudaStream_t stream)
+                      int dtype, cudaStream_t stream, const uint32_t *block_table, int64_t max_pages,
+                      int64_t num_pages)
 {
     if (dtype == L2K_BF16)
-        return launch_tc<__nv_bfloat16>(q, k, q_lens, kv_lens, max_q, max_kv, qk, batch, Hq, Hkv, Qc, S, stream);
-    return launch_tc<__half>(q, k, q_lens, kv_lens, max_q, max_kv, qk, batch, Hq, Hkv, Qc, S, stream);
+        return launch_tc<__nv_bfloat16>(q, k, q_lens, kv_lens, max_q, max_kv, qk, batch, Hq, Hkv, Qc, S, block_table,
+                                        max_pages, num_pages, stream);
+    return launch_tc<__half>(q, k, q_lens, kv_lens, max_q, max_kv, qk, batch, Hq, Hkv, Qc, S, block_table, max_pages,
+                             num_pages, stream);
 }
 
 int read_scores_error(bool clear); // decode_scores.cu

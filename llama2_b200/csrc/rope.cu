@@ -59,8 +59,8 @@ struct RopeArgs
     int64_t S;
     const float2 *table;
     int64_t table_pos;
-    // Paged caches (decode only): k and v are (num_pages, Hkv, page_rows, hd);
-    // position pos of sequence b lives in page block_table[b][pos / page_rows].
+    // Paged caches: k and v are (num_pages, Hkv, page_rows, hd); position pos
+    // of sequence b lives in page block_table[b][pos / page_rows].
     const uint32_t *block_table;
     int64_t max_pages;
     int64_t num_pages;
@@ -461,4 +461,27 @@ extern "C" int l2k_fused_reshape_rope_kvcache_paged_decode(const void *input, co
     a.num_pages = num_pages;
     a.page_rows = page_rows;
     return rope_entry(a, pairing, false, dtype, stream, "l2k_fused_reshape_rope_kvcache_paged_decode");
+}
+
+extern "C" int l2k_fused_pad_reshape_transpose_rope_kvcache_paged(
+    const void *input, const uint32_t *q_lens, const uint32_t *kv_lens, const uint32_t *unpad_to_pad_idx, void *q,
+    void *k_pages, void *v_pages, const uint32_t *block_table, int64_t max_pages, int64_t num_pages, int64_t page_rows,
+    int64_t num_tokens, int64_t batch, int64_t q_head_num, int64_t kv_head_num, int64_t head_dim, int64_t q_cache_len,
+    const float *rope_table, int64_t rope_table_positions, int pairing, int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    L2K_REQUIRE(pairing == L2K_ROPE_INTERLEAVED || pairing == L2K_ROPE_HALF,
+                "l2k_fused_pad_reshape_transpose_rope_kvcache_paged: bad pairing %d", pairing);
+    L2K_REQUIRE(max_pages >= 0 && num_pages >= 0 && page_rows > 0,
+                "l2k_fused_pad_reshape_transpose_rope_kvcache_paged: bad page geometry");
+    L2K_REQUIRE(batch == 0 || num_tokens == 0 || (block_table && max_pages > 0 && num_pages > 0),
+                "l2k_fused_pad_reshape_transpose_rope_kvcache_paged: null or empty block table");
+    RopeArgs a = prefill_args(input, q_lens, kv_lens, unpad_to_pad_idx, q, k_pages, v_pages, num_tokens, batch,
+                              q_head_num, kv_head_num, head_dim, q_cache_len, max_pages * page_rows, rope_table,
+                              rope_table_positions);
+    a.block_table = block_table;
+    a.max_pages = max_pages;
+    a.num_pages = num_pages;
+    a.page_rows = page_rows;
+    return rope_entry(a, pairing, true, dtype, stream, "l2k_fused_pad_reshape_transpose_rope_kvcache_paged");
 }

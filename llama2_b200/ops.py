@@ -449,6 +449,63 @@ def decode_attention_paged(q, k_pages, v_pages, block_table, kv_lens, max_kv_len
               qkv.data_ptr(), b, hq, hkv, hd, _code(q), _stream())
 
 
+def launch_rope_kvcache_paged_prefill(input, q_lens, kv_lens, unpad_to_pad_idx, q, k_pages, v_pages, block_table, *,
+                                      pairing, use_table=True):
+    """Prefill RoPE + K/V append (the padded q of
+    launch_fused_pad_reshape_transpose_rope_kvcache[_llama2]) into paged caches
+    k_pages / v_pages (num_pages, Hkv, page_rows, hd); block_table (B, max_pages) u32."""
+    _dev(input, q_lens, kv_lens, unpad_to_pad_idx, q, k_pages, v_pages, block_table)
+    for t, nm in ((q_lens, "q_lens"), (kv_lens, "kv_lens"), (unpad_to_pad_idx, "unpad_to_pad_idx"),
+                  (block_table, "block_table")):
+        _u32(t, nm)
+    for t in (q, k_pages, v_pages):
+        _same(input, t, "launch_rope_kvcache_paged_prefill")
+    n = input.shape[0]
+    b, hq, qc, hd = q.shape
+    n_pages, hkv, page_rows, _ = k_pages.shape
+    _require(tuple(v_pages.shape) == tuple(k_pages.shape), "Incorrect v_pages size")
+    _require(input.shape[1] == (hq + 2 * hkv) * hd, "Incorrect embedding dim")
+    _require(block_table.shape[0] == b and q_lens.shape[0] == b and kv_lens.shape[0] == b, "Incorrect batch size")
+    _require(unpad_to_pad_idx.numel() >= n, "unpad_to_pad_idx too small")
+    table = rope_table(hd, q.device) if use_table else None
+    capi.call("l2k_fused_pad_reshape_transpose_rope_kvcache_paged", input.data_ptr(), q_lens.data_ptr(),
+              kv_lens.data_ptr(), unpad_to_pad_idx.data_ptr(), q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
+              block_table.data_ptr(), block_table.shape[1], n_pages, page_rows, n, b, hq, hkv, hd, qc,
+              table.data_ptr() if table is not None else None, ROPE_TABLE_POSITIONS if table is not None else 0,
+              int(pairing), _code(q), _stream())
+
+
+def prefill_attention_scores_paged(q, k_pages, block_table, q_lens, kv_lens, max_q_len, max_kv_len, qk):
+    """prefill_attention_scores over a paged K cache (num_pages, Hkv, 64, 128),
+    16-bit; qk (B, Hq, q_cache_len, max_pages * 64)."""
+    _dev(q, k_pages, block_table, q_lens, kv_lens, qk)
+    _u32(block_table, "block_table")
+    _same(q, k_pages, "prefill_attention_scores_paged")
+    _same(q, qk, "prefill_attention_scores_paged")
+    b, hq, qc, hd = q.shape
+    n_pages, hkv = k_pages.shape[0], k_pages.shape[1]
+    max_pages = block_table.shape[1]
+    _require(tuple(qk.shape) == (b, hq, qc, max_pages * 64), "Incorrect qk size")
+    capi.call("l2k_prefill_attention_scores_paged", q.data_ptr(), k_pages.data_ptr(), block_table.data_ptr(),
+              max_pages, n_pages, q_lens.data_ptr(), kv_lens.data_ptr(), int(max_q_len), int(max_kv_len),
+              qk.data_ptr(), b, hq, hkv, qc, hd, _code(q), _stream())
+
+
+def launch_attention_qkv_paged(qk, v_pages, block_table, kv_lens, qkv, M, N):
+    """launch_attention_qkv over a paged V cache (num_pages, Hkv, 64, 128), 16-bit."""
+    _dev(qk, v_pages, block_table, kv_lens, qkv)
+    _u32(block_table, "block_table")
+    _same(qk, v_pages, "launch_attention_qkv_paged")
+    _same(qk, qkv, "launch_attention_qkv_paged")
+    b, hq, qc, s = qk.shape
+    n_pages, hkv, _, hd = v_pages.shape
+    max_pages = block_table.shape[1]
+    _require(s == max_pages * 64, "Incorrect qk size")
+    _require(tuple(qkv.shape) == (b, hq, qc, hd), "Incorrect qkv size")
+    capi.call("l2k_attention_qkv_paged", qk.data_ptr(), v_pages.data_ptr(), block_table.data_ptr(), max_pages,
+              n_pages, kv_lens.data_ptr(), qkv.data_ptr(), b, hq, hkv, qc, hd, int(M), int(N), _code(qk), _stream())
+
+
 def prefill_attention_scores(q, k, q_lens, kv_lens, max_q_len, max_kv_len, qk):
     """Fused QK^T + scale + causal mask + softmax for q_len query rows per sequence."""
     _dev(q, k, q_lens, kv_lens, qk)

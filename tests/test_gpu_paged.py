@@ -111,3 +111,88 @@ def test_paged_attention_page_past_the_pool_is_an_error_not_a_read():
     torch.cuda.synchronize()
     assert capi.lib().l2k_device_error(1) == 0x206
     assert np.isfinite(host(qk)).all() and np.isfinite(host(o)).all()
+
+
+# ---------------------------------------------------------------------------
+# Paged prefill: RoPE + append, tensor-core scores and P.V over paged caches
+# ---------------------------------------------------------------------------
+def _prefill_inputs(dtype, q_lens, hist, hq, hkv, hd, seed):
+    from oracle import port
+    b = len(q_lens)
+    qc = max(q_lens)
+    ql = np.asarray(q_lens, np.uint32)
+    unpad, _ = port.build_padding_index_maps(ql, qc)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    t = int(ql.sum())
+    qkv = torch.randn(t, (hq + 2 * hkv) * hd, generator=g, device="cuda").to(dtype)
+    q_lens_d = torch.tensor(q_lens, dtype=torch.uint32, device="cuda")
+    kv_lens_d = torch.tensor([h + q for h, q in zip(hist, q_lens)], dtype=torch.uint32, device="cuda")
+    return qkv, q_lens_d, kv_lens_d, torch.from_numpy(unpad.astype(np.uint32)).cuda(), qc
+
+
+@pytest.mark.parametrize("dtype,pairing", [(torch.bfloat16, 1), (torch.float32, 0), (torch.float16, 1)])
+def test_paged_prefill_rope_append_matches_contiguous(dtype, pairing):
+    """Ragged prompts after a history: every token's K/V row lands on its page
+    and q is the padded q of the contiguous operator, bit for bit."""
+    b, hq, hkv, hd, max_pages = 3, 8, 2, 128, 8
+    k, v, kp, vp, table, rows = _paged_setup(dtype, b, hq, hkv, hd, max_pages, spare=4, seed=11)
+    s = max_pages * rows
+    q_lens, hist = [5, rows + 7, 2 * rows], [0, rows - 3, s - 2 * rows]
+    qkv, ql, kl, unpad, qc = _prefill_inputs(dtype, q_lens, hist, hq, hkv, hd, seed=12)
+    q1 = torch.zeros(b, hq, qc, hd, dtype=dtype, device="cuda")
+    q2 = torch.zeros_like(q1)
+    rope = (ops.launch_fused_pad_reshape_transpose_rope_kvcache_llama2 if pairing
+            else ops.launch_fused_pad_reshape_transpose_rope_kvcache)
+    rope(qkv, ql, kl, unpad, q1, k, v)
+    ops.launch_rope_kvcache_paged_prefill(qkv, ql, kl, unpad, q2, kp, vp, table, pairing=pairing)
+    torch.cuda.synchronize()
+    assert bits_equal(host(q1), host(q2))
+    assert bits_equal(host(_gather(kp, table, rows)), host(k))
+    assert bits_equal(host(_gather(vp, table, rows)), host(v))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("q_lens,hist", [([128, 77, 300], [0, 100, 212]),   # ragged, with history
+                                         ([256, 256], [0, 0])])              # fresh prompts, whole tiles
+def test_paged_prefill_scores_and_pv_match_contiguous(dtype, q_lens, hist):
+    """The tensor-core scores over a shuffled page pool equal the contiguous
+    scores bit for bit (the same tiles, two pages per 128-key tile), and P.V
+    over paged V equals the contiguous P.V."""
+    b, hq, hkv, hd, max_pages = len(q_lens), 8, 2, 128, 10
+    k, v, kp, vp, table, rows = _paged_setup(dtype, b, hq, hkv, hd, max_pages, spare=5, seed=21)
+    assert rows == 64
+    s = max_pages * rows
+    qc = max(q_lens)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(22)
+    q = torch.randn(b, hq, qc, hd, generator=g, device="cuda").to(dtype)
+    ql = torch.tensor(q_lens, dtype=torch.uint32, device="cuda")
+    kv = [h + x for h, x in zip(hist, q_lens)]
+    kl = torch.tensor(kv, dtype=torch.uint32, device="cuda")
+    max_q, max_kv = max(q_lens), max(kv)
+    p1 = torch.full((b, hq, qc, s), 3.0, dtype=dtype, device="cuda")
+    p2 = p1.clone()
+    ops.prefill_attention_scores(q, k, ql, kl, max_q, max_kv, p1)
+    ops.prefill_attention_scores_paged(q, kp, table, ql, kl, max_q, max_kv, p2)
+    torch.cuda.synchronize()
+    assert bits_equal(host(p1), host(p2))
+    o1 = torch.zeros(b, hq, qc, hd, dtype=dtype, device="cuda")
+    o2 = torch.zeros_like(o1)
+    ops.launch_attention_qkv(p1, v, o1, max_q, max_kv)
+    ops.launch_attention_qkv_paged(p2, vp, table, kl, o2, max_q, max_kv)
+    torch.cuda.synchronize()
+    # equal as numbers (an all-zero probability row may sum its zero products to -0 or +0)
+    assert torch.equal(o1.float(), o2.float())
+    assert capi.lib().l2k_device_error(1) == 0
+
+
+def test_paged_prefill_rejects_shapes_the_tensor_cores_do_not_take():
+    b, hq, hkv, hd = 1, 2, 2, 64
+    kp = torch.zeros(4, hkv, 64, hd, dtype=torch.bfloat16, device="cuda")
+    table = torch.zeros(b, 2, dtype=torch.uint32, device="cuda")
+    q = torch.zeros(b, hq, 64, hd, dtype=torch.bfloat16, device="cuda")
+    ql = torch.tensor([64], dtype=torch.uint32, device="cuda")
+    qk = torch.zeros(b, hq, 64, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(capi.L2KError):
+        ops.prefill_attention_scores_paged(q, kp, table, ql, ql, 64, 64, qk)
