@@ -182,8 +182,11 @@ def test_paged_prefill_scores_and_pv_match_contiguous(dtype, q_lens, hist):
     ops.launch_attention_qkv(p1, v, o1, max_q, max_kv)
     ops.launch_attention_qkv_paged(p2, vp, table, kl, o2, max_q, max_kv)
     torch.cuda.synchronize()
-    # equal as numbers (an all-zero probability row may sum its zero products to -0 or +0)
-    assert torch.equal(o1.float(), o2.float())
+    # Rows i < q_len of each sequence (the rows the scores defined; rows past
+    # q_len hold whatever the buffer held, so their products are unspecified),
+    # equal as numbers.
+    for bi, n in enumerate(q_lens):
+        assert torch.equal(o1[bi, :, :n].float(), o2[bi, :, :n].float()), bi
     assert capi.lib().l2k_device_error(1) == 0
 
 
