@@ -14,7 +14,9 @@
  * (batch, kv_head, kv_cache_len, head_dim).
  *
  * Element types (`dtype`): L2K_F32, L2K_F16, L2K_BF16. Arithmetic is fp32 in
- * every kernel; 16-bit types are rounded to nearest-even on store.
+ * every kernel; 16-bit types are rounded to nearest-even on store. The fp8
+ * K/V cache entries (l2k_*_fp8_*) store cache elements as e4m3 bytes with a
+ * per-cache fp32 scale (value = scale * e4m3) next to 16-bit activations.
  */
 #ifndef LLAMA2_B200_H
 #define LLAMA2_B200_H
@@ -31,7 +33,8 @@ enum l2k_dtype
 {
     L2K_F32 = 0,
     L2K_F16 = 1,
-    L2K_BF16 = 2
+    L2K_BF16 = 2,
+    L2K_E4M3 = 3 /* fp8 e4m3 K/V cache elements: only l2k_paged_block_rows takes this code */
 };
 
 enum l2k_status
@@ -456,6 +459,44 @@ int l2k_decode_attention_paged(const void *q, const void *k_pages, const void *v
                                int64_t max_pages, int64_t num_pages, const uint32_t *kv_lens,
                                const uint32_t *max_kv_len, void *qk, void *qkv, int64_t batch, int64_t q_head_num,
                                int64_t kv_head_num, int64_t head_dim, int dtype, l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * fp8 (e4m3) K/V caches (decode). No counterpart in the reference, whose
+ * DataType stops at FP32/FP16/INT8 (include/common/types.h:60-71); each
+ * replaces the 16-bit operator named beside it for caches of one byte per
+ * element, holding value / scale rounded to e4m3 (nearest even, saturating
+ * at +-448), with one positive fp32 scale per cache (k_scale, v_scale).
+ * dtype is the activation type, L2K_BF16 or L2K_F16.
+ *
+ * l2k_fused_reshape_rope_kvcache_fp8_decode: the decode RoPE + append of
+ *   l2k_fused_reshape_rope_kvcache[_llama2]_decode (pairing selects which):
+ *   q in dtype; the rotated k and the v row scaled by 1 / scale (fp32) and
+ *   rounded once to e4m3 at row kv_lens[b] - 1 of the byte caches
+ *   (batch, kv_head_num, kv_cache_len, head_dim).
+ * l2k_decode_attention_fp8: l2k_decode_attention over those caches: logits
+ *   (q . k8) * (k_scale / sqrt(head_dim)), output v_scale * sum p_j v8_j,
+ *   fp32 arithmetic on the exact e4m3 values; head_dim 64/128/256/512,
+ *   16-byte aligned operands; qk (B, Hq, 1, kv_cache_len) and qkv in dtype.
+ * l2k_decode_attention_fp8_paged: the same over page pools (num_pages,
+ *   kv_head_num, 16384 / head_dim, head_dim) of bytes and a block table as
+ *   for l2k_decode_attention_paged (l2k_paged_block_rows(head_dim,
+ *   L2K_E4M3) rows per page); qk is (B, Hq, 1, max_pages * page_rows).
+ * ------------------------------------------------------------------------ */
+int l2k_fused_reshape_rope_kvcache_fp8_decode(const void *input, const uint8_t *is_done, const uint32_t *kv_lens,
+                                              void *q, void *k_cache, void *v_cache, float k_scale, float v_scale,
+                                              int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                              int64_t head_dim, int64_t kv_cache_len, const float *rope_table,
+                                              int64_t rope_table_positions, int pairing, int dtype,
+                                              l2k_stream_t stream);
+int l2k_decode_attention_fp8(const void *q, const void *k_cache, const void *v_cache, float k_scale, float v_scale,
+                             const uint32_t *kv_lens, const uint32_t *max_kv_len, void *qk, void *qkv, int64_t batch,
+                             int64_t q_head_num, int64_t kv_head_num, int64_t kv_cache_len, int64_t head_dim,
+                             int dtype, l2k_stream_t stream);
+int l2k_decode_attention_fp8_paged(const void *q, const void *k_pages, const void *v_pages, float k_scale,
+                                   float v_scale, const uint32_t *block_table, int64_t max_pages, int64_t num_pages,
+                                   const uint32_t *kv_lens, const uint32_t *max_kv_len, void *qk, void *qkv,
+                                   int64_t batch, int64_t q_head_num, int64_t kv_head_num, int64_t head_dim, int dtype,
+                                   l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Paged K/V caches (prefill), same pool layout and block table as above.

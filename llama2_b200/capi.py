@@ -20,6 +20,7 @@ vp = ctypes.c_void_p
 i64 = ctypes.c_int64
 u32 = ctypes.c_uint32
 cint = ctypes.c_int
+f32 = ctypes.c_float
 
 
 class DecodeStepArgs(ctypes.Structure):
@@ -80,6 +81,11 @@ SIGNATURES = {
     "l2k_prefill_attention_scores_paged": [vp, vp, vp, i64, i64, vp, vp, u32, u32, vp, i64, i64, i64, i64, i64, cint,
                                            vp],
     "l2k_attention_qkv_paged": [vp, vp, vp, i64, i64, vp, vp, i64, i64, i64, i64, i64, i64, i64, cint, vp],
+    "l2k_fused_reshape_rope_kvcache_fp8_decode": [vp, vp, vp, vp, vp, vp, f32, f32, i64, i64, i64, i64, i64, vp, i64,
+                                                  cint, cint, vp],
+    "l2k_decode_attention_fp8": [vp, vp, vp, f32, f32, vp, vp, vp, vp, i64, i64, i64, i64, i64, cint, vp],
+    "l2k_decode_attention_fp8_paged": [vp, vp, vp, f32, f32, vp, i64, i64, vp, vp, vp, vp, i64, i64, i64, i64, cint,
+                                       vp],
     "l2k_decode_step_workspace_bytes": ([], i64),
     "l2k_decode_step_supported": [ctypes.POINTER(DecodeStepArgs)],
     "l2k_decode_step": [ctypes.POINTER(DecodeStepArgs), vp, vp],

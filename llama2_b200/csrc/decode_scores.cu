@@ -78,15 +78,16 @@ __global__ void __launch_bounds__(kStreamThreads) score_rows_stream_kernel(const
 
 // Attention rows: the score row and its P.V output in one streamed pass
 // over the row's K and V blocks (score_row_stream with PV).
-template <typename T, int LPR>
+// TC: the cache element type (T, or fp8 e4m3 with 16-bit T).
+template <typename T, int LPR, typename TC = T>
 __global__ void __launch_bounds__(kStreamThreads) attention_rows_stream_kernel(const DecodeArgs a)
 {
     extern __shared__ __align__(128) uint8_t stream_smem[];
     __shared__ StreamShared sh;
     cg::cluster_group cluster = cg::this_cluster();
     const StepRowArgs none{};
-    score_row_stream<T, LPR, false, true>(a, none, (int64_t)blockIdx.x / cluster.num_blocks(), cluster, stream_smem,
-                                          sh, &g_scores_error);
+    score_row_stream<T, LPR, false, true, TC>(a, none, (int64_t)blockIdx.x / cluster.num_blocks(), cluster,
+                                              stream_smem, sh, &g_scores_error);
 }
 
 // Any head_dim / alignment: one thread per key, q staged in shared memory.
@@ -171,11 +172,11 @@ bool stream_rows_ok(const DecodeArgs &a, bool pv)
     return vec && (lpr == 4 || lpr == 8 || lpr == 16 || lpr == 32);
 }
 
-template <typename T>
+template <typename T, typename TC = T>
 int launch_attention_rows(const DecodeArgs &a, int64_t batch, cudaStream_t stream)
 {
     const int64_t rows = batch * a.Hq * a.Qc;
-    const int64_t row_bytes = a.hd * (int64_t)sizeof(T);
+    const int64_t row_bytes = a.hd * (int64_t)sizeof(TC);
     const int lpr = (int)(row_bytes / 16);
     const int64_t kb = kBlockBytes / row_bytes;
     const int64_t blocks_per_row = ceil_div(a.S, kb);
@@ -187,13 +188,13 @@ int launch_attention_rows(const DecodeArgs &a, int64_t batch, cudaStream_t strea
                       (long long)a.S);
     cudaError_t e;
     if (lpr == 32)
-        e = launch_clustered(attention_rows_stream_kernel<T, 32>, C, rows, smem, stream, a, kStreamThreads);
+        e = launch_clustered(attention_rows_stream_kernel<T, 32, TC>, C, rows, smem, stream, a, kStreamThreads);
     else if (lpr == 16)
-        e = launch_clustered(attention_rows_stream_kernel<T, 16>, C, rows, smem, stream, a, kStreamThreads);
+        e = launch_clustered(attention_rows_stream_kernel<T, 16, TC>, C, rows, smem, stream, a, kStreamThreads);
     else if (lpr == 8)
-        e = launch_clustered(attention_rows_stream_kernel<T, 8>, C, rows, smem, stream, a, kStreamThreads);
+        e = launch_clustered(attention_rows_stream_kernel<T, 8, TC>, C, rows, smem, stream, a, kStreamThreads);
     else
-        e = launch_clustered(attention_rows_stream_kernel<T, 4>, C, rows, smem, stream, a, kStreamThreads);
+        e = launch_clustered(attention_rows_stream_kernel<T, 4, TC>, C, rows, smem, stream, a, kStreamThreads);
     if (e != cudaSuccess)
         return set_error(L2K_ERR_CUDA, "attention rows: %s", cudaGetErrorString(e));
     return check_launch("attention rows");
@@ -321,9 +322,9 @@ extern "C" int l2k_decode_attention(const void *q, const void *k, const void *v,
 extern "C" int64_t l2k_paged_block_rows(int64_t head_dim, int dtype)
 {
     using namespace l2k;
-    if (!dtype_ok(dtype) || head_dim <= 0)
+    if (!(dtype_ok(dtype) || dtype == L2K_E4M3) || head_dim <= 0)
         return 0;
-    const int64_t row_bytes = head_dim * (int64_t)dtype_size(dtype);
+    const int64_t row_bytes = head_dim * (dtype == L2K_E4M3 ? int64_t(1) : (int64_t)dtype_size(dtype));
     const int64_t lpr = row_bytes / 16;
     if (row_bytes % 16 != 0 || !(lpr == 4 || lpr == 8 || lpr == 16 || lpr == 32))
         return 0;
@@ -387,4 +388,77 @@ extern "C" int l2k_decode_attention_scores(const void *q, const void *k, const u
                  kv_cache_len, head_dim, 0, 1.f / sqrtf((float)head_dim)};
     L2K_DISPATCH(dtype, { return launch_score_rows<T>(a, batch, stream); });
     return L2K_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention over fp8 (e4m3) K/V caches: the streaming attention rows
+// with each 16 KB block holding 16384 / head_dim rows; q, the probabilities
+// and the output in `dtype` (16-bit); the logits are (q . k8) * (k_scale /
+// sqrt(hd)) and the output v_scale * sum_j p_j v8_j, fp32 throughout.
+// block_table == NULL: contiguous caches (B, Hkv, S, hd) of bytes; else pools
+// (num_pages, Hkv, 16384 / hd, hd) with S = max_pages * 16384 / hd.
+// ---------------------------------------------------------------------------
+namespace l2k
+{
+namespace
+{
+int decode_attention_fp8(const char *name, const void *q, const void *k, const void *v, float k_scale, float v_scale,
+                         const uint32_t *block_table, int64_t max_pages, int64_t num_pages, const uint32_t *kv_lens,
+                         const uint32_t *max_kv_len, void *qk, void *qkv, int64_t batch, int64_t q_head_num,
+                         int64_t kv_head_num, int64_t kv_cache_len, int64_t head_dim, int dtype, cudaStream_t stream)
+{
+    L2K_REQUIRE(dtype == L2K_BF16 || dtype == L2K_F16, "%s: q/qk/qkv must be bf16 or f16 (dtype %d)", name, dtype);
+    L2K_REQUIRE(batch >= 0 && q_head_num >= 0 && kv_head_num >= 0 && kv_cache_len >= 0 && head_dim > 0,
+                "%s: bad size", name);
+    L2K_REQUIRE(k_scale > 0.f && v_scale > 0.f && std::isfinite(k_scale) && std::isfinite(v_scale),
+                "%s: the cache scales must be positive and finite", name);
+    if (batch == 0 || q_head_num == 0)
+        return L2K_OK;
+    L2K_REQUIRE(kv_head_num > 0 && q_head_num % kv_head_num == 0, "%s: q_head_num must be a multiple of kv_head_num",
+                name);
+    L2K_REQUIRE(q && k && v && kv_lens && max_kv_len && qk && qkv, "%s: null pointer", name);
+    L2K_REQUIRE(kv_cache_len > 0, "%s: kv_cache_len must be positive", name);
+    L2K_REQUIRE_SHAPE(head_dim == 64 || head_dim == 128 || head_dim == 256 || head_dim == 512,
+                      "%s: head_dim must be 64, 128, 256 or 512 (16-byte slices of 1-byte elements)", name);
+    L2K_REQUIRE_SHAPE(is_aligned(q, 16) && is_aligned(k, 16) && is_aligned(v, 16) && is_aligned(qkv, 16),
+                      "%s: q, the caches and qkv must be 16-byte aligned", name);
+    L2K_REQUIRE_SHAPE(batch * q_head_num * 16 < (int64_t(1) << 31), "%s: grid too large", name);
+    DecodeArgs a{q, k, nullptr, kv_lens, max_kv_len, 0u, qk, q_head_num, q_head_num / kv_head_num, kv_head_num, 1,
+                 kv_cache_len, head_dim, 0, (1.f / sqrtf((float)head_dim)) * k_scale};
+    a.v = v;
+    a.qkv = qkv;
+    a.v_scale = v_scale;
+    a.block_table = block_table;
+    a.max_pages = max_pages;
+    a.num_pages = num_pages;
+    if (dtype == L2K_BF16)
+        return launch_attention_rows<__nv_bfloat16, __nv_fp8_e4m3>(a, batch, stream);
+    return launch_attention_rows<__half, __nv_fp8_e4m3>(a, batch, stream);
+}
+} // namespace
+} // namespace l2k
+
+extern "C" int l2k_decode_attention_fp8(const void *q, const void *k_cache, const void *v_cache, float k_scale,
+                                        float v_scale, const uint32_t *kv_lens, const uint32_t *max_kv_len, void *qk,
+                                        void *qkv, int64_t batch, int64_t q_head_num, int64_t kv_head_num,
+                                        int64_t kv_cache_len, int64_t head_dim, int dtype, l2k_stream_t stream)
+{
+    return l2k::decode_attention_fp8("l2k_decode_attention_fp8", q, k_cache, v_cache, k_scale, v_scale, nullptr, 0, 0,
+                                     kv_lens, max_kv_len, qk, qkv, batch, q_head_num, kv_head_num, kv_cache_len,
+                                     head_dim, dtype, stream);
+}
+
+extern "C" int l2k_decode_attention_fp8_paged(const void *q, const void *k_pages, const void *v_pages, float k_scale,
+                                              float v_scale, const uint32_t *block_table, int64_t max_pages,
+                                              int64_t num_pages, const uint32_t *kv_lens, const uint32_t *max_kv_len,
+                                              void *qk, void *qkv, int64_t batch, int64_t q_head_num,
+                                              int64_t kv_head_num, int64_t head_dim, int dtype, l2k_stream_t stream)
+{
+    using namespace l2k;
+    L2K_REQUIRE(max_pages > 0 && num_pages > 0 && block_table, "l2k_decode_attention_fp8_paged: empty block table "
+                                                               "or page pool");
+    L2K_REQUIRE_SHAPE(head_dim > 0 && 16384 % head_dim == 0, "l2k_decode_attention_fp8_paged: bad head_dim");
+    return l2k::decode_attention_fp8("l2k_decode_attention_fp8_paged", q, k_pages, v_pages, k_scale, v_scale,
+                                     block_table, max_pages, num_pages, kv_lens, max_kv_len, qk, qkv, batch,
+                                     q_head_num, kv_head_num, max_pages * (16384 / head_dim), head_dim, dtype, stream);
 }

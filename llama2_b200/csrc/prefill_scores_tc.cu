@@ -5,11 +5,14 @@
 // each tcgen05.mma is 128 x 128 x 16 (wide enough to keep the tensor pipe
 // efficient; two CTAs per SM still fit: 112 KB of shared memory, 256 TMEM
 // columns each).
-// Warp roles (288 threads):
-//   * warp 8 (control): TMA (cp.async.bulk.tensor, 128-byte swizzle) of the
-//     Q tile once and of K tiles (2 x 16 KB boxes) through a 2-stage ring;
-//     tcgen05.mma with both operands in shared memory and the fp32
-//     accumulator in tensor memory (2 x 128 columns, double buffered);
+// Warp roles (320 threads):
+//   * warp 9 (producer): TMA (cp.async.bulk.tensor, 128-byte swizzle) of the
+//     Q tile once and of K tiles (2 x 16 KB boxes) through a 2-stage ring,
+//     each stage refilled as soon as the MMAs that read it have completed
+//     (tcgen05.commit onto the stage's "empty" mbarrier);
+//   * warp 8 (MMA): tcgen05.mma with both operands in shared memory and the
+//     fp32 accumulator in tensor memory (2 x 128 columns, double buffered),
+//     issued back to back as K stages and TMEM buffers become available;
 //     tcgen05.commit signals "tile ready" on an mbarrier.
 //   * warps 0-7 (epilogue): warp w reads TMEM lanes 32*(w%4).. (its rows) and
 //     columns 64*(w/4).. of each tile (two tcgen05.ld of 32 columns).
@@ -55,8 +58,9 @@ namespace
 
 constexpr int BM = 128, BN = 128, HD = 128, KH = 64; // KH: elements per 128-byte swizzle row
 constexpr int kEpiWarps = 8;
-constexpr int kThreads = 32 * (kEpiWarps + 1);
-constexpr int kCtl = kEpiWarps;                        // control warp index
+constexpr int kThreads = 32 * (kEpiWarps + 2);
+constexpr int kCtl = kEpiWarps;                        // MMA warp index
+constexpr int kProd = kEpiWarps + 1;                   // producer warp index
 constexpr int kColGroups = kEpiWarps / 4;              // epilogue warps per TMEM lane quadrant
 constexpr int kColsPerWarp = BN / kColGroups;          // 64
 constexpr uint32_t kQBox = 128 * 128;                  // 128 rows x 128 B
@@ -151,6 +155,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t bar_kfull = bar_q + 8;    // + 8 * stage (kKStages)
     const uint32_t bar_mma = bar_q + 32;     // + 8 * buffer: tile in TMEM buffer is ready
     const uint32_t bar_tfree = bar_q + 48;   // + 8 * buffer: epilogue finished with TMEM buffer
+    const uint32_t bar_kempty = bar_q + 64;  // + 8 * stage: the MMAs reading the K stage completed
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kOffMisc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kOffMisc + 8);
     float2 *stats = reinterpret_cast<float2 *>(smem + kOffP); // [kColGroups][128], after the zero stores
@@ -185,6 +190,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             mbar_init(bar_mma + 8 * i, 1);
             mbar_init(bar_tfree + 8 * i, kEpiWarps);
         }
+        for (int i = 0; i < kKStages; ++i)
+            mbar_init(bar_kempty + 8 * i, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -206,13 +213,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == kCtl)
+    if (warp == kProd)
     {
-        // ================= control warp =================
+        // ================= producer warp =================
         if (lane == 0 && n_steps > 0)
         {
-            const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-            const uint32_t idesc_full = instr_desc(fmt, BN), idesc_half = instr_desc(fmt, BN / 2);
             const int kz = (int)(b * a.Hkv + kvh);
             // Paged: the tile's two 64-key pages. A page wholly past the
             // sequence's length (its table entry may be unset) is replaced by
@@ -249,8 +254,25 @@ __global__ void __launch_bounds__(kThreads, 2)
             mbar_expect_tx(bar_q, 2 * kQBox);
             for (int hf = 0; hf < 2; ++hf)
                 tma_load_3d(sbase + kOffQ + hf * kQBox, &tm_q, hf * KH, (int)row0, (int)bh, bar_q);
-            for (int t = 0; t < kKStages && t < n_steps; ++t)
+            for (int t = 0; t < n_steps && !*abort_flag; ++t)
+            {
+                const int ks = t % kKStages;
+                if (t >= kKStages && !mbar_wait(bar_kempty + 8 * ks, ((t / kKStages) - 1) & 1, abort_flag))
+                {
+                    fail(ERR_WAIT_MMA, abort_flag);
+                    break;
+                }
                 issue_k(t);
+            }
+        }
+    }
+    else if (warp == kCtl)
+    {
+        // ================= MMA warp =================
+        if (lane == 0 && n_steps > 0)
+        {
+            const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+            const uint32_t idesc_full = instr_desc(fmt, BN), idesc_half = instr_desc(fmt, BN / 2);
             if (!mbar_wait(bar_q, 0, abort_flag))
                 fail(ERR_WAIT_Q, abort_flag);
             for (int t = 0; t < n_steps && !*abort_flag; ++t)
@@ -279,17 +301,8 @@ __global__ void __launch_bounds__(kThreads, 2)
                     const uint32_t offb = (uint32_t)((k & 3) * 32) + (uint32_t)(k >> 2) * kKBox;
                     mma_f16(d, smem_desc(sbase + kOffQ + offa), smem_desc(kb + offb), idesc, k > 0 ? 1u : 0u);
                 }
-                mma_commit(bar_mma + 8 * st);
-                if (t + kKStages < n_steps)
-                {
-                    // the K stage is free once this tile's MMAs have read it
-                    if (!mbar_wait(bar_mma + 8 * st, (t >> 1) & 1, abort_flag))
-                    {
-                        fail(ERR_WAIT_MMA, abort_flag);
-                        break;
-                    }
-                    issue_k(t + kKStages);
-                }
+                mma_commit(bar_mma + 8 * st);    // the tile is in TMEM
+                mma_commit(bar_kempty + 8 * ks); // the K stage may be refilled
             }
         }
     }

@@ -30,6 +30,7 @@
 #include "rope_math.cuh"
 
 #include <algorithm>
+#include <cmath>
 
 namespace l2k
 {
@@ -484,4 +485,120 @@ extern "C" int l2k_fused_pad_reshape_transpose_rope_kvcache_paged(
     a.num_pages = num_pages;
     a.page_rows = page_rows;
     return rope_entry(a, pairing, true, dtype, stream, "l2k_fused_pad_reshape_transpose_rope_kvcache_paged");
+}
+
+// ---------------------------------------------------------------------------
+// Decode RoPE + K/V append into fp8 (e4m3) caches. q is rotated and stored in
+// the activation type; the rotated k and the v row are scaled by the inverse
+// of their cache's scale and rounded once to e4m3 (round to nearest even,
+// saturating at +-448), straight from fp32 — no 16-bit rounding in between.
+// One CTA per (sequence, head), one thread per rotation pair (a v head: two
+// elements per thread).
+// ---------------------------------------------------------------------------
+namespace l2k
+{
+namespace
+{
+struct RopeFp8Args
+{
+    const void *input;
+    const uint8_t *is_done;
+    const uint32_t *kv_lens;
+    void *q;
+    uint8_t *k;
+    uint8_t *v;
+    int64_t batch, hq, hkv, hd, S;
+    const float2 *table;
+    int64_t table_pos;
+    float inv_k_scale, inv_v_scale;
+};
+
+__device__ __forceinline__ uint8_t to_e4m3(float x)
+{
+    return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+
+template <typename T, int PAIRING>
+__global__ void __launch_bounds__(256) rope_kvcache_fp8_decode_kernel(const RopeFp8Args a)
+{
+    const int64_t seq = blockIdx.x / (a.hq + 2 * a.hkv);
+    const int64_t head = blockIdx.x - seq * (a.hq + 2 * a.hkv);
+    if (a.is_done[seq])
+        return;
+    const uint32_t kv_len = a.kv_lens[seq];
+    const uint32_t pos = kv_len - 1u;
+    if ((int64_t)pos >= a.S)
+        return;
+    const int64_t half = a.hd / 2;
+    const T *src = static_cast<const T *>(a.input) + (seq * (a.hq + 2 * a.hkv) + head) * a.hd;
+    for (int64_t i = threadIdx.x; i < half; i += blockDim.x)
+    {
+        const int64_t i0 = PAIRING == L2K_ROPE_INTERLEAVED ? 2 * i : i;
+        const int64_t i1 = PAIRING == L2K_ROPE_INTERLEAVED ? 2 * i + 1 : i + half;
+        if (head >= a.hq + a.hkv)
+        {
+            const int64_t h = head - a.hq - a.hkv;
+            uint8_t *dst = a.v + ((seq * a.hkv + h) * a.S + pos) * a.hd;
+            dst[i0] = to_e4m3(__fmul_rn(to_f(src[i0]), a.inv_v_scale));
+            dst[i1] = to_e4m3(__fmul_rn(to_f(src[i1]), a.inv_v_scale));
+            continue;
+        }
+        float c, s;
+        rope_cos_sin(a.table, a.table_pos, i, a.hd, pos, kv_len, c, s);
+        const float x0 = to_f(src[i0]), x1 = to_f(src[i1]);
+        const float o0 = rope_o0(c, s, x0, x1), o1 = rope_o1(c, s, x0, x1);
+        if (head < a.hq)
+        {
+            T *dst = static_cast<T *>(a.q) + (seq * a.hq + head) * a.hd;
+            dst[i0] = from_f<T>(o0);
+            dst[i1] = from_f<T>(o1);
+        }
+        else
+        {
+            uint8_t *dst = a.k + ((seq * a.hkv + (head - a.hq)) * a.S + pos) * a.hd;
+            dst[i0] = to_e4m3(__fmul_rn(o0, a.inv_k_scale));
+            dst[i1] = to_e4m3(__fmul_rn(o1, a.inv_k_scale));
+        }
+    }
+}
+} // namespace
+} // namespace l2k
+
+extern "C" int l2k_fused_reshape_rope_kvcache_fp8_decode(const void *input, const uint8_t *is_done,
+                                                         const uint32_t *kv_lens, void *q, void *k_cache,
+                                                         void *v_cache, float k_scale, float v_scale, int64_t batch,
+                                                         int64_t q_head_num, int64_t kv_head_num, int64_t head_dim,
+                                                         int64_t kv_cache_len, const float *rope_table,
+                                                         int64_t rope_table_positions, int pairing, int dtype,
+                                                         l2k_stream_t stream)
+{
+    using namespace l2k;
+    const char *name = "l2k_fused_reshape_rope_kvcache_fp8_decode";
+    L2K_REQUIRE(dtype_ok(dtype), "%s: unsupported dtype %d", name, dtype);
+    L2K_REQUIRE(pairing == L2K_ROPE_INTERLEAVED || pairing == L2K_ROPE_HALF, "%s: bad pairing %d", name, pairing);
+    L2K_REQUIRE(batch >= 0 && q_head_num >= 0 && kv_head_num >= 0 && head_dim >= 0 && kv_cache_len >= 0,
+                "%s: negative size", name);
+    L2K_REQUIRE(head_dim % 2 == 0, "%s: head_dim must be even (got %lld)", name, (long long)head_dim);
+    L2K_REQUIRE(k_scale > 0.f && v_scale > 0.f && std::isfinite(k_scale) && std::isfinite(v_scale),
+                "%s: the cache scales must be positive and finite", name);
+    L2K_REQUIRE(rope_table_positions >= 0, "%s: negative rope_table_positions", name);
+    if (batch == 0 || head_dim == 0 || q_head_num + kv_head_num == 0)
+        return L2K_OK;
+    L2K_REQUIRE(input && is_done && kv_lens && q && (kv_head_num == 0 || (k_cache && v_cache)), "%s: null pointer",
+                name);
+    L2K_REQUIRE_SHAPE(batch * (q_head_num + 2 * kv_head_num) < (int64_t(1) << 31), "%s: grid too large", name);
+    RopeFp8Args a{input, is_done, kv_lens, q, static_cast<uint8_t *>(k_cache), static_cast<uint8_t *>(v_cache),
+                  batch, q_head_num, kv_head_num, head_dim, kv_cache_len,
+                  reinterpret_cast<const float2 *>(rope_table), rope_table ? rope_table_positions : 0,
+                  1.f / k_scale, 1.f / v_scale};
+    const int threads = (int)std::min<int64_t>(256, std::max<int64_t>(32, (head_dim / 2 + 31) / 32 * 32));
+    const unsigned grid = (unsigned)(batch * (q_head_num + 2 * kv_head_num));
+    L2K_DISPATCH(dtype, {
+        if (pairing == L2K_ROPE_INTERLEAVED)
+            rope_kvcache_fp8_decode_kernel<T, L2K_ROPE_INTERLEAVED><<<grid, threads, 0, (cudaStream_t)stream>>>(a);
+        else
+            rope_kvcache_fp8_decode_kernel<T, L2K_ROPE_HALF><<<grid, threads, 0, (cudaStream_t)stream>>>(a);
+        return check_launch(name);
+    });
+    return L2K_OK;
 }

@@ -77,6 +77,9 @@ struct DecodeArgs
     const uint32_t *block_table;
     int64_t max_pages;
     int64_t num_pages;
+    // fp8 (e4m3) caches only: V values are v_scale * e4m3 (K's scale is
+    // folded into `scale`).
+    float v_scale;
 };
 
 // Extra inputs of a score row inside the fused decode step. kv_lens and
@@ -188,6 +191,36 @@ __device__ __forceinline__ float dot16(uint4 k, uint4 q, const float *qf)
 L2K_DOT16_MIXED(__nv_bfloat16, "bf16")
 L2K_DOT16_MIXED(__half, "f16")
 #undef L2K_DOT16_MIXED
+
+// 16 e4m3 cache elements as fp32: e4m3 -> f16 pairs (exact), f16 -> fp32 (exact).
+__device__ __forceinline__ void e4m3x16_to_f32(uint4 k, float (&f)[16])
+{
+    const uint32_t w[4] = {k.x, k.y, k.z, k.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] & 0xFFFFu), __NV_E4M3);
+        const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> 16), __NV_E4M3);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&lo));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&hi));
+        f[4 * i] = a.x;
+        f[4 * i + 1] = a.y;
+        f[4 * i + 2] = b.x;
+        f[4 * i + 3] = b.y;
+    }
+}
+// Dot product of 16 e4m3 elements of a K row with this lane's 16 q values
+// (fp32), as the chain sacc = fma(k_e, q_e, sacc) from 0.
+__device__ __forceinline__ float dot16_e4m3(uint4 k, const float *qf)
+{
+    float kf[16];
+    e4m3x16_to_f32(k, kf);
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+        s = fmaf(kf[e], qf[e], s);
+    return s;
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -419,13 +452,14 @@ __device__ __forceinline__ void prefetch_first_blocks(const DecodeArgs &a, int64
 // folds that block replaces the row in shared memory with the new V row
 // (vnew_src, this lane's 16-byte slice read at the start) before folding;
 // patch_pos < 0 when there is nothing to patch.
-template <typename T, int LPR>
+template <typename T, int LPR, typename TC = T>
 __device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, const RowInfo &ri,
                                        const int64_t n_keys, const int n_mine, const int c, const int C,
                                        const float2 row_stat, uint8_t *smem, StreamShared &sh, int *err,
                                        const int64_t patch_pos = -1, const T *vnew_src = nullptr)
 {
-    constexpr int N = Vec16<T>::N;
+    constexpr bool F8 = std::is_same<TC, __nv_fp8_e4m3>::value;
+    constexpr int N = F8 ? 16 : Vec16<T>::N; // V elements per lane slice (16 bytes of a V row)
     constexpr int ROW_BYTES = LPR * 16;
     constexpr int KB = kBlockBytes / ROW_BYTES;
     constexpr int HALF = KB / 2;
@@ -516,10 +550,21 @@ __device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, c
             const float *pr = logits + i * KB + hf * HALF;
             auto fold = [&](int r) {
                 const float p = pr[r];
-                const Vec16<T> vv = as_vec<T>(*reinterpret_cast<const uint4 *>(stage + r * ROW_BYTES));
+                if constexpr (F8)
+                {
+                    float vf[16];
+                    e4m3x16_to_f32(*reinterpret_cast<const uint4 *>(stage + r * ROW_BYTES), vf);
 #pragma unroll
-                for (int e = 0; e < N; ++e)
-                    acc[e] = fmaf(p, to_f(vv.v[e]), acc[e]);
+                    for (int e = 0; e < N; ++e)
+                        acc[e] = fmaf(p, vf[e], acc[e]);
+                }
+                else
+                {
+                    const Vec16<T> vv = as_vec<T>(*reinterpret_cast<const uint4 *>(stage + r * ROW_BYTES));
+#pragma unroll
+                    for (int e = 0; e < N; ++e)
+                        acc[e] = fmaf(p, to_f(vv.v[e]), acc[e]);
+                }
             };
             if (valid >= HALF)
             {
@@ -580,6 +625,9 @@ __device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, c
                 sum = make_float4(sum.x + x.x, sum.y + x.y, sum.z + x.z, sum.w + x.w);
             }
         }
+        if constexpr (F8)
+            sum = make_float4(__fmul_rn(sum.x, a.v_scale), __fmul_rn(sum.y, a.v_scale), __fmul_rn(sum.z, a.v_scale),
+                              __fmul_rn(sum.w, a.v_scale));
         T *o = static_cast<T *>(a.qkv) + row * a.hd + 4 * tid;
         o[0] = from_f<T>(sum.x);
         o[1] = from_f<T>(sum.y);
@@ -611,12 +659,16 @@ __device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, c
 // slice of head_dim). Lanes, warps and then the cluster's CTAs are summed in
 // a fixed order (peers push their partial rows into rank 0's shared memory
 // with st.async), so the output does not depend on timing.
-template <typename T, int LPR, bool STEP, bool PV = false>
+template <typename T, int LPR, bool STEP, bool PV = false, typename TC = T>
 __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const StepRowArgs &sa, const int64_t row,
                                                  cg::cluster_group &cluster, uint8_t *smem, StreamShared &sh,
                                                  int *err)
 {
-    constexpr int N = Vec16<T>::N;
+    // TC: the cache element type. fp8 (e4m3) caches hold 16 elements per
+    // 16-byte lane slice; the logits scale includes K's dequantization scale.
+    constexpr bool F8 = std::is_same<TC, __nv_fp8_e4m3>::value;
+    static_assert(!(F8 && STEP), "the fused decode step keeps 16-bit or fp32 caches");
+    constexpr int N = F8 ? 16 : Vec16<T>::N;
     constexpr int ROW_BYTES = LPR * 16;
     constexpr int KB = kBlockBytes / ROW_BYTES; // K rows per block
     constexpr int HALF = KB / 2;                // rows per consumer warp per block
@@ -768,78 +820,103 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
         if (C > 1)
             cluster_arrive_relaxed();
     }
-    else if (STEP && fresh)
-    {
-        // RoPE at pos of this lane's q and k slices; cos/sin shared by both,
-        // from the table (16-byte loads) when it covers the position.
-        constexpr int NPMAX = N;                  // pairs per lane: N (half) or N / 2 (interleaved)
-        const int np = half_pair ? N : N / 2;
-        const int64_t p0 = half_pair ? j0 : i0 / 2; // first pair index
-        float cs[2 * NPMAX];
-        if (sa.table && kv_new <= 4096u && (int64_t)pos < sa.table_pos)
-        {
-            const float4 *t4 = reinterpret_cast<const float4 *>(sa.table + (int64_t)pos * hh + p0);
-#pragma unroll
-            for (int v = 0; v < NPMAX / 2; ++v)
-                if (v < np / 2)
-                {
-                    const float4 t = __ldg(t4 + v);
-                    cs[4 * v] = t.x;
-                    cs[4 * v + 1] = t.y;
-                    cs[4 * v + 2] = t.z;
-                    cs[4 * v + 3] = t.w;
-                }
-        }
-        else
-        {
-#pragma unroll
-            for (int e = 0; e < NPMAX; ++e)
-                if (e < np)
-                    rope_cos_sin_device(p0 + e, a.hd, pos, kv_new, cs[2 * e], cs[2 * e + 1]);
-        }
-        Vec16<T> qo, ko;
-        if (!half_pair)
-        {
-            const Vec16<T> xq = as_vec<T>(qa), xk = as_vec<T>(ka);
-#pragma unroll
-            for (int e = 0; e < N / 2; ++e)
-            {
-                const float cc = cs[2 * e], ss = cs[2 * e + 1];
-                qo.v[2 * e] = from_f<T>(rope_o0(cc, ss, to_f(xq.v[2 * e]), to_f(xq.v[2 * e + 1])));
-                qo.v[2 * e + 1] = from_f<T>(rope_o1(cc, ss, to_f(xq.v[2 * e]), to_f(xq.v[2 * e + 1])));
-                ko.v[2 * e] = from_f<T>(rope_o0(cc, ss, to_f(xk.v[2 * e]), to_f(xk.v[2 * e + 1])));
-                ko.v[2 * e + 1] = from_f<T>(rope_o1(cc, ss, to_f(xk.v[2 * e]), to_f(xk.v[2 * e + 1])));
-            }
-        }
-        else
-        {
-            const bool lo = i0 < hh;
-            const Vec16<T> q0 = as_vec<T>(qa), q1 = as_vec<T>(qb), k0 = as_vec<T>(ka), k1 = as_vec<T>(kb);
-#pragma unroll
-            for (int e = 0; e < N; ++e)
-            {
-                const float cc = cs[2 * e], ss = cs[2 * e + 1];
-                const float qx0 = to_f(q0.v[e]), qx1 = to_f(q1.v[e]), kx0 = to_f(k0.v[e]), kx1 = to_f(k1.v[e]);
-                qo.v[e] = from_f<T>(lo ? rope_o0(cc, ss, qx0, qx1) : rope_o1(cc, ss, qx0, qx1));
-                ko.v[e] = from_f<T>(lo ? rope_o0(cc, ss, kx0, kx1) : rope_o1(cc, ss, kx0, kx1));
-            }
-        }
-#pragma unroll
-        for (int e = 0; e < N; ++e)
-            qf[e] = to_f(qo.v[e]);
-        qraw = as_u4(qo);
-        knew = as_u4(ko);
-        if (c == 0 && warp == 0 && lane < LPR)
-            stg(static_cast<T *>(sa.q_out) + row * a.hd + i0, as_u4(qo));
-    }
     else
     {
-        const T *qrow = static_cast<const T *>(a.q) + row * a.hd;
-        qraw = STEP ? ldg_coherent(qrow + i0) : ldg_keep(qrow + i0);
-        const Vec16<T> qv = as_vec<T>(qraw);
+        bool q_done = false;
+        if constexpr (STEP)
+        {
+            if (fresh)
+            {
+                // RoPE at pos of this lane's q and k slices; cos/sin shared by both,
+                // from the table (16-byte loads) when it covers the position.
+                constexpr int NPMAX = N;                  // pairs per lane: N (half) or N / 2 (interleaved)
+                const int np = half_pair ? N : N / 2;
+                const int64_t p0 = half_pair ? j0 : i0 / 2; // first pair index
+                float cs[2 * NPMAX];
+                if (sa.table && kv_new <= 4096u && (int64_t)pos < sa.table_pos)
+                {
+                    const float4 *t4 = reinterpret_cast<const float4 *>(sa.table + (int64_t)pos * hh + p0);
 #pragma unroll
-        for (int e = 0; e < N; ++e)
-            qf[e] = to_f(qv.v[e]);
+                    for (int v = 0; v < NPMAX / 2; ++v)
+                        if (v < np / 2)
+                        {
+                            const float4 t = __ldg(t4 + v);
+                            cs[4 * v] = t.x;
+                            cs[4 * v + 1] = t.y;
+                            cs[4 * v + 2] = t.z;
+                            cs[4 * v + 3] = t.w;
+                        }
+                }
+                else
+                {
+#pragma unroll
+                    for (int e = 0; e < NPMAX; ++e)
+                        if (e < np)
+                            rope_cos_sin_device(p0 + e, a.hd, pos, kv_new, cs[2 * e], cs[2 * e + 1]);
+                }
+                Vec16<T> qo, ko;
+                if (!half_pair)
+                {
+                    const Vec16<T> xq = as_vec<T>(qa), xk = as_vec<T>(ka);
+#pragma unroll
+                    for (int e = 0; e < N / 2; ++e)
+                    {
+                        const float cc = cs[2 * e], ss = cs[2 * e + 1];
+                        qo.v[2 * e] = from_f<T>(rope_o0(cc, ss, to_f(xq.v[2 * e]), to_f(xq.v[2 * e + 1])));
+                        qo.v[2 * e + 1] = from_f<T>(rope_o1(cc, ss, to_f(xq.v[2 * e]), to_f(xq.v[2 * e + 1])));
+                        ko.v[2 * e] = from_f<T>(rope_o0(cc, ss, to_f(xk.v[2 * e]), to_f(xk.v[2 * e + 1])));
+                        ko.v[2 * e + 1] = from_f<T>(rope_o1(cc, ss, to_f(xk.v[2 * e]), to_f(xk.v[2 * e + 1])));
+                    }
+                }
+                else
+                {
+                    const bool lo = i0 < hh;
+                    const Vec16<T> q0 = as_vec<T>(qa), q1 = as_vec<T>(qb), k0 = as_vec<T>(ka), k1 = as_vec<T>(kb);
+#pragma unroll
+                    for (int e = 0; e < N; ++e)
+                    {
+                        const float cc = cs[2 * e], ss = cs[2 * e + 1];
+                        const float qx0 = to_f(q0.v[e]), qx1 = to_f(q1.v[e]), kx0 = to_f(k0.v[e]), kx1 = to_f(k1.v[e]);
+                        qo.v[e] = from_f<T>(lo ? rope_o0(cc, ss, qx0, qx1) : rope_o1(cc, ss, qx0, qx1));
+                        ko.v[e] = from_f<T>(lo ? rope_o0(cc, ss, kx0, kx1) : rope_o1(cc, ss, kx0, kx1));
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < N; ++e)
+                    qf[e] = to_f(qo.v[e]);
+                qraw = as_u4(qo);
+                knew = as_u4(ko);
+                if (c == 0 && warp == 0 && lane < LPR)
+                    stg(static_cast<T *>(sa.q_out) + row * a.hd + i0, as_u4(qo));
+                q_done = true;
+            }
+        }
+        if (!q_done)
+        {
+            const T *qrow = static_cast<const T *>(a.q) + row * a.hd;
+            if constexpr (F8)
+            {
+                // 16 q values (the lane's slice of the row) as fp32
+                constexpr int QN = Vec16<T>::N;
+#pragma unroll
+                for (int part = 0; part < N / QN; ++part)
+                {
+                    const Vec16<T> qv = as_vec<T>(ldg_keep(qrow + i0 + part * QN));
+#pragma unroll
+                    for (int e = 0; e < QN; ++e)
+                        qf[part * QN + e] = to_f(qv.v[e]);
+                }
+                qraw = make_uint4(0u, 0u, 0u, 0u);
+            }
+            else
+            {
+                qraw = STEP ? ldg_coherent(qrow + i0) : ldg_keep(qrow + i0);
+                const Vec16<T> qv = as_vec<T>(qraw);
+#pragma unroll
+                for (int e = 0; e < N; ++e)
+                    qf[e] = to_f(qv.v[e]);
+            }
+        }
     }
     __syncthreads(); // the ring is initialized; q is ready
 
@@ -916,8 +993,11 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
 #pragma unroll
                 for (int j = 0; j < R; ++j)
                 {
-                    part[j] = dot16<T>(*reinterpret_cast<const uint4 *>(stage + (base + j * RPL) * ROW_BYTES), qraw,
-                                       qf);
+                    const uint4 kraw = *reinterpret_cast<const uint4 *>(stage + (base + j * RPL) * ROW_BYTES);
+                    if constexpr (F8)
+                        part[j] = dot16_e4m3(kraw, qf);
+                    else
+                        part[j] = dot16<T>(kraw, qraw, qf);
                 }
                 int idx;
                 const float dot = multi_reduce<R, LPR>(part, lane, idx);
@@ -1032,7 +1112,7 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                            vsrc);
         }
         else
-            pv_row<T, LPR>(a, row, ri, n_keys, n_mine, c, C, row_stat, smem, sh, err);
+            pv_row<T, LPR, TC>(a, row, ri, n_keys, n_mine, c, C, row_stat, smem, sh, err);
         return;
     }
     if (consumers_any(sh.abort_flag != 0))

@@ -1,6 +1,6 @@
 """Timings of single operators and of the decoder layer on one GPU.
 
-    python -m llama2_b200.microbench {gemm,attention,paged,pv,swiglu,unpad,rope,layer} [--iters N]
+    python -m llama2_b200.microbench {gemm,attention,paged,fp8,pv,swiglu,unpad,rope,layer} [--iters N]
 
 Each prints one line per shape. Kernels are timed with CUDA events on the
 current stream; ``gemm`` times back-to-back launches (compute-bound, L2
@@ -125,6 +125,31 @@ def bench_paged(iters):
             del k, v, kp, vp
 
 
+def bench_fp8(iters):
+    """Fused decode attention over fp8 (e4m3) caches next to bf16 caches of
+    the same shape (7B heads, 4096-position caches, seeded lengths)."""
+    h, s, hd = 32, 4096, 128
+    for b in (1, 16, 64):
+        q = torch.randn(b, h, 1, hd, device="cuda").to(torch.bfloat16)
+        k16 = torch.randn(b, h, s, hd, device="cuda").to(torch.bfloat16)
+        v16 = torch.randn(b, h, s, hd, device="cuda").to(torch.bfloat16)
+        k8 = (k16.float() / 0.25).to(torch.float8_e4m3fn).view(torch.uint8)
+        v8 = (v16.float() / 0.25).to(torch.float8_e4m3fn).view(torch.uint8)
+        lens = torch.randint(1, s, (b,), generator=torch.Generator().manual_seed(1))
+        kv = lens.to(torch.uint32).cuda()
+        mx = torch.tensor([int(lens.max())], dtype=torch.uint32, device="cuda")
+        qk = torch.empty(b, h, 1, s, device="cuda", dtype=torch.bfloat16)
+        out = torch.empty(b, h, 1, hd, device="cuda", dtype=torch.bfloat16)
+        keys = int(lens.sum())
+        n16 = 2 * keys * h * hd * 2 + b * h * int(mx) * 2
+        n8 = 2 * keys * h * hd + b * h * int(mx) * 2
+        t16 = time_ms(lambda: ops.decode_attention(q, k16, v16, kv, mx, qk, out), iters)
+        t8 = time_ms(lambda: ops.decode_attention_fp8(q, k8, v8, 0.25, 0.25, kv, mx, qk, out), iters)
+        print(f"decode attention b={b}: bf16 caches {t16 * 1e3:.1f} us {n16 / t16 / 1e6:.1f} GB/s | "
+              f"fp8 caches {t8 * 1e3:.1f} us {n8 / t8 / 1e6:.1f} GB/s ({t16 / t8:.2f}x)")
+        del k16, v16, k8, v8
+
+
 def bench_pv(iters):
     b, h, qc, s, hd = 8, 32, 2048, 2048, 128
     qk = torch.rand(b, h, qc, s, device="cuda", dtype=torch.bfloat16)
@@ -211,7 +236,7 @@ def bench_layer(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "paged", "pv", "swiglu", "unpad", "rope", "layer"])
+    ap.add_argument("what", choices=["gemm", "attention", "paged", "fp8", "pv", "swiglu", "unpad", "rope", "layer"])
     ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
     torch.manual_seed(0)

@@ -506,6 +506,54 @@ def launch_attention_qkv_paged(qk, v_pages, block_table, kv_lens, qkv, M, N):
               n_pages, kv_lens.data_ptr(), qkv.data_ptr(), b, hq, hkv, qc, hd, int(M), int(N), _code(qk), _stream())
 
 
+def launch_rope_kvcache_fp8_decode(input, is_done, kv_lens, q, k_cache, v_cache, k_scale, v_scale, *, pairing,
+                                   use_table=True):
+    """Decode RoPE + K/V append into fp8 (e4m3) caches k_cache / v_cache:
+    uint8 tensors (B, Hkv, S, hd) holding value / scale rounded to e4m3; q
+    (B, Hq, 1, hd) in the 16-bit activation type of input."""
+    _dev(input, is_done, kv_lens, q, k_cache, v_cache)
+    _same(input, q, "launch_rope_kvcache_fp8_decode")
+    _require(k_cache.dtype == torch.uint8 and v_cache.dtype == torch.uint8, "fp8 caches are uint8 tensors")
+    b, hq, _, hd = q.shape
+    hkv, s = k_cache.shape[1], k_cache.shape[2]
+    _require(tuple(v_cache.shape) == tuple(k_cache.shape) and k_cache.shape[3] == hd and k_cache.shape[0] == b,
+             "Incorrect cache size")
+    _require(input.shape[1] == (hq + 2 * hkv) * hd, "Incorrect embedding dim")
+    table = rope_table(hd, q.device) if use_table else None
+    capi.call("l2k_fused_reshape_rope_kvcache_fp8_decode", input.data_ptr(), is_done.data_ptr(), kv_lens.data_ptr(),
+              q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), float(k_scale), float(v_scale), b, hq, hkv, hd, s,
+              table.data_ptr() if table is not None else None, ROPE_TABLE_POSITIONS if table is not None else 0,
+              int(pairing), _code(q), _stream())
+
+
+def decode_attention_fp8(q, k_cache, v_cache, k_scale, v_scale, kv_lens, max_kv_len, qk, qkv):
+    """decode_attention over fp8 (e4m3, uint8 storage) caches (B, Hkv, S, hd)."""
+    _dev(q, k_cache, v_cache, kv_lens, max_kv_len, qk, qkv)
+    _same(q, qk, "decode_attention_fp8")
+    _same(q, qkv, "decode_attention_fp8")
+    b, hq, _, hd = q.shape
+    hkv, s = k_cache.shape[1], k_cache.shape[2]
+    _require(k_cache.dtype == torch.uint8 and tuple(v_cache.shape) == tuple(k_cache.shape), "Incorrect caches")
+    _require(tuple(qk.shape) == (b, hq, 1, s) and tuple(qkv.shape) == (b, hq, 1, hd), "Incorrect qk / qkv size")
+    capi.call("l2k_decode_attention_fp8", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), float(k_scale),
+              float(v_scale), kv_lens.data_ptr(), max_kv_len.data_ptr(), qk.data_ptr(), qkv.data_ptr(), b, hq, hkv, s,
+              hd, _code(q), _stream())
+
+
+def decode_attention_fp8_paged(q, k_pages, v_pages, k_scale, v_scale, block_table, kv_lens, max_kv_len, qk, qkv):
+    """decode_attention_fp8 over page pools (num_pages, Hkv, 16384 / hd, hd) of e4m3 bytes."""
+    _dev(q, k_pages, v_pages, block_table, kv_lens, max_kv_len, qk, qkv)
+    _u32(block_table, "block_table")
+    b, hq, _, hd = q.shape
+    n_pages, hkv, rows, _ = k_pages.shape
+    max_pages = block_table.shape[1]
+    _require(rows == 16384 // hd and k_pages.dtype == torch.uint8, "pages must be uint8 (num_pages, Hkv, 16384/hd, hd)")
+    _require(tuple(qk.shape) == (b, hq, 1, max_pages * rows), "Incorrect qk size")
+    capi.call("l2k_decode_attention_fp8_paged", q.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(), float(k_scale),
+              float(v_scale), block_table.data_ptr(), max_pages, n_pages, kv_lens.data_ptr(), max_kv_len.data_ptr(),
+              qk.data_ptr(), qkv.data_ptr(), b, hq, hkv, hd, _code(q), _stream())
+
+
 def prefill_attention_scores(q, k, q_lens, kv_lens, max_q_len, max_kv_len, qk):
     """Fused QK^T + scale + causal mask + softmax for q_len query rows per sequence."""
     _dev(q, k, q_lens, kv_lens, qk)

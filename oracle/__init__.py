@@ -244,6 +244,23 @@ class port:
         return out
 
     @staticmethod
+    def e4m3_from_f32(x, scale):
+        """Bytes of x / scale (x * float32(1 / scale)) rounded to e4m3, saturating."""
+        x = f32(x)
+        inv = np.float32(1.0) / np.float32(scale)
+        out = np.empty(x.shape, np.uint8)
+        port_lib().orc_e4m3_from_f32(_ptr(x), _i64(x.size), ctypes.c_float(inv), _ptr(out))
+        return out
+
+    @staticmethod
+    def e4m3_to_f32(b, scale):
+        """The values scale * e4m3(b) of a uint8 array."""
+        b = u8(b)
+        out = np.empty(b.shape, np.float32)
+        port_lib().orc_e4m3_to_f32(_ptr(b), _i64(b.size), ctypes.c_float(scale), _ptr(out))
+        return out
+
+    @staticmethod
     def attention_qkv(qk, v, m, n, qkv):
         """In place on qkv (B, Hq, Qc, hd) float32: rows < m, keys < n."""
         qk, v = f32(qk), f32(v)

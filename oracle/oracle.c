@@ -481,3 +481,67 @@ void orc_attention_qkv(const float *qk, const float *v, int64_t batch, int64_t q
             }
         }
 }
+
+/* ------------------------------------------------------------------------
+ * fp8 (e4m3) cache elements — no counterpart in the reference (its DataType
+ * stops at FP32/FP16/INT8, include/common/types.h:60-71). The format is the
+ * OCP 8-bit floating point "E4M3": sign bit, 4 exponent bits with bias 7,
+ * 3 mantissa bits, no infinities, largest finite magnitude 448 = 1.75 * 2^8,
+ * smallest normal 2^-6, subnormals m * 2^-9 (m = 1..7), NaN = S.1111.111.
+ *
+ * orc_e4m3_from_f32: y = x * inv_scale (one fp32 multiply), then y rounded
+ *   to the nearest e4m3 value, ties to an even mantissa; magnitudes above
+ *   448 saturate to 448 (the saturating conversion the cache writers use);
+ *   NaN -> 0x7F.
+ * orc_e4m3_to_f32: the exact value of each byte, times scale (fp32).
+ * ------------------------------------------------------------------------ */
+static uint8_t orc_e4m3_round(float y)
+{
+    if (y != y)
+        return 0x7F;
+    const uint8_t sign = (uint8_t)(signbit(y) ? 0x80 : 0x00);
+    double a = fabs((double)y);
+    if (a >= 448.0)
+        return (uint8_t)(sign | 0x7E);
+    if (a < 0.015625) /* below 2^-6: subnormal multiples of 2^-9 (8 * 2^-9 is the smallest normal) */
+    {
+        const double m = nearbyint(a * 512.0); /* default rounding mode: to nearest, ties to even */
+        return (uint8_t)(sign | (uint8_t)m);
+    }
+    int e2;
+    const double f = frexp(a, &e2); /* a = f * 2^e2, f in [0.5, 1) */
+    int e = e2 - 1;                 /* a = (2 f) * 2^e, 2 f in [1, 2) */
+    double q = nearbyint((2.0 * f - 1.0) * 8.0);
+    if (q == 8.0)
+    {
+        q = 0.0;
+        ++e;
+    }
+    if (e > 8 || (e == 8 && q == 7.0)) /* 480 is not finite in e4m3: saturate */
+        return (uint8_t)(sign | 0x7E);
+    return (uint8_t)(sign | (uint8_t)((e + 7) << 3) | (uint8_t)q);
+}
+
+void orc_e4m3_from_f32(const float *x, int64_t n, float inv_scale, uint8_t *out)
+{
+    for (int64_t i = 0; i < n; ++i)
+    {
+        const float y = x[i] * inv_scale;
+        out[i] = orc_e4m3_round(y);
+    }
+}
+
+static float orc_e4m3_value(uint8_t b)
+{
+    const int e = (b >> 3) & 0xF, m = b & 7;
+    if (e == 0xF && m == 7)
+        return NAN;
+    const double mag = e == 0 ? ldexp((double)m, -9) : ldexp(1.0 + m / 8.0, e - 7);
+    return (float)((b & 0x80) ? -mag : mag);
+}
+
+void orc_e4m3_to_f32(const uint8_t *x, int64_t n, float scale, float *out)
+{
+    for (int64_t i = 0; i < n; ++i)
+        out[i] = orc_e4m3_value(x[i]) * scale;
+}

@@ -150,3 +150,25 @@ def test_attention_qkv(case):
     got = np.full_like(a["qkv"], -7.0)
     port.attention_qkv(a["qk"], a["v"], p["m"], p["n"], got)
     assert _bits_equal(got, a["qkv"])
+
+
+def test_e4m3_oracle_rounding():
+    """The oracle's e4m3 rounding (round to nearest even, saturating) against
+    torch's float8_e4m3fn conversion on in-range values (normals, subnormals,
+    ties), and its exact decoding of every byte."""
+    import torch
+
+    from oracle import port
+
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal(100000) * np.exp(rng.uniform(-14, 6, 100000))).astype(np.float32)
+    ties = np.array([m * 2.0 ** -9 for m in np.arange(0.5, 8, 1.0)] + [1.0625, 1.1875, 240.0, 416.0], np.float32)
+    for scale in (1.0, 0.37, 3.1):
+        inv = np.float32(1) / np.float32(scale)
+        xs = np.concatenate([x[np.abs(x * inv) < 448], ties * np.float32(scale)])
+        want = torch.from_numpy(xs * inv).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+        assert np.array_equal(port.e4m3_from_f32(xs, scale), want)
+    assert port.e4m3_from_f32(np.array([500.0, -1e6, 448.0], np.float32), 1.0).tolist() == [0x7E, 0xFE, 0x7E]
+    vals = port.e4m3_to_f32(np.arange(256, dtype=np.uint8), 1.0)
+    want = torch.arange(256, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(np.isnan(vals), np.isnan(want)) and np.array_equal(vals[~np.isnan(vals)], want[~np.isnan(want)])
