@@ -222,6 +222,31 @@ __device__ __forceinline__ float dot16_e4m3(uint4 k, const float *qf)
     return s;
 }
 
+// The same dot product with q held as 8 f16 pairs (exact conversions of the
+// q values, see score_row_stream): each e4m3 pair widens to an f16 pair and
+// each element is the sm_100 mixed-precision fma (f16 operands, fp32
+// accumulate), which rounds k*q+s once as fmaf does on the widened values —
+// so the result equals dot16_e4m3's bit for bit, at fewer instructions.
+__device__ __forceinline__ float dot16_e4m3_h(uint4 k, const uint32_t (&qh)[8])
+{
+    const uint32_t w[4] = {k.x, k.y, k.z, k.w};
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] & 0xFFFFu), __NV_E4M3);
+        const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> 16), __NV_E4M3);
+        const uint32_t k0 = (uint32_t)lo.x | ((uint32_t)lo.y << 16), k1 = (uint32_t)hi.x | ((uint32_t)hi.y << 16);
+        asm("{\n\t.reg .b16 a0, a1, b0, b1, c0, c1, d0, d1;\n\t"
+            "mov.b32 {a0, a1}, %1;\n\tmov.b32 {b0, b1}, %2;\n\tmov.b32 {c0, c1}, %3;\n\tmov.b32 {d0, d1}, %4;\n\t"
+            "fma.rn.f32.f16 %0, a0, b0, %0;\n\tfma.rn.f32.f16 %0, a1, b1, %0;\n\t"
+            "fma.rn.f32.f16 %0, c0, d0, %0;\n\tfma.rn.f32.f16 %0, c1, d1, %0;\n\t}"
+            : "+f"(s)
+            : "r"(k0), "r"(qh[2 * i]), "r"(k1), "r"(qh[2 * i + 1]));
+    }
+    return s;
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 // Bounded wait on an mbarrier phase: false after ~2 s.
@@ -796,6 +821,8 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
 
     int n_issued = 0; // producer lane only
     float qf[N];
+    uint32_t qh[8] = {};  // F8: this lane's q slice as f16 pairs (when q_f16)
+    bool q_f16 = false;
     uint4 qraw;                              // the same slice as stored (16-bit types: the mixed fma's operand)
     uint4 knew = make_uint4(0u, 0u, 0u, 0u); // STEP and fresh: this lane's slice of the rotated new K row
     if (warp == kCW)
@@ -907,6 +934,25 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                         qf[part * QN + e] = to_f(qv.v[e]);
                 }
                 qraw = make_uint4(0u, 0u, 0u, 0u);
+                if constexpr (F8)
+                {
+                    // q as f16 pairs when every value of the slice converts exactly
+                    // (zero, or a normal f16 magnitude and no more than 11
+                    // significant bits, which 16-bit q always has); otherwise the
+                    // fp32 dot product is used.
+                    bool exact = true;
+#pragma unroll
+                    for (int e = 0; e < 16; e += 2)
+                    {
+                        const __half2 h = __floats2half2_rn(qf[e], qf[e + 1]);
+                        const float2 back = __half22float2(h);
+                        exact = exact && back.x == qf[e] && back.y == qf[e + 1] &&
+                                (qf[e] == 0.f || fabsf(qf[e]) >= 6.103515625e-05f) &&
+                                (qf[e + 1] == 0.f || fabsf(qf[e + 1]) >= 6.103515625e-05f);
+                        qh[e / 2] = *reinterpret_cast<const uint32_t *>(&h);
+                    }
+                    q_f16 = exact;
+                }
             }
             else
             {
@@ -995,7 +1041,7 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                 {
                     const uint4 kraw = *reinterpret_cast<const uint4 *>(stage + (base + j * RPL) * ROW_BYTES);
                     if constexpr (F8)
-                        part[j] = dot16_e4m3(kraw, qf);
+                        part[j] = q_f16 ? dot16_e4m3_h(kraw, qh) : dot16_e4m3(kraw, qf);
                     else
                         part[j] = dot16<T>(kraw, qraw, qf);
                 }

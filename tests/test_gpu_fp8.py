@@ -155,3 +155,30 @@ def test_fp8_rejects_bad_arguments():
     with pytest.raises(capi.L2KError):   # scale must be positive
         ops.decode_attention_fp8(q[..., :64].contiguous(), k[..., :64].contiguous(), k[..., :64].contiguous(), 0.0,
                                  1.0, kv, kv, qk, o[..., :64].contiguous())
+
+
+def test_fp8_attention_q_values_outside_the_f16_range():
+    """The K dot product takes q as f16 pairs only when every value of a
+    lane's slice converts exactly; slices holding values below the normal f16
+    range or above its largest value take the fp32 path. Both against the
+    oracle."""
+    b, hq, hkv, hd = 1, 4, 1, 128
+    s, n = 512, 300
+    r = ochain.rounder("bf16")
+    k8 = _cache_bytes((b, hkv, s, hd), 0.002, 13)
+    v8 = _cache_bytes((b, hkv, s, hd), 0.5, 14)
+    q = np.random.default_rng(15).standard_normal((b, hq, 1, hd), dtype=np.float32) * 0.01
+    q[0, 1, 0, 3] = 3e-6          # below the normal f16 range
+    q[0, 2, 0, 70] = 9.0e4        # above the largest f16 value
+    q[0, 3, 0, :] = 0.0           # all zero: uniform probabilities
+    q = r(q)
+    qk = torch.zeros(b, hq, 1, s, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(b, hq, 1, hd, dtype=torch.bfloat16, device="cuda")
+    kv = torch.tensor([n], dtype=torch.uint32, device="cuda")
+    ops.decode_attention_fp8(torch.from_numpy(q).cuda().to(torch.bfloat16), torch.from_numpy(k8).cuda(),
+                             torch.from_numpy(v8).cuda(), 0.002, 0.5, kv, kv, qk, out)
+    torch.cuda.synchronize()
+    for h in range(hq):
+        kd = port.e4m3_to_f32(k8[0, 0, :n], 0.002)
+        want = ochain.score_row(q[0, h, 0], kd, n - 1, hd)
+        assert max_rel_err(host(qk)[0, h, 0, :n], r(want)) <= 1e-2, h
