@@ -15,11 +15,14 @@
 // block into TMEM. The tensor maps bound rows at M, columns at N and k at K,
 // so partial tiles read zeros. Two warps per TMEM lane quadrant (32 rows)
 // read the accumulator, each taking half of the rows' 32-column chunks.
-// Three shapes:
-//   * more than 128 rows (prefill): the persistent kernel below, one CTA per
-//     SM over 128 x 256 tiles, a 4-stage ring of 48 KB, two TMEM
-//     accumulators so the epilogue warps drain one tile while the next one's
-//     MMAs run;
+// Four shapes:
+//   * at least 256 rows (prefill): the two-SM kernel below, clusters of two
+//     CTAs computing 256 x 256 tiles with tcgen05.mma.cta_group::2, each SM
+//     holding half of the A and half of the B tile (32 KB per 64-k step in a
+//     6-stage ring), two TMEM accumulators per CTA;
+//   * 129 to 255 rows: the persistent kernel below, one CTA per SM over
+//     128 x 256 tiles, a 4-stage ring of 48 KB, two TMEM accumulators so the
+//     epilogue warps drain one tile while the next one's MMAs run;
 //   * one row tile (M <= 128: decode batches, bound by reading B) with at
 //     most one 128-column tile per SM: 128 x 128 tiles with K split over a
 //     thread-block cluster of up to 8 CTAs that reduce their fp32 rows into
@@ -874,6 +877,271 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
 }
 
+// Two-SM variant for products of at least 256 rows: a cluster of two CTAs
+// (one per SM) computes 256 x 256 tiles with tcgen05.mma.cta_group::2
+// (M = 256, N = 256): CTA rank r holds rows [128 r, 128 r + 128) of the A
+// tile and op(B) columns [128 r, 128 r + 128) of the B tile in its shared
+// memory, at the same offsets, and receives rows [128 r, 128 r + 128) of the
+// 256 x 256 accumulator in its tensor memory. Per 64-k step each SM loads
+// 16 KB of A and 16 KB of B (the one-SM 128 x 256 tile loads 16 + 32 KB for
+// the same work per SM). Roles: warp 0 of each CTA streams its halves
+// through a 6-stage ring, the loads completing on rank 0's "full" barrier;
+// warp 1 of rank 0 issues the MMAs and commits to both CTAs' "empty" and
+// "accumulator full" barriers (tcgen05.commit multicast); warps 2-9 of each
+// CTA run the epilogue of their 128 rows and release the accumulator on
+// rank 0's "accumulator empty" barrier. The cluster walks the tiles
+// persistently; the two accumulators double-buffer the epilogue.
+constexpr int kQStages = 6;
+constexpr int kQBN = 256;                          // N of the pair's MMA (B columns per tile)
+constexpr uint32_t kQBHalf = 128 * 128;            // one CTA's B half: 128 columns x 64 k
+constexpr uint32_t kQStageBytes = kABox + kQBHalf; // 32 KB
+constexpr uint32_t kQOffBar = kQStages * kQStageBytes;
+constexpr uint32_t kQOffMisc = kQOffBar + 256;
+constexpr uint32_t kQSmemBytes = kQOffMisc + 64;
+
+__device__ __forceinline__ uint32_t cluster_rank0_addr(uint32_t local)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(local));
+    return r;
+}
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, int z,
+                                                 uint32_t bar_cluster)
+{
+    asm volatile("cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+                 "{%2, %3, %4}], [%5];" ::"r"(dst),
+                 "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar_cluster)
+                 : "memory");
+}
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                             uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+                 "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+// Arrives on the mbarrier at `bar` (same offset) in both CTAs of the pair once
+// the MMAs issued so far have completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::
+                     "r"(bar),
+                 "h"((uint16_t)3)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// kind::f16 for the pair: D f32, A K-major, B K-major (0) or MN-major (1), M = 256, N = 256.
+__host__ __device__ constexpr uint32_t pair_instr_desc(uint32_t ab_format, uint32_t b_mn)
+{
+    return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (b_mn << 16) | ((uint32_t)(kQBN >> 3) << 17) |
+           ((uint32_t)(256 >> 4) << 24);
+}
+
+template <typename T, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kPThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        const __grid_constant__ GemmTcArgs a)
+{
+    constexpr int BN = kQBN;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t sbase = smem_u32(smem);
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    const bool leader = rank == 0;
+    const uint32_t bar_full = sbase + kQOffBar;             // + 8 * stage (rank 0's are the live ones)
+    const uint32_t bar_empty = bar_full + 8 * kQStages;     // + 8 * stage
+    const uint32_t bar_acc_full = bar_empty + 8 * kQStages; // + 8 * accumulator
+    const uint32_t bar_acc_empty = bar_acc_full + 16;       // + 8 * accumulator (rank 0's are the live ones)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kQOffMisc);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kQOffMisc + 8);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t n_tiles = (int64_t)((a.m + 255) / 256) * a.n_nt;
+    const int64_t cluster_id = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+    const int n_kb = a.n_kb;
+    const bool misaligned = (sbase & 1023u) != 0; // uniform over the cluster (same layout); checked after the sync
+
+    if (tid == 0)
+    {
+        for (int i = 0; i < kQStages; ++i)
+        {
+            mbar_init(bar_full + 8 * i, 1);
+            mbar_init(bar_empty + 8 * i, 1);
+        }
+        for (int b = 0; b < 2; ++b)
+        {
+            mbar_init(bar_acc_full + 8 * b, 1);
+            mbar_init(bar_acc_empty + 8 * b, 2 * 4 * kEpiParts); // both CTAs' epilogue warps
+        }
+        *abort_flag = misaligned ? 1 : 0;
+        if (misaligned)
+            atomicCAS(&g_gemm_error, 0, ERR_GEMM_SMEM_ALIGN);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1)
+    {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(2 * BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    cluster_sync_all(); // both CTAs' barriers are initialized and the tensor memory allocated
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t full0 = cluster_rank0_addr(bar_full);          // rank 0's full barriers
+    const uint32_t acc_empty0 = cluster_rank0_addr(bar_acc_empty); // rank 0's accumulator-empty barriers
+
+    int64_t issued = 0;    // producer: k blocks whose loads were issued
+    int64_t mma_done = -1; // rank 0's MMA thread: the last k block whose MMAs were committed
+    if (warp == 0)
+    {
+        if (lane == 0 && !*abort_flag)
+        {
+            int64_t it = 0;
+            for (int64_t tile = cluster_id; tile < n_tiles && !*abort_flag; tile += n_clusters)
+            {
+                const int row0 = (int)(tile / a.n_nt) * 256 + 128 * (int)rank;
+                const int col0 = (int)(tile % a.n_nt) * BN;
+                for (int kb = 0; kb < n_kb; ++kb, ++it)
+                {
+                    const int st = (int)(it % kQStages);
+                    if (it >= kQStages && !mbar_wait(bar_empty + 8 * st, (uint32_t)((it / kQStages) - 1) & 1u,
+                                                     abort_flag))
+                    {
+                        gemm_fail(ERR_GEMM_WAIT_MMA, abort_flag);
+                        break;
+                    }
+                    const uint32_t dst = sbase + st * kQStageBytes;
+                    const uint32_t bar = full0 + 8 * st;
+                    if (leader)
+                        mbar_expect_tx(bar_full + 8 * st, 2 * kQStageBytes); // both CTAs' halves
+                    const int kx = kb * BK;
+                    tma_load_3d_pair(dst, &tm_a, kx, row0, 0, bar);
+                    if constexpr (B_MN)
+                    {
+#pragma unroll
+                        for (int hh = 0; hh < 2; ++hh)
+                        {
+                            const int h = 2 * (int)rank + hh; // 64-column chunk of the 256-column tile
+                            const int64_t cx = EPI == EPI_SWIGLU && h >= 2 ? a.up_col + col0 / 2 + 64 * (h - 2)
+                                                                           : (EPI == EPI_SWIGLU ? col0 / 2 : col0) + 64 * h;
+                            tma_load_3d_pair(dst + kABox + hh * BK * 128, &tm_b, (int)cx, kx, 0, bar);
+                        }
+                    }
+                    else
+                    {
+                        const int64_t cy = EPI == EPI_SWIGLU ? (rank ? a.up_col + col0 / 2 : col0 / 2)
+                                                             : col0 + 128 * (int64_t)rank;
+                        tma_load_3d_pair(dst + kABox, &tm_b, kx, (int)cy, 0, bar);
+                    }
+                    issued = it + 1;
+                }
+            }
+        }
+    }
+    else if (warp == 1)
+    {
+        if (leader && lane == 0 && !*abort_flag)
+        {
+            const uint32_t idesc =
+                pair_instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u, B_MN ? 1u : 0u);
+            int64_t it = 0, lt = 0;
+            for (int64_t tile = cluster_id; tile < n_tiles && !*abort_flag; tile += n_clusters, ++lt)
+            {
+                const int buf = (int)(lt & 1);
+                if (lt >= 2 && !mbar_wait(bar_acc_empty + 8 * buf, (uint32_t)((lt >> 1) - 1) & 1u, abort_flag))
+                {
+                    gemm_fail(ERR_GEMM_WAIT_DONE, abort_flag);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(buf * BN);
+                for (int kb = 0; kb < n_kb; ++kb, ++it)
+                {
+                    const int st = (int)(it % kQStages);
+                    if (!mbar_wait(bar_full + 8 * st, (uint32_t)(it / kQStages) & 1u, abort_flag))
+                    {
+                        gemm_fail(ERR_GEMM_WAIT_LOAD, abort_flag);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t pa = sbase + st * kQStageBytes, pb = pa + kABox;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                    {
+                        const uint64_t bd = B_MN ? desc_mn(pb + 2048u * k) : smem_desc(pb + 32u * k);
+                        mma_f16_pair(acc, smem_desc(pa + 32u * k), bd, idesc, (kb | k) ? 1u : 0u);
+                    }
+                    mma_commit_pair(bar_empty + 8 * st); // both CTAs may refill the stage
+                    mma_done = it;
+                }
+                if (*abort_flag)
+                    break;
+                mma_commit_pair(bar_acc_full + 8 * buf);
+            }
+        }
+    }
+    else
+    {
+        // epilogue warps 2..: TMEM lane quadrant warp % 4 holds rows 32 (warp % 4) + lane of this CTA's half
+        const int quad = warp & 3, part = (warp - 2) >> 2;
+        const bool wide = a.wide != 0;
+        int64_t lt = 0;
+        for (int64_t tile = cluster_id; tile < n_tiles && !*abort_flag; tile += n_clusters, ++lt)
+        {
+            const int buf = (int)(lt & 1);
+            const int64_t row = (tile / a.n_nt) * 256 + 128 * (int64_t)rank + 32 * quad + lane;
+            const int64_t ocol0 = (tile % a.n_nt) * (int64_t)(EPI == EPI_SWIGLU ? BN / 2 : BN);
+            const bool store = row < a.m;
+            RopeTok tok{false, 0, 0, 0u, 0u};
+            if constexpr (EPI == EPI_ROPE)
+                tok = rope_token(a.rope, row, store);
+            if (!mbar_wait(bar_acc_full + 8 * buf, (uint32_t)(lt >> 1) & 1u, abort_flag))
+            {
+                gemm_fail(ERR_GEMM_WAIT_DONE, abort_flag);
+                break;
+            }
+            tc_fence_after();
+            __syncwarp();
+            tile_epilogue<T, BN, false, EPI>(a, tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * quad) << 16), row,
+                                             store, wide, ocol0, nullptr, 0, 1, tok, part, kEpiParts);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive_cluster(acc_empty0 + 8 * buf);
+        }
+    }
+
+    // -------- teardown: after a failure, copies and MMAs in flight land first --------
+    if (*abort_flag)
+    {
+        const int quiet = 0;
+        if (tid == 32 && leader && mma_done >= 0)
+            mbar_wait(bar_empty + 8 * (int)(mma_done % kQStages), (uint32_t)(mma_done / kQStages) & 1u, &quiet);
+        if (tid == 0 && leader)
+            for (int64_t it = std::max<int64_t>(0, issued - kQStages); it < issued; ++it)
+                mbar_wait(bar_full + 8 * (int)(it % kQStages), (uint32_t)(it / kQStages) & 1u, &quiet);
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync_all(); // no CTA leaves while its peer may still signal its barriers or read its tensor memory
+    if (warp == 1)
+    {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+    }
+}
+
 // One GEMM and its epilogue: A (m x k, row stride lda), B (row stride ldb)
 // whose op(B) has nb columns, and the kernel arguments the caller fills (c,
 // ldc, n, up_col, rope).
@@ -926,6 +1194,52 @@ int launch_gemm_persistent(const GemmProblem &p, cudaStream_t stream)
     return check_launch("l2k_linear (tcgen05, persistent)");
 }
 
+// The two-SM kernel: 256 x 256 tiles over clusters of two CTAs.
+template <typename T, bool B_MN, int EPI>
+int launch_gemm_pair(const GemmProblem &p, cudaStream_t stream)
+{
+    const CUtensorMapDataType dt =
+        std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t m = (uint64_t)p.m, nb = (uint64_t)p.nb, k = (uint64_t)p.k;
+    const uint64_t lda = (uint64_t)p.lda, ldb = (uint64_t)p.ldb;
+    CUtensorMap ma, mb;
+    bool ok = make_map(&ma, dt, p.a, k, m, 1, lda * 2, lda * 2 * m, BM, BK);
+    if (B_MN) // B stored K x N: boxes of 64 k rows x 64 columns
+        ok = ok && make_map(&mb, dt, p.b, nb, k, 1, ldb * 2, ldb * 2 * k, BK, 64);
+    else // B stored N x K: each CTA's half, 128 n rows x 64 k
+        ok = ok && make_map(&mb, dt, p.b, k, nb, 1, ldb * 2, ldb * 2 * nb, 128, BK);
+    if (!ok)
+        return set_error(L2K_ERR_CUDA, "l2k_linear: tensor map encoding failed");
+    GemmTcArgs a = p.args;
+    a.m = p.m;
+    a.n_kb = (int)ceil_div(p.k, BK);
+    a.n_nt = (int)ceil_div(a.n, EPI == EPI_SWIGLU ? kQBN / 2 : kQBN);
+    a.wide = EPI != EPI_ROPE && (a.ldc * 2) % 16 == 0 && is_aligned(a.c, 16) ? 1 : 0;
+    a.split = 1;
+    auto kernel = gemm_tc_pair_kernel<T, B_MN, EPI>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kQSmemBytes);
+    if (e != cudaSuccess)
+        return set_error(L2K_ERR_CUDA, "l2k_linear: %s", cudaGetErrorString(e));
+    const int64_t tiles = ceil_div(p.m, 256) * a.n_nt;
+    const int64_t clusters = std::min<int64_t>(tiles, num_sms() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * clusters));
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = kQSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, a);
+    if (e != cudaSuccess)
+        return set_error(L2K_ERR_CUDA, "l2k_linear (two-SM tiles): %s", cudaGetErrorString(e));
+    return check_launch("l2k_linear (tcgen05, two-SM tiles)");
+}
+
 template <typename T, bool B_MN, int BN, int STAGES, bool SPLIT, int EPI>
 int launch_gemm_tc(const GemmProblem &p, cudaStream_t stream, int split)
 {
@@ -973,6 +1287,8 @@ int launch_gemm_tc(const GemmProblem &p, cudaStream_t stream, int split)
 template <typename T, bool B_MN, int EPI>
 int launch_tiles(const GemmProblem &p, cudaStream_t stream)
 {
+    if (p.m >= 2 * BM)
+        return launch_gemm_pair<T, B_MN, EPI>(p, stream);
     if (p.m > BM)
         return launch_gemm_persistent<T, B_MN, EPI>(p, stream);
     const int64_t tiles = ceil_div(p.nb, 128), n_kb = ceil_div(p.k, BK);

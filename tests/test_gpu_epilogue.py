@@ -164,6 +164,7 @@ def _prefill_case(dtype, q_lens_h, cached_h, qc, s, hq, hkv, hd, dim, seed):
 @pytest.mark.parametrize("dtype,q_lens_h,cached_h,pairing", [
     (torch.bfloat16, [100, 37, 1], [0, 20, 60], 1),   # 138 token rows: 128 x 256 tiles
     (torch.float16, [64, 40], [0, 10], 0),            # 104 rows: one row tile, k split over a cluster
+    (torch.bfloat16, [128, 100, 90], [0, 20, 60], 1), # 318 rows: 256 x 256 tiles over CTA pairs
 ])
 def test_linear_rope_prefill_bit_identical_to_linear_then_rope(dtype, q_lens_h, cached_h, pairing):
     hq, hkv, hd, dim, qc, s = 8, 4, 128, 512, 128, 256
