@@ -16,8 +16,7 @@ events), and value = tokens of all ranks / that time. Two ways to split:
 
   default        weak scaling: every rank holds its own batch of the
                  workload's size (its own activations and cache, the same
-                 multiset of sequence lengths in a rank-permuted order, so
-                 the ranks' work is equal);
+                 sequence lengths as rank 0, so the ranks' work is equal);
   --shard ORDER  strong scaling: one global seeded batch of the workload's
                  size is split by sequence over the ranks (ORDER contiguous:
                  rank r takes sequences [r*B/N, (r+1)*B/N); balanced: sorted
@@ -197,8 +196,8 @@ def bench_config(w_job, args, n_gpus):
             "global_batch": per_gpu * n_gpus, "batch_per_gpu": per_gpu, "prefill_len": w_job.prefill_len,
             "attention_output": bool(args.attention),
             "parallelism": (f"sequence-batch shards x{n_gpus}: one global batch split {args.shard} by sequence"
-                            if shard else f"sequence-batch shards x{n_gpus}: a batch of its own per GPU, same "
-                                          f"multiset of lengths on every rank"),
+                            if shard else f"sequence-batch shards x{n_gpus}: a batch of its own per GPU, the "
+                                          f"same lengths on every rank"),
             "positions": f"uniform in [{w_job.pos_lo}, {w_job.pos_hi}], seed 0" if w_job.decode
                          else "fresh prefill",
             "l2": flush}

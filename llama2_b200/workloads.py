@@ -73,10 +73,9 @@ def host_inputs(w: Workload, seed: int = 0, rank: int = 0, kv_cache: bool = True
     Prefill: a fresh prefill (kv_lens = 0 before the update, q_lens = prefill_len).
 
     Every rank draws its own activations, ids and cache from the seed
-    sequence [seed, rank]. The positions of rank r > 0 are a rank-seeded
-    permutation of rank 0's draw (`rank_positions`), so the ranks of a
-    weak-scaling job hold different sequences with the same multiset of
-    lengths: equal work per rank, as with statistically identical shards.
+    sequence [seed, rank]. The positions of rank r > 0 are rank 0's draw
+    (`rank_positions`), so the ranks of a weak-scaling job hold different
+    sequences with the same lengths in the same order: equal work per rank.
     """
     rng = np.random.default_rng([seed, rank])
     d, h, hd, f, s = w.dim, w.heads, w.head_dim, w.hidden, w.kv_cache_len
@@ -107,9 +106,10 @@ def host_inputs(w: Workload, seed: int = 0, rank: int = 0, kv_cache: bool = True
 
 def rank_positions(w: Workload, seed: int, rank: int) -> np.ndarray:
     """Rank 0's seeded positions (the same draw host_inputs makes for rank 0,
-    replayed from its seed sequence), permuted by a generator seeded with
-    [seed, rank, 1]. Every rank of a weak-scaling job thus holds the same
-    multiset of sequence lengths in a different order."""
+    replayed from its seed sequence). Every rank of a weak-scaling job thus
+    holds sequences of the same lengths in the same order (the fused step
+    schedules its rows in sequence order, so a reordering alone moves a
+    rank's time by a few per cent)."""
     rng = np.random.default_rng([seed, 0])
     d, f, t = w.dim, w.hidden, w.tokens
     # replay rank 0's draws up to its positions (same order and sizes as host_inputs)
@@ -118,8 +118,7 @@ def rank_positions(w: Workload, seed: int, rank: int) -> np.ndarray:
     rng.integers(0, w.vocab, t, dtype=np.uint32)
     rng.standard_normal((t, 3 * d), dtype=np.float32)
     rng.standard_normal((t, 2 * f), dtype=np.float32)
-    base = rng.integers(w.pos_lo, w.pos_hi + 1, w.batch, dtype=np.uint32)
-    return base[np.random.default_rng([seed, rank, 1]).permutation(w.batch)]
+    return rng.integers(w.pos_lo, w.pos_hi + 1, w.batch, dtype=np.uint32)
 
 
 def shard_rows(positions, world: int, rank: int, order: str = "contiguous") -> np.ndarray:
