@@ -53,10 +53,11 @@ def time_ms(fn, iters: int, flush: bool = True) -> float:
     return total / iters
 
 
-def bench_gemm(iters):
-    for (m, n, k) in [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 12288, 4096), (16384, 4096, 4096),
-                      (64, 12288, 4096), (1, 12288, 4096)]:
-        for trans_b in (0, 1):
+def bench_gemm(iters, shape=None):
+    shapes = [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 12288, 4096), (16384, 4096, 4096),
+              (64, 12288, 4096), (1, 12288, 4096)]
+    for (m, n, k) in ([shape] if shape else shapes):
+        for trans_b in ((0,) if shape else (0, 1)):
             a = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
             b = (torch.randn(n, k, device="cuda", dtype=torch.bfloat16) if trans_b
                  else torch.randn(k, n, device="cuda", dtype=torch.bfloat16))
@@ -125,11 +126,11 @@ def bench_paged(iters):
             del k, v, kp, vp
 
 
-def bench_fp8(iters):
+def bench_fp8(iters, batch=None):
     """Fused decode attention over fp8 (e4m3) caches next to bf16 caches of
     the same shape (7B heads, 4096-position caches, seeded lengths)."""
     h, s, hd = 32, 4096, 128
-    for b in (1, 16, 64):
+    for b in ([batch] if batch else (1, 16, 64)):
         q = torch.randn(b, h, 1, hd, device="cuda").to(torch.bfloat16)
         k16 = torch.randn(b, h, s, hd, device="cuda").to(torch.bfloat16)
         v16 = torch.randn(b, h, s, hd, device="cuda").to(torch.bfloat16)
@@ -238,9 +239,16 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm", "attention", "paged", "fp8", "pv", "swiglu", "unpad", "rope", "layer"])
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--shape", default="", help="gemm: one M,N,K product (B stored K x N) instead of the set")
+    ap.add_argument("--batch", type=int, default=0, help="fp8: one batch size instead of the set")
     args = ap.parse_args()
     torch.manual_seed(0)
-    globals()["bench_" + args.what](args.iters)
+    if args.what == "gemm":
+        bench_gemm(args.iters, tuple(int(x) for x in args.shape.split(",")) if args.shape else None)
+    elif args.what == "fp8":
+        bench_fp8(args.iters, args.batch or None)
+    else:
+        globals()["bench_" + args.what](args.iters)
 
 
 if __name__ == "__main__":
