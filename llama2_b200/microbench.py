@@ -3,10 +3,13 @@
     python -m llama2_b200.microbench {gemm,attention,paged,fp8,pv,swiglu,unpad,rope,layer} [--iters N]
 
 Each prints one line per shape. Kernels are timed with CUDA events on the
-current stream; ``gemm`` times back-to-back launches (compute-bound, L2
-irrelevant) next to ``torch.matmul`` on the same operands (cuBLAS, for
-reference); the others flush L2 before every timed launch (write a 512 MB
-buffer, then read another, outside the timed window). Inputs are seeded
+current stream; ``gemm`` times back-to-back launches of the products of
+more than 128 rows (compute-bound, L2 irrelevant) and flushed launches of
+the decode-sized ones (at most 128 rows: bound by reading B, whose 34-180 MB
+would otherwise sit in L2 between launches), next to ``torch.matmul`` on the
+same operands (cuBLAS, for reference); the others flush L2 before every
+timed launch (write a 512 MB buffer, then read another, outside the timed
+window). Inputs are seeded
 random tensors of the 7B shapes.
 """
 from __future__ import annotations
@@ -55,7 +58,7 @@ def time_ms(fn, iters: int, flush: bool = True) -> float:
 
 def bench_gemm(iters, shape=None):
     shapes = [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 12288, 4096), (16384, 4096, 4096),
-              (64, 12288, 4096), (1, 12288, 4096)]
+              (64, 12288, 4096), (64, 4096, 4096), (64, 22016, 4096), (64, 4096, 11008), (1, 12288, 4096)]
     for (m, n, k) in ([shape] if shape else shapes):
         for trans_b in ((0,) if shape else (0, 1)):
             a = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
@@ -66,10 +69,16 @@ def bench_gemm(iters, shape=None):
                                      c.data_ptr(), n, 0, None, None, None, capi.L2K_BF16,
                                      torch.cuda.current_stream().cuda_stream)
             ref = lambda: torch.matmul(a, b.t() if trans_b else b, out=c)
-            t1, t2 = time_ms(ours, iters, flush=False), time_ms(ref, iters, flush=False)
+            flush = m <= 128
+            t1, t2 = time_ms(ours, iters, flush=flush), time_ms(ref, iters, flush=flush)
             fl = 2.0 * m * n * k
-            print(f"gemm bf16 m={m} n={n} k={k} trans_b={trans_b}: {t1 * 1e3:.1f} us {fl / t1 / 1e9:.1f} TF/s | "
-                  f"torch.matmul {t2 * 1e3:.1f} us {fl / t2 / 1e9:.1f} TF/s")
+            if flush:  # bytes of A, B and C per launch
+                nb = 2.0 * (m * k + k * n + m * n)
+                print(f"gemm bf16 m={m} n={n} k={k} trans_b={trans_b} (L2 flushed): {t1 * 1e3:.1f} us "
+                      f"{nb / t1 / 1e6:.1f} GB/s | torch.matmul {t2 * 1e3:.1f} us {nb / t2 / 1e6:.1f} GB/s")
+            else:
+                print(f"gemm bf16 m={m} n={n} k={k} trans_b={trans_b}: {t1 * 1e3:.1f} us {fl / t1 / 1e9:.1f} TF/s | "
+                      f"torch.matmul {t2 * 1e3:.1f} us {fl / t2 / 1e9:.1f} TF/s")
 
 
 def bench_attention(iters):
