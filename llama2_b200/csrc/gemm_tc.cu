@@ -15,7 +15,7 @@
 // block into TMEM. The tensor maps bound rows at M, columns at N and k at K,
 // so partial tiles read zeros. Two warps per TMEM lane quadrant (32 rows)
 // read the accumulator, each taking half of the rows' 32-column chunks.
-// Four shapes:
+// Five shapes:
 //   * at least 256 rows (prefill): the two-SM kernel below, clusters of two
 //     CTAs computing 256 x 256 tiles with tcgen05.mma.cta_group::2, each SM
 //     holding half of the A and half of the B tile (32 KB per 64-k step in a
@@ -23,13 +23,17 @@
 //   * 129 to 255 rows: the persistent kernel below, one CTA per SM over
 //     128 x 256 tiles, a 4-stage ring of 48 KB, two TMEM accumulators so the
 //     epilogue warps drain one tile while the next one's MMAs run;
-//   * one row tile (M <= 128: decode batches, bound by reading B) with at
-//     most one 128-column tile per SM: 128 x 128 tiles with K split over a
-//     thread-block cluster of up to 8 CTAs that reduce their fp32 rows into
-//     rank 0 over distributed shared memory (3 stages of 32 KB, two CTAs per
-//     SM), or a 4-stage ring without the split;
-//   * one row tile with more 128-column tiles than SMs: 128 x 256 tiles in a
-//     4-stage ring of 48 KB, one CTA per SM, one wave.
+//   * at most 64 rows (decode batches, bound by streaming B once): the decode
+//     kernel below, M = 64 MMAs over 64 x 128 or 64 x 256 tiles with an 8- or
+//     5-stage ring, K split over a cluster whose ranks share the reduction
+//     and the epilogue (plan: dec_plan);
+//   * 65 to 128 rows with at most one 128-column tile per SM: 128 x 128
+//     tiles with K split over a thread-block cluster of up to 8 CTAs that
+//     reduce their fp32 rows into rank 0 over distributed shared memory
+//     (3 stages of 32 KB, two CTAs per SM), or a 4-stage ring without the
+//     split;
+//   * 65 to 128 rows with more 128-column tiles than SMs: 128 x 256 tiles in
+//     a 4-stage ring of 48 KB, one CTA per SM, one wave.
 // Every mbarrier wait is bounded; on expiry the kernel records an error code
 // (l2k_device_error) and leaves after its copies and MMAs have drained.
 //
@@ -279,15 +283,15 @@ __device__ __forceinline__ void acc32(uint32_t taddr, int c0, uint32_t (&r)[32],
     }
 }
 
-// The epilogue of one tile for this thread's row: BN accumulator columns at
-// taddr (this warp's lane quadrant included); col0 = the tile's first column
-// of op(B) (EPI_SWIGLU: of the gate half, also the first output column).
-// The row's 32-column chunks are dealt to nparts warps of the same lane
-// quadrant: this warp takes chunks part, part + nparts, ...
-template <typename T, int BN, bool SPLIT, int EPI>
-__device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t taddr, int64_t row, bool store,
-                                              bool wide, int64_t col0, const float *red, int64_t red_stride,
-                                              int split, const RopeTok &tok, int part, int nparts)
+// The epilogue of one tile for this thread's row: load(c, r) fills r with
+// the row's fp32 sums of accumulator columns [c, c + 32) (called by every
+// lane of the warp: a TMEM load is warp-wide); col0 = the tile's first
+// column of op(B) (EPI_SWIGLU: of the gate half, also the first output
+// column). The row's 32-column chunks are dealt to nparts warps: this warp
+// takes chunks part, part + nparts, ...
+template <typename T, int BN, int EPI, typename Load>
+__device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, Load &&load, int64_t row, bool store, bool wide,
+                                              int64_t col0, const RopeTok &tok, int part, int nparts)
 {
     if constexpr (EPI == EPI_STORE)
     {
@@ -296,7 +300,7 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
         for (int c0 = 32 * part; c0 < BN; c0 += 32 * nparts)
         {
             uint32_t r[32];
-            acc32<SPLIT>(taddr, c0, r, store, red, red_stride, split);
+            load(c0, r);
             if (!store)
                 continue;
             float o[32];
@@ -314,8 +318,8 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
         for (int c0 = 32 * part; c0 < BN / 2; c0 += 32 * nparts)
         {
             uint32_t g[32], u[32];
-            acc32<SPLIT>(taddr, c0, g, store, red, red_stride, split);
-            acc32<SPLIT>(taddr, BN / 2 + c0, u, store, red, red_stride, split);
+            load(c0, g);
+            load(BN / 2 + c0, u);
             if (!store)
                 continue;
             float o[32];
@@ -377,7 +381,7 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
                     if (item++ % nparts != part)
                         continue;
                     uint32_t r[32];
-                    acc32<SPLIT>(taddr, hc + c0, r, store, red, red_stride, split);
+                    load(hc + c0, r);
                     if (!dst)
                         continue;
                     float o[32];
@@ -396,7 +400,7 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
                     if (item++ % nparts != part)
                         continue;
                     uint32_t r[32];
-                    acc32<SPLIT>(taddr, hc + c0, r, store, red, red_stride, split);
+                    load(hc + c0, r);
                     if (!dst)
                         continue;
                     float o[32];
@@ -425,8 +429,8 @@ __device__ __forceinline__ void tile_epilogue(const GemmTcArgs &a, uint32_t tadd
                     if (item++ % nparts != part)
                         continue;
                     uint32_t r0[32], r1[32];
-                    acc32<SPLIT>(taddr, hc + c0, r0, store, red, red_stride, split);
-                    acc32<SPLIT>(taddr, hc + half + c0, r1, store, red, red_stride, split);
+                    load(hc + c0, r0);
+                    load(hc + half + c0, r1);
                     if (!dst)
                         continue;
                     float o0[32], o1[32];
@@ -638,9 +642,14 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
             }
         }
         if (!*abort_flag && (!SPLIT || rank == 0))
-            tile_epilogue<T, BN, SPLIT, EPI>(a, tmem + ((uint32_t)(32 * quad) << 16), row, store, wide, col0,
-                                             red + (int64_t)lrow * BN, (int64_t)m_tile * BN, split, tok, part,
-                                             kEpiParts);
+        {
+            const uint32_t taddr = tmem + ((uint32_t)(32 * quad) << 16);
+            const float *rrow = red + (int64_t)lrow * BN;
+            const int64_t rstride = (int64_t)m_tile * BN;
+            tile_epilogue<T, BN, EPI>(
+                a, [&](int c0, uint32_t(&r)[32]) { acc32<SPLIT>(taddr, c0, r, store, rrow, rstride, split); }, row,
+                store, wide, col0, tok, part, kEpiParts);
+        }
     }
     else if (EPI == EPI_STORE && store && part == 0)
     {
@@ -664,6 +673,379 @@ __global__ void __launch_bounds__(kThreads, (Cfg<BN, STAGES>::kMinBlocks))
     {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// Decode-sized products (at most 64 rows of A), bound by streaming B once:
+// M = 64 MMAs (row r of the accumulator in TMEM lane (r % 16) + 32 (r / 16)),
+// so a stage holds 8 KB of A and a deep ring of B tiles (8 stages of 16 KB
+// at 128 columns, 5 of 32 KB at 256), one CTA per SM. Thread 0 initialises
+// the barriers and issues the first stages' loads before TMEM is allocated,
+// so the first tiles are in flight during the set-up. K is split over a
+// thread-block cluster of `split` CTAs; the reduction is spread over the
+// cluster: every rank writes its fp32 partial tile to its own shared memory
+// (the drained ring), and after a cluster barrier each rank sums the column
+// chunks dealt to it from all ranks' copies (distributed shared memory
+// loads, rank 0's partial first, then ranks 1.. in order: the order of the
+// single-rank reduction) and runs the epilogue on them; a second cluster
+// barrier keeps every copy alive until its readers are done.
+constexpr int kDM = 64;                  // rows of the MMA and of the A box
+constexpr uint32_t kDABox = kDM * 128;   // 64 rows x 64 k
+constexpr int kDThreads = 256;
+
+template <int BN>
+struct DecCfg
+{
+    static constexpr uint32_t kStageBytes = kDABox + BN * 128;
+    static constexpr int kStages = BN == 128 ? 8 : 5;
+    static constexpr uint32_t kOffBar = kStages * kStageBytes;
+    static constexpr uint32_t kOffMisc = kOffBar + 8 * (2 * kStages + 1);
+    static constexpr uint32_t kSmemBytes = kOffMisc + 16;
+    static constexpr int kStride = BN + 4; // floats per staged partial row (16-byte shift per row: no bank conflicts)
+    static_assert(2u * kDM * kStride * 4 <= kOffBar, "the staged and the reduced tile must fit the ring");
+};
+
+// kind::f16, D f32, A and B bf16 (1) or f16 (0), A K-major, B K-major (0) or MN-major (1), M = 64, N = n.
+__host__ __device__ constexpr uint32_t dec_instr_desc(uint32_t ab_format, uint32_t b_mn, uint32_t n)
+{
+    return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (b_mn << 16) | ((n >> 3) << 17) |
+           ((uint32_t)(kDM >> 4) << 24);
+}
+
+__device__ __forceinline__ void cluster_barrier()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr)
+{
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// Index of the k-th set bit of m (k < popcount(m)).
+__device__ __forceinline__ int nth_set_bit(uint32_t m, int k)
+{
+    for (int i = 0; i < k; ++i)
+        m &= m - 1;
+    return __ffs((int)m) - 1;
+}
+
+// Bit c: the epilogue items of a tile that tile_epilogue deals to `rank`
+// (items i with i % split == rank, counted in tile_epilogue's order) read
+// accumulator columns [32 c, 32 c + 32).
+template <int BN, int EPI>
+__device__ __forceinline__ uint32_t owned_chunks(const GemmTcArgs &a, int64_t col0, int rank, int split)
+{
+    uint32_t mask = 0;
+    if constexpr (EPI == EPI_STORE)
+    {
+        for (int c = 0; c < BN / 32; ++c)
+            if (c % split == rank)
+                mask |= 1u << c;
+    }
+    else if constexpr (EPI == EPI_SWIGLU)
+    {
+        for (int i = 0; i < BN / 64; ++i)
+            if (i % split == rank)
+                mask |= (1u << i) | (1u << (BN / 64 + i));
+    }
+    else
+    {
+        const RopeEpi &R = a.rope;
+        const int hd = (int)R.hd, half = hd / 2;
+        const int64_t total_heads = R.hq + 2 * R.hkv;
+        int item = 0;
+        for (int j = 0; j < BN / hd; ++j)
+        {
+            const int64_t head = col0 / hd + j;
+            if (head >= total_heads)
+                break;
+            const int hc = j * hd;
+            if (head >= R.hq + R.hkv || R.pairing == L2K_ROPE_INTERLEAVED)
+            {
+                for (int c0 = 0; c0 < hd; c0 += 32)
+                    if (item++ % split == rank)
+                        mask |= 1u << ((hc + c0) / 32);
+            }
+            else
+            {
+                for (int c0 = 0; c0 < half; c0 += 32)
+                    if (item++ % split == rank)
+                        mask |= (1u << ((hc + c0) / 32)) | (1u << ((hc + half + c0) / 32));
+            }
+        }
+    }
+    return mask;
+}
+
+template <typename T, bool B_MN, int BN, int EPI>
+__global__ void __launch_bounds__(kDThreads, 1)
+    gemm_dec_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                    const __grid_constant__ GemmTcArgs a)
+{
+    using C = DecCfg<BN>;
+    constexpr int kStages = C::kStages;
+    constexpr uint32_t kStageBytes = C::kStageBytes;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t sbase = smem_u32(smem);
+    if (sbase & 1023u) // (the same in every CTA: the whole cluster leaves)
+    {
+        if (threadIdx.x == 0)
+            atomicCAS(&g_gemm_error, 0, ERR_GEMM_SMEM_ALIGN);
+        return;
+    }
+    const uint32_t bar_full = sbase + C::kOffBar;      // + 8 * stage: the stage's tiles landed
+    const uint32_t bar_freed = bar_full + 8 * kStages; // + 8 * stage: the MMAs reading it completed
+    const uint32_t bar_done = bar_freed + 8 * kStages; // every MMA completed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::kOffMisc);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::kOffMisc + 8);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int split = a.split;
+    const int rank = (int)(blockIdx.x % split);
+    const int nt = (int)(blockIdx.x / split);
+    const int64_t col0 = EPI == EPI_SWIGLU ? (int64_t)nt * (BN / 2) : (int64_t)nt * BN;
+    const int kb0 = (int)((int64_t)rank * a.n_kb / split);
+    const int n_kb = (int)((int64_t)(rank + 1) * a.n_kb / split) - kb0;
+
+    // the loads of k block kb (relative to kb0) into its stage
+    auto issue = [&](int kb) {
+        const int st = kb % kStages;
+        const uint32_t dst = sbase + st * kStageBytes;
+        const uint32_t bar = bar_full + 8 * st;
+        mbar_expect_tx(bar, kStageBytes);
+        const int kx = (kb0 + kb) * BK;
+        tma_load_3d(dst, &tm_a, kx, 0, 0, bar);
+        if constexpr (B_MN)
+        {
+#pragma unroll
+            for (int h = 0; h < BN / 64; ++h)
+            {
+                const int64_t cx =
+                    EPI == EPI_SWIGLU && h >= BN / 128 ? a.up_col + col0 + 64 * (h - BN / 128) : col0 + 64 * h;
+                tma_load_3d(dst + kDABox + h * BK * 128, &tm_b, (int)cx, kx, 0, bar);
+            }
+        }
+        else if constexpr (EPI == EPI_SWIGLU)
+        {
+            tma_load_3d(dst + kDABox, &tm_b, kx, (int)col0, 0, bar);
+            tma_load_3d(dst + kDABox + (BN / 2) * 128, &tm_b, kx, (int)(a.up_col + col0), 0, bar);
+        }
+        else
+            tma_load_3d(dst + kDABox, &tm_b, kx, (int)col0, 0, bar);
+    };
+
+    int issued = 0; // producer thread: k blocks whose loads were issued
+    if (tid == 0)
+    {
+        for (int i = 0; i < kStages; ++i)
+        {
+            mbar_init(bar_full + 8 * i, 1);
+            mbar_init(bar_freed + 8 * i, 1);
+        }
+        mbar_init(bar_done, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_a) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tm_b) : "memory");
+        for (; issued < n_kb && issued < kStages; ++issued)
+            issue(issued);
+    }
+    if (warp == 1)
+    {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (tid == 0)
+    {
+        // ---- producer: the rest of the ring ----
+        for (int kb = issued; kb < n_kb && !*abort_flag; ++kb)
+        {
+            const int st = kb % kStages;
+            if (!mbar_wait(bar_freed + 8 * st, ((kb / kStages) - 1) & 1, abort_flag))
+            {
+                gemm_fail(ERR_GEMM_WAIT_MMA, abort_flag);
+                break;
+            }
+            issue(kb);
+            issued = kb + 1;
+        }
+    }
+    else if (tid == 32 && n_kb > 0)
+    {
+        // ---- MMA issuer ----
+        const uint32_t idesc =
+            dec_instr_desc(std::is_same<T, __nv_bfloat16>::value ? 1u : 0u, B_MN ? 1u : 0u, (uint32_t)BN);
+        for (int kb = 0; kb < n_kb && !*abort_flag; ++kb)
+        {
+            const int st = kb % kStages;
+            if (!mbar_wait(bar_full + 8 * st, (kb / kStages) & 1, abort_flag))
+            {
+                gemm_fail(ERR_GEMM_WAIT_LOAD, abort_flag);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t pa = sbase + st * kStageBytes, pb = pa + kDABox;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+            {
+                const uint64_t bd = B_MN ? desc_mn(pb + 2048u * k) : smem_desc(pb + 32u * k);
+                mma_f16(tmem, smem_desc(pa + 32u * k), bd, idesc, (kb | k) ? 1u : 0u);
+            }
+            mma_commit(bar_freed + 8 * st);
+        }
+        mma_commit(bar_done);
+    }
+    __syncwarp();
+
+    if (n_kb > 0 && !mbar_wait(bar_done, 0, abort_flag))
+        gemm_fail(ERR_GEMM_WAIT_DONE, abort_flag);
+    if (tid == 0 && *abort_flag)
+    {
+        // after a failure the copies and MMAs in flight land before the ring is reused
+        const int quiet = 0;
+        for (int kb = std::max(0, issued - kStages); kb < issued; ++kb)
+            mbar_wait(bar_full + 8 * (kb % kStages), (kb / kStages) & 1, &quiet);
+        if (n_kb > 0)
+            mbar_wait(bar_done, 0, &quiet);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    // -------- this CTA's partial tile to its shared memory: warps w and w + 4
+    // read TMEM lane quadrant w (rows 16 w .. 16 w + 15 in lanes 0-15), each
+    // half of the 32-column chunks --------
+    float *stage = reinterpret_cast<float *>(smem); // [kDM][kStride] (the ring is drained)
+    {
+        const int quad = warp & 3, half = warp >> 2;
+        const int srow = 16 * quad + lane;
+#pragma unroll 1
+        for (int c0 = 32 * half; c0 < BN; c0 += 64)
+        {
+            uint32_t r[32];
+            tmem_ld32_async(tmem + ((uint32_t)(32 * quad) << 16) + (uint32_t)c0, r);
+            tmem_wait_ld();
+            if (lane < 16)
+            {
+                float4 *dst = reinterpret_cast<float4 *>(stage + srow * C::kStride + c0);
+#pragma unroll
+                for (int v = 0; v < 8; ++v)
+                    dst[v] = n_kb > 0 ? make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                                    __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            __syncwarp();
+        }
+    }
+    cluster_barrier(); // every rank's partial is in its shared memory
+
+    // -------- reduction (split > 1): the chunks that this rank's epilogue
+    // items read, summed over the ranks' copies in rank order into `reduced`;
+    // thread t takes float4 positions t, t + 256, ... two at a time, with all
+    // ranks' loads of both in flight before the adds --------
+    float *reduced = stage + kDM * C::kStride;
+    if (split > 1)
+    {
+        const uint32_t own = owned_chunks<BN, EPI>(a, col0, rank, split);
+        const int n_pos = __popc(own) * kDM * 8;
+        const uint32_t stage_u32 = smem_u32(stage);
+        uint32_t peer[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+        {
+            uint32_t v = 0;
+            if (q < split)
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(v) : "r"(stage_u32), "r"(q));
+            peer[q] = v;
+        }
+#pragma unroll 1
+        for (int pos0 = tid; pos0 < n_pos; pos0 += 2 * kDThreads)
+        {
+            float4 x[2][8];
+            uint32_t off[2];
+#pragma unroll
+            for (int b = 0; b < 2; ++b)
+            {
+                const int pos = pos0 + b * kDThreads;
+                off[b] = 0;
+                if (pos < n_pos)
+                {
+                    const int k = pos / (kDM * 8), rem = pos - k * (kDM * 8);
+                    off[b] = (uint32_t)(((rem >> 3) * C::kStride + 32 * nth_set_bit(own, k) + 4 * (rem & 7)) * 4);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        if (q < split)
+                            x[b][q] = ld_cluster_f4(peer[q] + off[b]);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < 2; ++b)
+            {
+                if (pos0 + b * kDThreads >= n_pos)
+                    continue;
+                float4 sum = x[b][0];
+#pragma unroll
+                for (int q = 1; q < 8; ++q)
+                    if (q < split)
+                    {
+                        sum.x += x[b][q].x;
+                        sum.y += x[b][q].y;
+                        sum.z += x[b][q].z;
+                        sum.w += x[b][q].w;
+                    }
+                *reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(reduced) + off[b]) = sum;
+            }
+        }
+    }
+    __syncthreads();
+
+    // -------- epilogue: warps 2p and 2p + 1 take rows 0-31 and 32-63 of part
+    // p; items are dealt over (part, rank) as owned_chunks assumes --------
+    {
+        const int64_t row = 32 * (warp & 1) + lane;
+        const int part = (warp >> 1) * split + rank, nparts = (kDThreads / 64) * split;
+        const bool store = row < a.m;
+        RopeTok tok{false, 0, 0, 0u, 0u};
+        if constexpr (EPI == EPI_ROPE)
+            tok = rope_token(a.rope, row, store);
+        const float *mine = (split > 1 ? reduced : stage) + row * C::kStride;
+        auto load = [&](int c0, uint32_t(&r)[32]) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+            {
+                const float4 x = *reinterpret_cast<const float4 *>(mine + c0 + 4 * v);
+                r[4 * v] = __float_as_uint(x.x);
+                r[4 * v + 1] = __float_as_uint(x.y);
+                r[4 * v + 2] = __float_as_uint(x.z);
+                r[4 * v + 3] = __float_as_uint(x.w);
+            }
+        };
+        if (!*abort_flag)
+            tile_epilogue<T, BN, EPI>(a, load, row, store, a.wide != 0, col0, tok, part, nparts);
+    }
+    __syncwarp();
+    cluster_barrier(); // no rank leaves while another may still read its partial
+
+    // -------- teardown --------
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1)
+    {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
     }
 }
 
@@ -849,8 +1231,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
             tc_fence_after();
             __syncwarp();
-            tile_epilogue<T, BN, false, EPI>(a, tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * quad) << 16), row,
-                                             store, wide, ocol0, nullptr, 0, 1, tok, part, kEpiParts);
+            const uint32_t taddr = tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * quad) << 16);
+            tile_epilogue<T, BN, EPI>(
+                a, [&](int c0, uint32_t(&r)[32]) { acc32<false>(taddr, c0, r, store, nullptr, 0, 1); }, row, store,
+                wide, ocol0, tok, part, kEpiParts);
             tc_fence_before();
             __syncwarp();
             if (lane == 0)
@@ -1113,8 +1497,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
             }
             tc_fence_after();
             __syncwarp();
-            tile_epilogue<T, BN, false, EPI>(a, tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * quad) << 16), row,
-                                             store, wide, ocol0, nullptr, 0, 1, tok, part, kEpiParts);
+            const uint32_t taddr = tmem + (uint32_t)(buf * BN) + ((uint32_t)(32 * quad) << 16);
+            tile_epilogue<T, BN, EPI>(
+                a, [&](int c0, uint32_t(&r)[32]) { acc32<false>(taddr, c0, r, store, nullptr, 0, 1); }, row, store,
+                wide, ocol0, tok, part, kEpiParts);
             tc_fence_before();
             __syncwarp();
             if (lane == 0)
@@ -1278,6 +1664,133 @@ int launch_gemm_tc(const GemmProblem &p, cudaStream_t stream, int split)
     return check_launch("l2k_linear (tcgen05, split k)");
 }
 
+// The decode kernel: BN-column tiles, K split over clusters of `split` CTAs.
+template <typename T, bool B_MN, int BN, int EPI>
+int launch_gemm_dec(const GemmProblem &p, cudaStream_t stream, int split)
+{
+    constexpr uint32_t kSmemBytes = DecCfg<BN>::kSmemBytes;
+    const CUtensorMapDataType dt =
+        std::is_same<T, __nv_bfloat16>::value ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const uint64_t m = (uint64_t)p.m, nb = (uint64_t)p.nb, k = (uint64_t)p.k;
+    const uint64_t lda = (uint64_t)p.lda, ldb = (uint64_t)p.ldb;
+    CUtensorMap ma, mb;
+    bool ok = make_map(&ma, dt, p.a, k, m, 1, lda * 2, lda * 2 * m, kDM, BK);
+    if (B_MN) // B stored K x N: boxes of 64 k rows x 64 columns
+        ok = ok && make_map(&mb, dt, p.b, nb, k, 1, ldb * 2, ldb * 2 * k, BK, 64);
+    else // B stored N x K: boxes of BN n rows x 64 k (EPI_SWIGLU: two boxes of BN/2 rows)
+        ok = ok && make_map(&mb, dt, p.b, k, nb, 1, ldb * 2, ldb * 2 * nb, EPI == EPI_SWIGLU ? BN / 2 : BN, BK);
+    if (!ok)
+        return set_error(L2K_ERR_CUDA, "l2k_linear: tensor map encoding failed");
+    GemmTcArgs a = p.args;
+    a.m = p.m;
+    a.n_kb = (int)ceil_div(p.k, BK);
+    a.n_nt = (int)ceil_div(a.n, EPI == EPI_SWIGLU ? BN / 2 : BN);
+    a.wide = EPI != EPI_ROPE && (a.ldc * 2) % 16 == 0 && is_aligned(a.c, 16) ? 1 : 0;
+    a.split = split;
+    auto kernel = gemm_dec_kernel<T, B_MN, BN, EPI>;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess)
+        return set_error(L2K_ERR_CUDA, "l2k_linear: %s", cudaGetErrorString(e));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((int64_t)a.n_nt * split));
+    cfg.blockDim = dim3(kDThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)split;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, a);
+    if (e != cudaSuccess)
+        return set_error(L2K_ERR_CUDA, "l2k_linear (decode tiles): %s", cudaGetErrorString(e));
+    return check_launch("l2k_linear (tcgen05, decode tiles)");
+}
+
+// Clusters of `split` CTAs of the decode kernel with BN-column tiles that
+// the device runs at once (cached per device; 0 when the query fails).
+template <int BN>
+int dec_max_clusters(int split)
+{
+    static std::mutex mu;
+    static int cache[64][9] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || split < 1 || split > 8)
+        return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    int &c = cache[dev][split];
+    if (c == 0)
+    {
+        auto kernel = gemm_dec_kernel<__nv_bfloat16, true, BN, EPI_STORE>;
+        constexpr uint32_t kSmemBytes = DecCfg<BN>::kSmemBytes;
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) != cudaSuccess)
+            return 0;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)split);
+        cfg.blockDim = dim3(kDThreads);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)split;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess)
+        {
+            (void)cudaGetLastError();
+            return 0;
+        }
+        c = n > 0 ? n : -1;
+    }
+    return c > 0 ? c : 0;
+}
+
+// Decode-kernel plan for a product of at most 64 rows. The k-block rate of
+// one CTA, not its bytes in flight, paces the stream: measured on B200 with
+// these rings, about 40 GB/s of B per CTA with 128-column tiles and 76 GB/s
+// with 256-column tiles. A plan (tile width, cluster size; every cluster
+// resident at once, at least two k blocks per rank) streams at about
+// min(CTAs x rate, 6.5 TB/s); the plan is the fastest, and among plans
+// within 3 % of it, the smallest cluster (the least reduction), then 256
+// columns. False when no tile width fits one wave.
+template <int EPI>
+bool dec_plan(int64_t n_out, int64_t n_kb, int *bn_out, int *split_out)
+{
+    struct Cand
+    {
+        int bn, split;
+        double rate;
+    } cand[16];
+    int nc = 0;
+    double best = 0.0;
+    for (int bn : {256, 128})
+    {
+        const int64_t tiles = ceil_div(n_out, EPI == EPI_SWIGLU ? bn / 2 : bn);
+        for (int s = 1; s <= 8 && (s == 1 || 2LL * s <= n_kb); ++s)
+        {
+            const int cap = bn == 128 ? dec_max_clusters<128>(s) : dec_max_clusters<256>(s);
+            if (tiles > cap)
+                continue;
+            const double rate = std::min(6500.0, (double)(tiles * s) * (bn == 256 ? 76.0 : 40.0));
+            cand[nc++] = Cand{bn, s, rate};
+            best = std::max(best, rate);
+        }
+    }
+    int pick = -1;
+    for (int i = 0; i < nc; ++i)
+        if (cand[i].rate >= 0.97 * best && (pick < 0 || cand[i].split < cand[pick].split))
+            pick = i;
+    if (pick < 0)
+        return false;
+    *bn_out = cand[pick].bn;
+    *split_out = cand[pick].split;
+    return true;
+}
+
 // Tile shape by M: above 128 rows, 128 x 256 tiles (N = 256 MMAs read half
 // the A operand per FLOP from shared memory) in a 2-stage ring, two CTAs per
 // SM; up to 128 rows (decode-sized products, bound by reading B), 128 x 128
@@ -1292,6 +1805,10 @@ int launch_tiles(const GemmProblem &p, cudaStream_t stream)
     if (p.m > BM)
         return launch_gemm_persistent<T, B_MN, EPI>(p, stream);
     const int64_t tiles = ceil_div(p.nb, 128), n_kb = ceil_div(p.k, BK);
+    int dec_bn = 0, dec_split = 0;
+    if (p.m <= kDM && dec_plan<EPI>(p.args.n, n_kb, &dec_bn, &dec_split))
+        return dec_bn == 128 ? launch_gemm_dec<T, B_MN, 128, EPI>(p, stream, dec_split)
+                             : launch_gemm_dec<T, B_MN, 256, EPI>(p, stream, dec_split);
     // One row tile, more 128-column tiles than SMs (a gate/up projection):
     // 256-column tiles with a 4-stage ring (128 KB of B in flight per SM) in
     // one wave. Measured at 64 x 22016 x 4096: 39 us, against 66 us for
