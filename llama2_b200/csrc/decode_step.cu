@@ -145,8 +145,12 @@ __device__ __forceinline__ void swiglu_range(const StepArgs &a, int64_t n)
 
 // PV: the score rows also produce the attention output P.V (the V blocks
 // stream after the K blocks; this step's V row is patched in like the K row).
-template <typename T, int LPR, bool PV>
-__global__ void __launch_bounds__(kStreamThreads) decode_step_kernel(const StepArgs a)
+// DEV_ANGLES: some position of the launch may lie outside the host cos/sin
+// table (see score_row_stream). Three CTAs per SM: the streaming rows need
+// three 64 KB rings per SM, so registers are capped at what three CTAs leave
+// (80 per thread at 7 warps).
+template <typename T, int LPR, bool PV, bool DEV_ANGLES>
+__global__ void __launch_bounds__(kStreamThreads, 3) decode_step_kernel(const StepArgs a)
 {
     extern __shared__ __align__(128) uint8_t step_smem[];
     __shared__ StreamShared sh;
@@ -155,8 +159,8 @@ __global__ void __launch_bounds__(kStreamThreads) decode_step_kernel(const StepA
     {
         // (takes its ticket for the length update inside)
         cg::cluster_group cluster = cg::this_cluster();
-        score_row_stream<T, LPR, true, PV>(a.d, a.r, bid / (int64_t)cluster.num_blocks(), cluster, step_smem, sh,
-                                           &g_step_error);
+        score_row_stream<T, LPR, true, PV, T, DEV_ANGLES>(a.d, a.r, bid / (int64_t)cluster.num_blocks(), cluster,
+                                                          step_smem, sh, &g_step_error);
         return;
     }
     // Other roles read no lengths: their ticket comes first.
@@ -173,6 +177,7 @@ struct Plan
     int lpr;
     int C;
     bool pv;
+    bool dev_angles; // some appended position may lie outside the host cos/sin table
     size_t smem;
     StepArgs k;
 };
@@ -243,6 +248,9 @@ int plan_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace
     plan.lpr = lpr;
     plan.C = C;
     plan.pv = attn_out != nullptr;
+    // Appended positions are < kv_cache_len, and the table row is used when the
+    // updated length is at most 4096 and the position is in the table.
+    plan.dev_angles = !(p.rope_table && p.kv_cache_len <= 4096 && p.kv_cache_len <= p.rope_table_positions);
     plan.smem = smem;
     return L2K_OK;
 }
@@ -250,7 +258,7 @@ int plan_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace
 template <typename T, int LPR, bool PV>
 cudaError_t launch_step_kernel(const Plan &plan, cudaStream_t stream)
 {
-    auto kernel = decode_step_kernel<T, LPR, PV>;
+    auto kernel = plan.dev_angles ? decode_step_kernel<T, LPR, PV, true> : decode_step_kernel<T, LPR, PV, false>;
     if (plan.smem > 48 * 1024)
     {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);

@@ -353,6 +353,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                 v[j] = __uint_as_float(raw0[j]);
                 v[32 + j] = __uint_as_float(raw1[j]);
             }
+            // live[hh]: some row of this warp sees a key of columns [32 hh, 32 hh + 32);
+            // a half no row sees is all -inf and adds nothing to the statistics.
+            bool live[2] = {true, true};
             if ((int64_t)kt * BN + BN - 1 > min_lim)
             {
                 // keys past this row's limit (tile-uniform test, 32-bit compares)
@@ -361,6 +364,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
                 for (int j = 0; j < 64; ++j)
                     v[j] = j < vis ? v[j] : -INFINITY;
+                live[0] = __any_sync(0xffffffffu, vis > 0);
+                live[1] = __any_sync(0xffffffffu, vis > 32);
             }
             if (!phase_b)
             {
@@ -371,10 +376,16 @@ __global__ void __launch_bounds__(kThreads, 2)
                 const float m_new = fmaxf(m, tmax * a.c);
                 float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-                for (int j = 0; j < 64; j += 2)
+                for (int hh = 0; hh < 2; ++hh)
                 {
-                    sum0 += ex2(fmaf(v[j], a.c, -m_new));
-                    sum1 += ex2(fmaf(v[j + 1], a.c, -m_new));
+                    if (!live[hh])
+                        continue; // (its terms are exact zeros: the sums do not change)
+#pragma unroll
+                    for (int j = 32 * hh; j < 32 * hh + 32; j += 2)
+                    {
+                        sum0 += ex2(fmaf(v[j], a.c, -m_new));
+                        sum1 += ex2(fmaf(v[j + 1], a.c, -m_new));
+                    }
                 }
                 l = l * ex2(m - m_new) + (sum0 + sum1);
                 m = m_new;

@@ -279,6 +279,7 @@ struct StreamShared
     uint64_t xbar;      // completes when the C - 1 peers' pairs have landed in cstat
     uint64_t pvbar;     // PV, rank 0: completes when the C - 1 peers' partial P.V rows have landed
     uint32_t wkv[kCW];  // STEP: per consumer warp, max of the updated lengths
+    uint4 knew[32];     // STEP and fresh: the rotated new K row, one 16-byte slice per lane of a row
     float scratch[32];  // (block reductions of the step kernel's other roles)
     int abort_flag;
 };
@@ -684,7 +685,12 @@ __device__ __forceinline__ void pv_row(const DecodeArgs &a, const int64_t row, c
 // slice of head_dim). Lanes, warps and then the cluster's CTAs are summed in
 // a fixed order (peers push their partial rows into rank 0's shared memory
 // with st.async), so the output does not depend on timing.
-template <typename T, int LPR, bool STEP, bool PV = false, typename TC = T>
+// DEV_ANGLES (STEP): whether cos/sin may be evaluated on the device for
+// positions the host table does not cover. A launch whose every position is in
+// the table passes false: the device formula (powf, cosf, sinf, whose slow
+// paths are calls) is then not compiled into the kernel, which lets the
+// register allocator keep the key loop free of spills.
+template <typename T, int LPR, bool STEP, bool PV = false, typename TC = T, bool DEV_ANGLES = true>
 __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const StepRowArgs &sa, const int64_t row,
                                                  cg::cluster_group &cluster, uint8_t *smem, StreamShared &sh,
                                                  int *err)
@@ -721,6 +727,7 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
     uint32_t mx_kv = 0;          // STEP: max updated length over this thread's sequences
     uint32_t pq = 0, pkv = 0;    // STEP, producer warp, batch <= 32: lengths of sequence `lane`
     uint4 qa = make_uint4(0u, 0u, 0u, 0u), qb = qa, ka = qa, kb = qa; // STEP: q / k slices and rotation partners
+    uint4 va = qa; // STEP, the lanes that append: this lane's slice of the new V row
     const bool half_pair = sa.pairing != L2K_ROPE_INTERLEAVED;
     const int64_t hh = a.hd / 2;
     const int64_t j0 = half_pair ? (i0 < hh ? i0 : i0 - hh) : i0;
@@ -742,6 +749,8 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                 qb = ldg_keep(qh + j0 + hh);
                 kb = ldg_keep(kh + j0 + hh);
             }
+            if (c == 0 && warp == 0 && lane < LPR && ri.h % a.group == 0)
+                va = ldg_keep(src + (a.Hq + a.Hkv + ri.h / a.group) * a.hd + i0);
             for (int64_t b = tid; b < sa.batch; b += kCW * 32)
                 mx_kv = max(mx_kv, sa.kv_lens[b] + sa.q_lens[b]);
         }
@@ -824,7 +833,6 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
     uint32_t qh[8] = {};  // F8: this lane's q slice as f16 pairs (when q_f16)
     bool q_f16 = false;
     uint4 qraw;                              // the same slice as stored (16-bit types: the mixed fma's operand)
-    uint4 knew = make_uint4(0u, 0u, 0u, 0u); // STEP and fresh: this lane's slice of the rotated new K row
     if (warp == kCW)
     {
         if (lane == 0)
@@ -874,12 +882,21 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                             cs[4 * v + 3] = t.w;
                         }
                 }
-                else
+                else if constexpr (DEV_ANGLES)
                 {
 #pragma unroll
                     for (int e = 0; e < NPMAX; ++e)
                         if (e < np)
                             rope_cos_sin_device(p0 + e, a.hd, pos, kv_new, cs[2 * e], cs[2 * e + 1]);
+                }
+                else
+                {
+                    // unreachable when the host's coverage check holds: recorded, not guessed
+                    if (lane == 0)
+                        atomicCAS(err, 0, 0x204);
+#pragma unroll
+                    for (int e = 0; e < 2 * NPMAX; ++e)
+                        cs[e] = 0.f;
                 }
                 Vec16<T> qo, ko;
                 if (!half_pair)
@@ -912,9 +929,22 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                 for (int e = 0; e < N; ++e)
                     qf[e] = to_f(qo.v[e]);
                 qraw = as_u4(qo);
-                knew = as_u4(ko);
+                if (warp == 0 && lane < LPR)
+                    sh.knew[sub] = as_u4(ko); // (read in the key loop: not held in registers across it)
                 if (c == 0 && warp == 0 && lane < LPR)
+                {
                     stg(static_cast<T *>(sa.q_out) + row * a.hd + i0, as_u4(qo));
+                    // Append K and V at pos (one CTA per kv head). A copy of the
+                    // block holding pos may read the row before or after this
+                    // store: every reader overwrites the row in its shared-memory
+                    // copy with the rotated row (the key loop below).
+                    if (ri.h % a.group == 0)
+                    {
+                        const int64_t crow = ((ri.b * a.Hkv + ri.h / a.group) * a.S + pos) * a.hd + i0;
+                        stg(static_cast<T *>(sa.k_cache) + crow, as_u4(ko));
+                        stg(static_cast<T *>(sa.v_cache) + crow, va);
+                    }
+                }
                 q_done = true;
             }
         }
@@ -964,6 +994,16 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
             }
         }
     }
+    if constexpr (STEP)
+    {
+        // the largest updated length, reduced now (not held in registers across the key loop)
+        if (warp < kCW)
+        {
+            const uint32_t wm = warp_max_u32(mx_kv);
+            if (lane == 0)
+                sh.wkv[warp] = wm;
+        }
+    }
     __syncthreads(); // the ring is initialized; q is ready
 
     float2 st_l = make_float2(-INFINITY, 0.f); // online (max, sum of exp) of this lane's logits
@@ -996,6 +1036,22 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
         if (C > 1)
             cluster_wait_acquire(); // phase 0: every peer has started (waited while the first blocks land)
         const int st = warp % kNS, hf = warp / kNS; // ring stage, half of the block
+        // STEP: the ring sequence number and stage row of this step's key when
+        // it falls in this warp's half of one of this rank's blocks (else -1).
+        int patch_i = -1, patch_row = 0;
+        if constexpr (STEP)
+        {
+            if (fresh)
+            {
+                const int64_t gp = (int64_t)pos / KB;
+                const int r = (int)((int64_t)pos - gp * KB);
+                if (gp % C == c && r / HALF == hf)
+                {
+                    patch_i = (int)(gp / C);
+                    patch_row = r;
+                }
+            }
+        }
         const uint8_t *stage = smem + st * kBlockBytes + (hf * HALF + lane / LPR) * ROW_BYTES + sub * 16;
         for (int i = st; i < n_mine; i += kNS)
         {
@@ -1010,23 +1066,14 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
             {
                 // The block holding this step's key: its cache row is stale (or
                 // being written) — use the rotated row instead.
-                const int64_t rib = (int64_t)pos - g * KB - hf * HALF;
-                if (fresh && rib >= 0 && rib < HALF)
+                if (i == patch_i)
                 {
                     if (lane < LPR)
                     {
-                        *reinterpret_cast<uint4 *>(smem + st * kBlockBytes + (hf * HALF + rib) * ROW_BYTES +
-                                                   sub * 16) = knew;
+                        *reinterpret_cast<uint4 *>(smem + st * kBlockBytes + patch_row * ROW_BYTES + sub * 16) =
+                            sh.knew[sub];
                         // the next bulk copy into this stage must see the generic writes ordered
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        if (ri.h % a.group == 0)
-                        {
-                            const int64_t crow = ((ri.b * a.Hkv + kvh) * a.S + pos) * a.hd + i0;
-                            const T *vsrc = static_cast<const T *>(sa.qkv) + ri.b * sa.qkv_stride +
-                                            (a.Hq + a.Hkv + kvh) * a.hd + i0;
-                            stg(static_cast<T *>(sa.k_cache) + crow, knew);
-                            stg(static_cast<T *>(sa.v_cache) + crow, ldg_keep(vsrc));
-                        }
                     }
                     __syncwarp();
                 }
@@ -1073,14 +1120,8 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1)
             st_l = stat_merge(st_l, shfl_xor_stat(st_l, off));
-        if constexpr (STEP)
-            mx_kv = warp_max_u32(mx_kv);
         if (lane == 0)
-        {
             sh.wstat[warp] = st_l;
-            if (STEP)
-                sh.wkv[warp] = mx_kv;
-        }
     }
     __syncthreads(); // logits and warp statistics are complete
     if (sh.abort_flag && warp == kCW && lane == 0)

@@ -266,3 +266,52 @@ def test_step_attention_matches_operator_sequence(dtype, hd, pairing, S, hq, hkv
         assert bits_equal(host(f[n]), host(u[n])), n
     assert bits_equal(host(out_f), host(out_u)), "attention output"
     assert max_rel_err(host(f["normed"]), host(u["normed"])) <= (1e-5 if dtype == torch.float32 else 1e-2)
+
+
+@pytest.mark.parametrize("dtype,use_table,S,kv", [
+    (torch.bfloat16, False, 512, [255, 7, 511]),     # no host table: angles on the device
+    (torch.float32, True, 4608, [4200, 4095, 30]),   # lengths past 4096: the length-scaled angles on the device
+    (torch.bfloat16, True, 4608, [4200, 100, 4607]),
+    (torch.bfloat16, True, 4096, [4095, 0, 2000]),   # every position in the table: the table-only kernel
+])
+def test_step_angle_sources_against_operator_sequence(dtype, use_table, S, kv):
+    """The fused step has a kernel for launches whose every position is in the
+    host cos/sin table and one that may evaluate angles on the device; each
+    is bit-identical to the operator sequence with the same angle source."""
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(S + len(kv) + int(use_table))
+    B, H, hd, F, V = 3, 4, 128, 256, 500
+    D = H * hd
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(dtype)
+
+    base = dict(q_lens=torch.ones(B, dtype=torch.uint32, device=dev),
+                input_ids=torch.tensor([3, 499, 250], dtype=torch.uint32, device=dev),
+                embed_table=rnd(V, D, scale=0.02), norm_weight=(torch.rand(D, generator=g, device=dev) + 0.5).to(dtype),
+                qkv=rnd(B, 3 * D), is_done=torch.zeros(B, dtype=torch.uint8, device=dev), gate_up=rnd(B, 2 * F))
+    kv0 = torch.tensor(kv, dtype=torch.uint32, device=dev)
+    k0, v0 = rnd(B, H, S, hd), rnd(B, H, S, hd)
+
+    def fresh():
+        return dict(kv_lens=kv0.clone(), max_lens=torch.zeros(2, dtype=torch.uint32, device=dev),
+                    x=torch.empty(B, D, dtype=dtype, device=dev), normed=torch.empty(B, D, dtype=dtype, device=dev),
+                    q=torch.zeros(B, H, 1, hd, dtype=dtype, device=dev), k_cache=k0.clone(), v_cache=v0.clone(),
+                    qk=torch.full((B, H, 1, S), 7.0, dtype=dtype, device=dev),
+                    ffn_out=torch.empty(B, F, dtype=dtype, device=dev))
+
+    f = fresh()
+    ops.decode_step(**base, **f, workspace=ops.decode_step_workspace(dev), pairing=1, use_table=use_table)
+    u = fresh()
+    ops.launch_update_q_kv_lens(base["q_lens"], u["kv_lens"], u["max_lens"][0:1], u["max_lens"][1:2])
+    ops.launch_embedding(base["input_ids"], base["embed_table"], u["x"])
+    ops.launch_fused_add_residual_rmsnorm(base["norm_weight"], u["x"], u["normed"], False)
+    ops.launch_fused_reshape_rope_kvcache_llama2_decode(base["qkv"], base["is_done"], u["kv_lens"], u["q"],
+                                                        u["k_cache"], u["v_cache"], use_table=use_table)
+    ops.decode_attention_scores(u["q"], u["k_cache"], u["kv_lens"], u["max_lens"][1:2], u["qk"])
+    ops.launch_swiglu(base["gate_up"], u["ffn_out"])
+    torch.cuda.synchronize()
+    for n in ("kv_lens", "max_lens", "x", "q", "k_cache", "v_cache", "qk", "ffn_out"):
+        assert bits_equal(host(f[n]), host(u[n])), n
+    assert max_rel_err(host(f["normed"]), host(u["normed"])) <= (1e-5 if dtype == torch.float32 else 1e-2)
