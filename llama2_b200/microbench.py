@@ -1,6 +1,6 @@
 """Timings of single operators and of the decoder layer on one GPU.
 
-    python -m llama2_b200.microbench {gemm,attention,paged,fp8,pv,swiglu,unpad,rope,layer} [--iters N]
+    python -m llama2_b200.microbench {gemm,attention,paged,paged_prefill,fp8,pv,swiglu,unpad,rope,layer} [--iters N]
 
 Each prints one line per shape. Kernels are timed with CUDA events on the
 current stream; ``gemm`` times back-to-back launches of the products of
@@ -135,6 +135,42 @@ def bench_paged(iters):
             del k, v, kp, vp
 
 
+def bench_paged_prefill(iters):
+    """Prefill attention over paged K/V caches (64-row pages of 7B heads,
+    shuffled block table) next to the contiguous operators: the tcgen05
+    scores (8 x 2048 causal rows, bf16) and the tcgen05 P.V."""
+    b, h, qc, hd = 8, 32, 2048, 128
+    dt = torch.bfloat16
+    rows = 64
+    max_pages = qc // rows
+    g = torch.Generator(device="cuda")
+    g.manual_seed(3)
+    q = torch.randn(b, h, qc, hd, device="cuda", generator=g).to(dt)
+    k = torch.randn(b, h, qc, hd, device="cuda", generator=g).to(dt)
+    v = torch.randn(b, h, qc, hd, device="cuda", generator=g).to(dt)
+    perm = torch.randperm(b * max_pages, generator=torch.Generator().manual_seed(2))
+    table = perm.view(b, max_pages).to(torch.int32).cuda()
+    kp = torch.empty(b * max_pages, h, rows, hd, device="cuda", dtype=dt)
+    vp = torch.empty_like(kp)
+    kp[perm] = k.view(b, h, max_pages, rows, hd).transpose(1, 2).reshape(b * max_pages, h, rows, hd)
+    vp[perm] = v.view(b, h, max_pages, rows, hd).transpose(1, 2).reshape(b * max_pages, h, rows, hd)
+    ql = torch.full((b,), qc, dtype=torch.uint32, device="cuda")
+    kl = torch.full((b,), qc, dtype=torch.uint32, device="cuda")
+    qk = torch.empty(b, h, qc, qc, device="cuda", dtype=dt)
+    out = torch.empty(b, h, qc, hd, device="cuda", dtype=dt)
+    es = 2
+    score_bytes = (2 * b * h * qc * hd + b * h * qc * qc) * es  # q, K, P
+    pv_bytes = (b * h * qc * qc + 2 * b * h * qc * hd) * es     # P, V, output
+    for name, fn_c, fn_p, nb in (
+            ("scores", lambda: ops.prefill_attention_scores(q, k, ql, kl, qc, qc, qk),
+             lambda: ops.prefill_attention_scores_paged(q, kp, table, ql, kl, qc, qc, qk), score_bytes),
+            ("P.V", lambda: ops.launch_attention_qkv(qk, v, out, qc, qc),
+             lambda: ops.launch_attention_qkv_paged(qk, vp, table, kl, out, qc, qc), pv_bytes)):
+        t1, t2 = time_ms(fn_c, iters), time_ms(fn_p, iters)
+        print(f"prefill {name} bf16 8 x 2048: contiguous {t1 * 1e3:.1f} us {nb / t1 / 1e6:.1f} GB/s | "
+              f"paged (64-row pages) {t2 * 1e3:.1f} us {nb / t2 / 1e6:.1f} GB/s")
+
+
 def bench_fp8(iters, batch=None):
     """Fused decode attention over fp8 (e4m3) caches next to bf16 caches of
     the same shape (7B heads, 4096-position caches, seeded lengths)."""
@@ -246,7 +282,8 @@ def bench_layer(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "paged", "fp8", "pv", "swiglu", "unpad", "rope", "layer"])
+    ap.add_argument("what", choices=["gemm", "attention", "paged", "paged_prefill", "fp8", "pv", "swiglu", "unpad",
+                                        "rope", "layer"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--shape", default="", help="gemm: one M,N,K product (B stored K x N) instead of the set")
     ap.add_argument("--batch", type=int, default=0, help="fp8: one batch size instead of the set")
