@@ -555,6 +555,27 @@ int l2k_decode_step_attention(const l2k_decode_step_args *args, void *attn_out, 
 int l2k_decode_step_attention_no_alloc(const l2k_decode_step_args *args, void *attn_out, l2k_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * The fused decode step (with or without the attention output) over paged
+ * K/V caches: args->k_cache and args->v_cache are page pools
+ * (num_pages, kv_head_num, page_rows, head_dim) with page_rows =
+ * l2k_paged_block_rows(head_dim, dtype); args->kv_cache_len must be
+ * max_pages * page_rows (the logical cache length). Positions
+ * [j * page_rows, (j + 1) * page_rows) of sequence b live in page
+ * block_table[b * max_pages + j] (u32, device; every entry a sequence's keys
+ * reach must name a page of the pool). The appended K/V rows go to the page
+ * holding the position; results are bit-identical to l2k_decode_step /
+ * l2k_decode_step_attention on the contiguous caches those pages form.
+ * The reference's caches are contiguous (batch, kv_head, kv_cache_len,
+ * head_dim) (include/kernel/fused_reshape_rope_kvcache_decode.h:11-12) and it
+ * has no fused step; paging widens that cache contract.
+ * ------------------------------------------------------------------------ */
+int l2k_decode_step_paged(const l2k_decode_step_args *args, const uint32_t *block_table, int64_t max_pages,
+                          int64_t num_pages, uint32_t *workspace, l2k_stream_t stream);
+int l2k_decode_step_attention_paged(const l2k_decode_step_args *args, const uint32_t *block_table,
+                                    int64_t max_pages, int64_t num_pages, void *attn_out, uint32_t *workspace,
+                                    l2k_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * l2k_decode_step without a workspace argument, for callers that cannot
  * provide device memory (for example a binding whose host side only passes
  * the tensors it already has and owns no device allocator). The workspace is

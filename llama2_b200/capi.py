@@ -90,6 +90,8 @@ SIGNATURES = {
     "l2k_decode_step_supported": [ctypes.POINTER(DecodeStepArgs)],
     "l2k_decode_step": [ctypes.POINTER(DecodeStepArgs), vp, vp],
     "l2k_decode_step_attention": [ctypes.POINTER(DecodeStepArgs), vp, vp, vp],
+    "l2k_decode_step_paged": [ctypes.POINTER(DecodeStepArgs), vp, i64, i64, vp, vp],
+    "l2k_decode_step_attention_paged": [ctypes.POINTER(DecodeStepArgs), vp, i64, i64, vp, vp, vp],
     "l2k_decode_step_attention_no_alloc": [ctypes.POINTER(DecodeStepArgs), vp, vp],
     "l2k_decode_step_no_alloc": [ctypes.POINTER(DecodeStepArgs), vp],
     "l2k_device_error": ([cint], cint),

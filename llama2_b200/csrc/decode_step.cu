@@ -172,6 +172,17 @@ __global__ void __launch_bounds__(kStreamThreads, 3) decode_step_kernel(const St
         swiglu_range<T>(a, bid - a.score_ctas - a.norm_ctas);
 }
 
+// Paged K/V caches of a step: pools (num_pages, Hkv, page_rows, head_dim)
+// with page_rows = l2k_paged_block_rows (one streamed key block per page);
+// positions [j page_rows, (j + 1) page_rows) of sequence b live in page
+// block_table[b * max_pages + j].
+struct PagedCaches
+{
+    const uint32_t *block_table;
+    int64_t max_pages;
+    int64_t num_pages;
+};
+
 struct Plan
 {
     int lpr;
@@ -184,7 +195,8 @@ struct Plan
 
 // Validates the arguments and lays out the grid; L2K_OK or a status.
 template <typename T>
-int plan_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace, Plan &plan)
+int plan_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace, const PagedCaches *paged,
+              Plan &plan)
 {
     constexpr int N = Vec16<T>::N;
     const int64_t row_bytes = p.head_dim * (int64_t)sizeof(T);
@@ -225,6 +237,16 @@ int plan_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace
                      (p.kv_cache_len * (int64_t)sizeof(T)) % 16 == 0 && is_aligned(p.qk, 16)};
     k.d.v = p.v_cache;
     k.d.qkv = attn_out; // (B, Hq, 1, hd); null without the attention output
+    if (paged)
+    {
+        // k_cache / v_cache are page pools; kv_cache_len is the logical length
+        L2K_REQUIRE_SHAPE(p.kv_cache_len == paged->max_pages * kb,
+                          "l2k_decode_step_paged: kv_cache_len (%lld) must be max_pages * page_rows (%lld * %lld)",
+                          (long long)p.kv_cache_len, (long long)paged->max_pages, (long long)kb);
+        k.d.block_table = paged->block_table;
+        k.d.max_pages = paged->max_pages;
+        k.d.num_pages = paged->num_pages;
+    }
     k.r = StepRowArgs{p.qkv, p.is_done, p.q_lens, p.kv_lens, p.max_lens, workspace, p.q, p.k_cache, p.v_cache,
                       reinterpret_cast<const float2 *>(p.rope_table), p.rope_table ? p.rope_table_positions : 0,
                       p.batch, (p.q_head_num + 2 * p.kv_head_num) * p.head_dim, p.pairing};
@@ -298,10 +320,11 @@ cudaError_t launch_step_lpr(const Plan &plan, cudaStream_t stream)
 }
 
 template <typename T>
-int run_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace, cudaStream_t stream, bool launch)
+int run_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace, const PagedCaches *paged,
+             cudaStream_t stream, bool launch)
 {
     Plan plan;
-    if (int st = plan_step<T>(p, attn_out, workspace, plan))
+    if (int st = plan_step<T>(p, attn_out, workspace, paged, plan))
         return st;
     if (!launch)
         return L2K_OK;
@@ -311,7 +334,8 @@ int run_step(const l2k_decode_step_args &p, void *attn_out, uint32_t *workspace,
     return check_launch("l2k_decode_step");
 }
 
-int step_entry(const l2k_decode_step_args *pp, void *attn_out, uint32_t *workspace, cudaStream_t stream, bool launch)
+int step_entry(const l2k_decode_step_args *pp, void *attn_out, uint32_t *workspace, cudaStream_t stream, bool launch,
+               const PagedCaches *paged = nullptr)
 {
     L2K_REQUIRE(pp != nullptr, "l2k_decode_step: null args");
     const l2k_decode_step_args &p = *pp;
@@ -331,7 +355,10 @@ int step_entry(const l2k_decode_step_args *pp, void *attn_out, uint32_t *workspa
                 "l2k_decode_step: null pointer");
     L2K_REQUIRE(p.hidden == 0 || (p.gate_up && p.ffn_out), "l2k_decode_step: null gate_up / ffn_out");
     L2K_REQUIRE(p.x != p.normed, "l2k_decode_step: x and normed must be distinct buffers");
-    L2K_DISPATCH(p.dtype, { return run_step<T>(p, attn_out, workspace, stream, launch); });
+    if (paged)
+        L2K_REQUIRE(paged->block_table && paged->max_pages > 0 && paged->num_pages > 0,
+                    "l2k_decode_step_paged: null block table or empty page pool");
+    L2K_DISPATCH(p.dtype, { return run_step<T>(p, attn_out, workspace, paged, stream, launch); });
     return L2K_OK;
 }
 
@@ -371,6 +398,22 @@ extern "C" int l2k_decode_step_attention(const l2k_decode_step_args *args, void 
 {
     L2K_REQUIRE(attn_out != nullptr, "l2k_decode_step_attention: null attn_out");
     return l2k::step_entry(args, attn_out, workspace, stream, true);
+}
+
+extern "C" int l2k_decode_step_paged(const l2k_decode_step_args *args, const uint32_t *block_table, int64_t max_pages,
+                                     int64_t num_pages, uint32_t *workspace, l2k_stream_t stream)
+{
+    const l2k::PagedCaches paged{block_table, max_pages, num_pages};
+    return l2k::step_entry(args, nullptr, workspace, stream, true, &paged);
+}
+
+extern "C" int l2k_decode_step_attention_paged(const l2k_decode_step_args *args, const uint32_t *block_table,
+                                               int64_t max_pages, int64_t num_pages, void *attn_out,
+                                               uint32_t *workspace, l2k_stream_t stream)
+{
+    L2K_REQUIRE(attn_out != nullptr, "l2k_decode_step_attention_paged: null attn_out");
+    const l2k::PagedCaches paged{block_table, max_pages, num_pages};
+    return l2k::step_entry(args, attn_out, workspace, stream, true, &paged);
 }
 
 // ---------------------------------------------------------------------------

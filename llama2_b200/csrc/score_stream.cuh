@@ -940,9 +940,21 @@ __device__ __forceinline__ void score_row_stream(const DecodeArgs &a, const Step
                     // copy with the rotated row (the key loop below).
                     if (ri.h % a.group == 0)
                     {
-                        const int64_t crow = ((ri.b * a.Hkv + ri.h / a.group) * a.S + pos) * a.hd + i0;
-                        stg(static_cast<T *>(sa.k_cache) + crow, as_u4(ko));
-                        stg(static_cast<T *>(sa.v_cache) + crow, va);
+                        // contiguous (B, Hkv, S, hd), or the page holding pos (a page past
+                        // the pool is not written; its streamed copy records the error)
+                        const int64_t kvh0 = ri.h / a.group;
+                        int64_t crow = ((ri.b * a.Hkv + kvh0) * a.S + pos) * a.hd + i0;
+                        if (a.block_table)
+                        {
+                            const int64_t page = a.block_table[ri.b * a.max_pages + (int64_t)pos / KB];
+                            crow = page < a.num_pages ? ((page * a.Hkv + kvh0) * KB + (int64_t)pos % KB) * a.hd + i0
+                                                      : -1;
+                        }
+                        if (crow >= 0)
+                        {
+                            stg(static_cast<T *>(sa.k_cache) + crow, as_u4(ko));
+                            stg(static_cast<T *>(sa.v_cache) + crow, va);
+                        }
                     }
                 }
                 q_done = true;

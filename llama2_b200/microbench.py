@@ -1,6 +1,6 @@
 """Timings of single operators and of the decoder layer on one GPU.
 
-    python -m llama2_b200.microbench {gemm,attention,paged,paged_prefill,fp8,pv,swiglu,unpad,rope,layer} [--iters N]
+    python -m llama2_b200.microbench {gemm,attention,paged,paged_step,paged_prefill,fp8,pv,swiglu,unpad,rope,layer} [--iters N]
 
 Each prints one line per shape. Kernels are timed with CUDA events on the
 current stream; ``gemm`` times back-to-back launches of the products of
@@ -133,6 +133,57 @@ def bench_paged(iters):
             print(f"decode attention {dt} b={b}: contiguous {t1 * 1e3:.1f} us {nbytes / t1 / 1e6:.1f} GB/s | "
                   f"paged ({rows}-row pages) {t2 * 1e3:.1f} us {nbytes / t2 / 1e6:.1f} GB/s")
             del k, v, kp, vp
+
+
+def bench_paged_step(iters):
+    """The one-launch decode step (7B dims) over paged caches (shuffled block
+    table) next to the same step over the contiguous caches."""
+    h, s, hd, dim, hidden, vocab = 32, 4096, 128, 4096, 11008, 32000
+    for dt in (torch.float32, torch.bfloat16):
+        rows = ops.paged_block_rows(hd, dt)
+        max_pages = s // rows
+        b = 64
+        g = torch.Generator(device="cuda")
+        g.manual_seed(5)
+        k = torch.randn(b, h, s, hd, device="cuda", generator=g).to(dt)
+        v = torch.randn(b, h, s, hd, device="cuda", generator=g).to(dt)
+        perm = torch.randperm(b * max_pages, generator=torch.Generator().manual_seed(2))
+        table = perm.view(b, max_pages).to(torch.int32).cuda()
+        kp = torch.empty(b * max_pages, h, rows, hd, device="cuda", dtype=dt)
+        vp = torch.empty_like(kp)
+        kp[perm] = k.view(b, h, max_pages, rows, hd).transpose(1, 2).reshape(b * max_pages, h, rows, hd)
+        vp[perm] = v.view(b, h, max_pages, rows, hd).transpose(1, 2).reshape(b * max_pages, h, rows, hd)
+        lens = torch.randint(1, s - 1, (b,), generator=torch.Generator().manual_seed(1))
+        kv0 = lens.to(torch.uint32).cuda()
+        kv = kv0.clone()
+        base = dict(q_lens=torch.ones(b, dtype=torch.uint32, device="cuda"), kv_lens=kv,
+                    max_lens=torch.zeros(2, dtype=torch.uint32, device="cuda"),
+                    input_ids=torch.randint(0, vocab, (b,), dtype=torch.int32, device="cuda"),
+                    embed_table=(torch.randn(vocab, dim, device="cuda", generator=g) * 0.02).to(dt),
+                    norm_weight=torch.ones(dim, device="cuda", dtype=dt),
+                    x=torch.empty(b, dim, device="cuda", dtype=dt), normed=torch.empty(b, dim, device="cuda", dtype=dt),
+                    qkv=torch.randn(b, 3 * dim, device="cuda", generator=g).to(dt),
+                    is_done=torch.zeros(b, dtype=torch.uint8, device="cuda"),
+                    q=torch.empty(b, h, 1, hd, device="cuda", dtype=dt),
+                    qk=torch.empty(b, h, 1, s, device="cuda", dtype=dt),
+                    gate_up=torch.randn(b, 2 * hidden, device="cuda", generator=g).to(dt),
+                    ffn_out=torch.empty(b, hidden, device="cuda", dtype=dt),
+                    workspace=ops.decode_step_workspace(torch.device("cuda")), pairing=1)
+        es = torch.finfo(dt).bits // 8
+        nbytes = (int(lens.sum()) + b) * h * hd * es + b * h * s * es  # K rows read, score rows written
+
+        def contiguous():
+            kv.copy_(kv0)
+            ops.decode_step(**base, k_cache=k, v_cache=v)
+
+        def paged():
+            kv.copy_(kv0)
+            ops.decode_step_paged(**base, k_pages=kp, v_pages=vp, block_table=table)
+
+        t1, t2 = time_ms(contiguous, iters), time_ms(paged, iters)
+        print(f"decode step {dt} b={b}: contiguous {t1 * 1e3:.1f} us {nbytes / t1 / 1e6:.1f} GB/s | "
+              f"paged ({rows}-row pages) {t2 * 1e3:.1f} us {nbytes / t2 / 1e6:.1f} GB/s")
+        del k, v, kp, vp
 
 
 def bench_paged_prefill(iters):
@@ -282,7 +333,7 @@ def bench_layer(iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "paged", "paged_prefill", "fp8", "pv", "swiglu", "unpad",
+    ap.add_argument("what", choices=["gemm", "attention", "paged", "paged_step", "paged_prefill", "fp8", "pv", "swiglu", "unpad",
                                         "rope", "layer"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--shape", default="", help="gemm: one M,N,K product (B stored K x N) instead of the set")

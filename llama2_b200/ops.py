@@ -576,7 +576,7 @@ def decode_step_workspace(device) -> torch.Tensor:
 
 
 def _decode_step_args(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done, q,
-                      k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table):
+                      k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table, block_table=None):
     _dev(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done, q, k_cache, v_cache,
          qk, gate_up, ffn_out)
     for t, n in ((q_lens, "q_lens"), (kv_lens, "kv_lens"), (max_lens, "max_lens"), (input_ids, "input_ids")):
@@ -589,8 +589,18 @@ def _decode_step_args(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_we
     hkv, s = k_cache.shape[1], k_cache.shape[2]
     hidden = ffn_out.shape[-1]
     _require(one == 1 and q.shape[0] == b, "Incorrect q size")
-    _require(tuple(k_cache.shape) == (b, hkv, s, hd) and tuple(v_cache.shape) == (b, hkv, s, hd),
-             "Incorrect k/v cache size")
+    if block_table is None:
+        _require(tuple(k_cache.shape) == (b, hkv, s, hd) and tuple(v_cache.shape) == (b, hkv, s, hd),
+                 "Incorrect k/v cache size")
+    else:
+        # page pools (num_pages, Hkv, page_rows, hd); s = the logical cache length
+        _dev(block_table)
+        _u32(block_table, "block_table")
+        page_rows = k_cache.shape[2]
+        _require(page_rows == paged_block_rows(hd, q.dtype), "page_rows must be paged_block_rows(head_dim, dtype)")
+        _require(tuple(v_cache.shape) == tuple(k_cache.shape) and k_cache.shape[3] == hd, "Incorrect k/v pool size")
+        _require(block_table.dim() == 2 and block_table.shape[0] == b, "Incorrect block_table size")
+        s = block_table.shape[1] * page_rows
     _require(tuple(qk.shape) == (b, hq, 1, s), "Incorrect qk size")
     _require(qkv.numel() == b * (hq + 2 * hkv) * hd, "Incorrect qkv size")
     _require(x.numel() == b * dim and normed.numel() == b * dim and norm_weight.numel() == dim, "Incorrect x size")
@@ -615,6 +625,28 @@ def decode_step(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weigh
                              q, k_cache, v_cache, qk, gate_up, ffn_out, pairing, use_table)
     _dev(workspace)
     capi.call("l2k_decode_step", ctypes.byref(args), workspace.data_ptr(), _stream())
+
+
+def decode_step_paged(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done, q,
+                      k_pages, v_pages, block_table, qk, gate_up, ffn_out, workspace, pairing, use_table=True,
+                      attn_out=None):
+    """decode_step (or, with attn_out, decode_step_attention) over paged caches
+    k_pages / v_pages (num_pages, Hkv, page_rows, hd), page_rows =
+    paged_block_rows(hd, dtype); block_table (B, max_pages) u32; qk
+    (B, Hq, 1, max_pages * page_rows) (l2k_decode_step[_attention]_paged)."""
+    args = _decode_step_args(q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv, is_done,
+                             q, k_pages, v_pages, qk, gate_up, ffn_out, pairing, use_table, block_table=block_table)
+    _dev(workspace)
+    max_pages, num_pages = block_table.shape[1], k_pages.shape[0]
+    if attn_out is None:
+        capi.call("l2k_decode_step_paged", ctypes.byref(args), block_table.data_ptr(), max_pages, num_pages,
+                  workspace.data_ptr(), _stream())
+        return
+    _dev(attn_out)
+    _same(qk, attn_out, "decode_step_paged")
+    _require(attn_out.numel() == q.numel(), "attn_out must hold (batch, Hq, 1, head_dim)")
+    capi.call("l2k_decode_step_attention_paged", ctypes.byref(args), block_table.data_ptr(), max_pages, num_pages,
+              attn_out.data_ptr(), workspace.data_ptr(), _stream())
 
 
 def decode_step_attention(*, q_lens, kv_lens, max_lens, input_ids, embed_table, norm_weight, x, normed, qkv,

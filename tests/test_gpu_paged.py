@@ -199,3 +199,59 @@ def test_paged_prefill_rejects_shapes_the_tensor_cores_do_not_take():
     qk = torch.zeros(b, hq, 64, 128, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(capi.L2KError):
         ops.prefill_attention_scores_paged(q, kp, table, ql, ql, 64, 64, qk)
+
+
+@pytest.mark.parametrize("dtype,b,hq,hkv,max_pages,kv,attention,pairing", [
+    (torch.float32, 3, 4, 4, 12, [383, 0, 31], False, 1),            # last position, first, a page's last row
+    (torch.bfloat16, 4, 8, 2, 16, [1023, 64, 500, 7], False, 1),     # GQA, a fresh page at 64
+    (torch.bfloat16, 4, 8, 8, 16, [1000, 63, 1023, 300], True, 0),   # with the attention output, interleaved pairs
+    (torch.float32, 2, 4, 2, 10, [319, 32], True, 1),
+])
+def test_paged_decode_step_matches_contiguous(dtype, b, hq, hkv, max_pages, kv, attention, pairing):
+    """The one-launch decode step over page pools (shuffled block table)
+    against the same step on the contiguous caches the pages form: every
+    output bit-identical, and the appended K/V rows land in the right page."""
+    hd, F, V = 128, 256, 500
+    D = hq * hd
+    k, v, kp, vp, table, rows = _paged_setup(dtype, b, hq, hkv, hd, max_pages, spare=4, seed=b + hkv)
+    s = max_pages * rows
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device="cuda") * scale).to(dtype)
+
+    base = dict(q_lens=torch.ones(b, dtype=torch.uint32, device="cuda"),
+                input_ids=torch.randint(0, V, (b,), generator=torch.Generator().manual_seed(2)).to(torch.uint32).cuda(),
+                embed_table=rnd(V, D, scale=0.02), norm_weight=(torch.rand(D, generator=g, device="cuda") + 0.5).to(dtype),
+                qkv=rnd(b, (hq + 2 * hkv) * hd), is_done=torch.zeros(b, dtype=torch.uint8, device="cuda"),
+                gate_up=rnd(b, 2 * F))
+    base["is_done"][-1] = 1  # a finished sequence: not rotated or appended
+    kv0 = torch.tensor(kv, dtype=torch.uint32, device="cuda")
+
+    def outs():
+        return dict(kv_lens=kv0.clone(), max_lens=torch.zeros(2, dtype=torch.uint32, device="cuda"),
+                    x=torch.empty(b, D, dtype=dtype, device="cuda"), normed=torch.empty(b, D, dtype=dtype, device="cuda"),
+                    q=torch.zeros(b, hq, 1, hd, dtype=dtype, device="cuda"),
+                    qk=torch.full((b, hq, 1, s), 7.0, dtype=dtype, device="cuda"),
+                    ffn_out=torch.empty(b, F, dtype=dtype, device="cuda"))
+
+    ws = ops.decode_step_workspace(torch.device("cuda"))
+    c, p = outs(), outs()
+    attn_c = torch.zeros(b, hq, 1, hd, dtype=dtype, device="cuda") if attention else None
+    attn_p = torch.zeros_like(attn_c) if attention else None
+    if attention:
+        ops.decode_step_attention(**base, **c, k_cache=k, v_cache=v, workspace=ws, pairing=pairing, attn_out=attn_c)
+    else:
+        ops.decode_step(**base, **c, k_cache=k, v_cache=v, workspace=ws, pairing=pairing)
+    ops.decode_step_paged(**base, **p, k_pages=kp, v_pages=vp, block_table=table, workspace=ws, pairing=pairing,
+                          attn_out=attn_p)
+    torch.cuda.synchronize()
+    for n in ("kv_lens", "max_lens", "x", "normed", "q", "qk", "ffn_out"):
+        assert bits_equal(host(c[n]), host(p[n])), n
+    if attention:
+        assert bits_equal(host(attn_c), host(attn_p))
+    assert bits_equal(host(_gather(kp, table, rows)), host(k))
+    assert bits_equal(host(_gather(vp, table, rows)), host(v))
+    assert int(host(ws).astype(np.int64).sum()) == 0
+    assert capi.lib().l2k_device_error(1) == 0
